@@ -1,0 +1,483 @@
+"""Benchmark of the paged decode step (KV write + paged decode attention) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config 2] [--layers L] [--variant auto|mma|fma]
+
+One *step* is one pass of the hot path over one batch: the KV write of the
+batch's new tokens (one per sequence) into one layer's pool, then the paged
+decode of every sequence against that layer.  Steps rotate over L layers
+(independent K/V pools, default 4 x 149 MB for config 2), so each step streams
+a pool that is not in the 126 MB L2: "inputs larger than L2".
+
+Workload (default): config 2 — 256 sequences per GPU, context lengths
+U[128, 2048], 14 query / 2 KV heads, head_dim 64, block 16, bf16, seeded
+synthetic data (no dataset exists for this path).  N GPUs run one process each
+(torchrun); each rank owns its own 256 sequences and pool (sequence sharding,
+weak scaling) and the step ends with an NCCL all-gather of the outputs, the
+only collective of the path.
+
+Printed (rank 0, one JSON line):
+  value       aggregate algorithmic HBM GB/s of the device-resident step loop
+              (bytes of the write + decode, SURVEY-style formula in
+              workloads.PagedDecodeSpec) over the max-over-ranks time of K steps
+              replayed from a CUDA graph;
+  e2e         the same metric through the public backend API with the step's
+              inputs copied from pinned host memory each step and the output
+              copied back;
+  roofline    the decode kernel alone: algorithmic bytes per launch / mean
+              CUDA-event launch duration, against MEASURED_PEAKS.json hbm_gbs;
+  cpu_baseline  the CPU oracle (C/OpenMP port of the reference's torch path)
+              on this host's cores, rank 0 at N=1.
+
+``--impl reference`` times that CPU port alone on the same workload (rank 0;
+other ranks exit 0) and prints the same line with "impl": "reference".
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+import numpy as np  # noqa: E402
+
+METRIC = "paged decode attn HBM GB/s (% of peak) + decode tok/s at 1/2/4/8 B200"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20000)
+    p.add_argument("--warmup", type=int, default=200)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--config", type=int, default=2, choices=[2, 3, 4])
+    p.add_argument("--layers", type=int, default=4)
+    p.add_argument("--variant", default="auto", choices=["auto", "mma", "fma"])
+    p.add_argument("--partition-tokens", type=int, default=0)
+    p.add_argument("--e2e-steps", type=int, default=400)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--seed", type=int, default=0)
+    return p.parse_args()
+
+
+def peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def workload_desc(config: int) -> str:
+    return {
+        2: "config2: paged decode + KV write, 256 seqs/GPU, ctx U[128,2048], 14q/2kv/d64, block 16, bf16",
+        3: "config3: split-K paged decode + KV write, 32 seqs/GPU, ctx 32768, 14q/2kv/d64, block 16, bf16",
+        4: "config4: paged decode + KV write, 32q/8kv/d128, ctx lognormal(7,0.8) in [16,8192], block 16, bf16",
+    }[config]
+
+
+def rank_spec(config: int, rank: int, world: int, seed: int):
+    from mini_vllm_b200 import workloads as W
+
+    if config == 4:
+        # global batch 1024 sharded by sequence (token-balanced snake assignment)
+        from mini_vllm_b200 import sharding
+
+        ctx = W.context_lengths(4, seed=seed)
+        owned = sharding.snake_assignment(ctx, world)[rank]
+        c = W.CONFIGS[4]
+        spec = W.build_spec("config4", ctx[owned], c["num_heads"], c["num_kv_heads"], c["head_dim"],
+                            c["block_size"], seed=seed + 101 * rank)
+        return spec, owned
+    spec = W.make_spec(config, seed=seed + 101 * rank)
+    owned = np.arange(spec.num_seqs, dtype=np.int64) + rank * spec.num_seqs
+    return spec, owned
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu = gpu_id
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        return False
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU side: the oracle port of the reference's CPU path
+# ---------------------------------------------------------------------------
+def cpu_port_run(spec, tensors_np, steps: int, budget_s: float):
+    """Time write + decode of the oracle on the host cores; returns (s/step, threads, reps)."""
+    import oracle
+
+    kc, vc = tensors_np["key_cache"].copy(), tensors_np["value_cache"].copy()
+    times = []
+    t_end = time.perf_counter() + budget_s
+    for i in range(steps):
+        t0 = time.perf_counter()
+        oracle.cache_write(tensors_np["new_key"], tensors_np["new_value"], kc, vc, spec.slot_mapping,
+                           spec.block_size, "bf16")
+        oracle.decode(tensors_np["query"], kc, vc, spec.block_tables, spec.context_lens, spec.block_size,
+                      "bf16", threads=0)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() > t_end and i >= 2:
+            break
+    return statistics.median(times), oracle.max_threads(), len(times)
+
+
+def reference_arm(args, rank, world):
+    if rank != 0:
+        return
+    from mini_vllm_b200 import workloads as W
+
+    spec, _ = rank_spec(args.config, 0, 1, args.seed)
+    t = W.numpy_tensors(spec, "bf16")
+    for _ in range(max(1, min(args.warmup, 3))):
+        cpu_port_run(spec, t, 1, 0.0)
+    steps = max(1, min(args.steps, 50))
+    sec, threads, reps = cpu_port_run(spec, t, steps, budget_s=60.0)
+    nbytes = spec.decode_bytes(2) + spec.write_bytes(2)
+    gbs = nbytes / sec / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s",
+        "n_gpus": world, "steps": reps, "warmup": min(args.warmup, 3), "ms_per_step": round(sec * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic", "config": {"workload": workload_desc(args.config), "global_batch": spec.num_seqs,
+                                       "kind": "CPU oracle (C/OpenMP port of the reference torch path)"},
+        "decode_tok_s": round(spec.num_seqs / sec, 1),
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"full {spec.name} step (write {spec.num_seqs} tokens + decode "
+                                   f"{spec.num_seqs} seqs), median of {reps}"},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    import mini_vllm_b200 as M
+    from mini_vllm_b200 import sharding
+    from mini_vllm_b200 import workloads as W
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    spec, owned = rank_spec(args.config, rank, world, args.seed)
+    L = args.layers
+    t = W.torch_tensors(spec, torch.bfloat16, dev, num_layers=L)
+    kcs, vcs = t["key_caches"], t["value_caches"]
+    q, nk, nv = t["query"], t["new_key"], t["new_value"]
+    bt, kvl, slots = t["block_tables"], t["kv_len"], t["slot_mapping"]
+    out = torch.empty_like(q)
+    pt = args.partition_tokens or None
+    owned_all = None
+    if world > 1:
+        counts = [None] * world
+        dist.all_gather_object(counts, owned.tolist())
+        owned_all = [np.asarray(c, dtype=np.int64) for c in counts]
+
+    def step(layer):
+        M.paged_cache_write(nk, nv, kcs[layer], vcs[layer], slots, spec.block_size, strict=False,
+                            check_duplicates=False)
+        M.paged_decode_attention(q, kcs[layer], vcs[layer], bt, kvl, spec.block_size, out=out,
+                                 variant=args.variant, partition_tokens=pt, strict=False)
+
+    plan = M.decode_plan(spec.num_seqs, spec.num_heads, spec.num_kv_heads, spec.head_dim, spec.block_size,
+                         spec.num_blocks, spec.max_blocks, torch.bfloat16, args.variant, pt,
+                         kcs[0].data_ptr())
+    launches_per_step = 2 + (1 if plan["num_partitions"] > 1 else 0)
+
+    # correctness gate before timing: one strict step
+    M.paged_cache_write(nk, nv, kcs[0], vcs[0], slots, spec.block_size)
+    M.paged_decode_attention(q, kcs[0], vcs[0], bt, kvl, spec.block_size, out=out, variant=args.variant,
+                             partition_tokens=pt)
+    torch.cuda.synchronize()
+
+    # ---- CUDA graph of L layer-steps (the gather stays outside the graph) ----
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        for layer in range(L):
+            step(layer)
+    torch.cuda.current_stream(dev).wait_stream(s)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for layer in range(L):
+            step(layer)
+    replays = max(1, args.steps // L)
+    warm = max(1, args.warmup // L)
+    gather_every = world > 1
+
+    def run_replays(n):
+        for _ in range(n):
+            graph.replay()
+            if gather_every:
+                sharding.gather_outputs(out, owned_all, rank)
+
+    run_replays(warm)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(physical_gpu(local_rank)) as clocks:
+        ev0.record()
+        run_replays(replays)
+        ev1.record()
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    elapsed = ev0.elapsed_time(ev1) / 1e3
+    if world > 1:
+        tt = torch.tensor([elapsed], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        elapsed = float(tt.item())
+    n_steps = replays * L
+    sec_per_step = elapsed / n_steps
+    esz = 2
+    step_bytes_rank = spec.decode_bytes(esz) + spec.write_bytes(esz)
+    tot = torch.tensor([step_bytes_rank, spec.num_seqs], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(tot)
+    step_bytes_all, seqs_all = float(tot[0]), float(tot[1])
+    value_gbs = step_bytes_all / sec_per_step / 1e9
+    M.check_device_errors(dev)
+
+    # ---- roofline: the decode kernel alone, per-launch CUDA events ----
+    dec_graphs = []
+    for layer in range(L):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            M.paged_decode_attention(q, kcs[layer], vcs[layer], bt, kvl, spec.block_size, out=out,
+                                     variant=args.variant, partition_tokens=pt, strict=False)
+        dec_graphs.append(g)
+    reps = max(50, min(2000, args.steps // 10))
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    for i in range(min(20, reps)):
+        dec_graphs[i % L].replay()
+    torch.cuda.synchronize()
+    torch.cuda._sleep(400_000_000)  # keep the stream busy so the host queues the timed launches ahead
+    for i, (a, b) in enumerate(evs):
+        a.record()
+        dec_graphs[i % L].replay()
+        b.record()
+    torch.cuda.synchronize()
+    dec_times = [a.elapsed_time(b) / 1e3 for a, b in evs]
+    dec_mean = statistics.mean(dec_times)
+    peak, peak_kind = peaks()
+    dec_bytes = spec.decode_bytes(esz)
+    achieved = dec_bytes / dec_mean / 1e9
+    traffic = read_traffic(args.config)
+    M.check_device_errors(dev)
+
+    # ---- e2e: public API, host buffers in, output back to host ----
+    backend = M.AttentionBackendB200(M.ModelConfig(num_heads=spec.num_heads, num_kv_heads=spec.num_kv_heads,
+                                                   head_dim=spec.head_dim), strict=False,
+                                     decode_variant=args.variant, partition_tokens=pt)
+    pool = M.KVCachePool(kcs, vcs, spec.num_blocks, spec.block_size, L, spec.num_kv_heads, spec.head_dim,
+                         dev, torch.bfloat16)
+    backend._pool = pool
+    backend._block_size = spec.block_size
+    h = {k: v.cpu().pin_memory() for k, v in (("q", q), ("nk", nk), ("nv", nv), ("bt", bt), ("slots", slots))}
+    h["kv_len_after"] = spec.context_lens.copy()
+    h_kvl = torch.from_numpy(h.pop("kv_len_after")).pin_memory()
+    out_host = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    h2d = sum(x.numel() * x.element_size() for x in h.values()) + h_kvl.numel() * h_kvl.element_size()
+    d2h = out_host.numel() * out_host.element_size()
+    meta_group = M.AttentionGroup(seq_indices=list(range(spec.num_seqs)), attention_type="decode_gpu",
+                                  cached_len_before=None, query_len=None, kv_len_after=None)
+    meta = M.AttentionMetadata(groups=[meta_group], block_size=spec.block_size,
+                               num_kv_heads=spec.num_kv_heads, head_dim=spec.head_dim)
+
+    def e2e_step(layer):
+        qd = h["q"].to(dev, non_blocking=True)
+        kd = h["nk"].to(dev, non_blocking=True)
+        vd = h["nv"].to(dev, non_blocking=True)
+        sd = h["slots"].to(dev, non_blocking=True)
+        meta.decode_block_tables = h["bt"].to(dev, non_blocking=True)
+        meta_group.kv_len_after = h_kvl.to(dev, non_blocking=True)
+        backend.write_kv_cache(layer, kd, vd, sd)
+        o = backend.decode_attention(layer, qd, meta, pool)
+        out_host.copy_(o, non_blocking=True)
+
+    e2e_n = max(L, args.e2e_steps)
+    for i in range(min(10, e2e_n)):
+        e2e_step(i % L)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(e2e_n):
+        e2e_step(i % L)
+        if world > 1:
+            sharding.gather_outputs(out, owned_all, rank)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_sec = e0.elapsed_time(e1) / 1e3 / e2e_n
+    if world > 1:
+        tt = torch.tensor([e2e_sec], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_sec = float(tt.item())
+    M.check_device_errors(dev)
+    e2e_gbs = step_bytes_all / e2e_sec / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        host_t = {
+            "query": to_np_bf16(q), "key_cache": to_np_bf16(kcs[0]), "value_cache": to_np_bf16(vcs[0]),
+            "new_key": to_np_bf16(nk), "new_value": to_np_bf16(nv),
+        }
+        sec, threads, nrep = cpu_port_run(spec, host_t, 20, budget_s=15.0)
+        cgbs = step_bytes_rank / sec / 1e9
+        cpu = {"value": round(cgbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+               "sample": f"full {spec.name} step on one layer (write {spec.num_seqs} tokens + decode "
+                         f"{spec.num_seqs} seqs), median of {nrep}",
+               "decode_tok_s": round(spec.num_seqs / sec, 1)}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value_gbs, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": n_steps, "warmup": warm * L, "ms_per_step": round(sec_per_step * 1e3, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": workload_desc(args.config), "global_batch": int(seqs_all),
+                       "seqs_per_gpu": spec.num_seqs, "layers_rotated": L,
+                       "l2": f"inputs larger than L2: {L} layer pools of "
+                             f"{2 * kcs[0].numel() * 2 / 1e6:.0f} MB rotated",
+                       "parallelism": f"sequence-sharded x{world}" + (" + NCCL all-gather" if world > 1 else ""),
+                       "variant": plan["variant"], "partition_tokens": plan["partition_tokens"],
+                       "num_partitions": plan["num_partitions"], "timing": "CUDA graph of L steps, CUDA events"},
+            "pct_of_peak": round(100 * value_gbs / (peak * world), 2),
+            "pct_of_8tbs": round(100 * value_gbs / (8000.0 * world), 2),
+            "decode_tok_s": round(seqs_all / sec_per_step, 1),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
+                         "kernel": f"paged decode ({plan['variant']})",
+                         "bytes_per_launch": dec_bytes, "mean_launch_us": round(dec_mean * 1e6, 2),
+                         "p10_us": round(np.percentile(dec_times, 10) * 1e6, 2),
+                         "p90_us": round(np.percentile(dec_times, 90) * 1e6, 2)},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(d2h), "ms_per_step": round(e2e_sec * 1e3, 4),
+                    "decode_tok_s": round(seqs_all / e2e_sec, 1)},
+            "gpu_launches": n_steps * launches_per_step,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    del graph, dec_graphs
+
+
+def physical_gpu(local_rank: int) -> str:
+    """nvidia-smi id of this process's GPU (CUDA_VISIBLE_DEVICES remaps indices)."""
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [v.strip() for v in vis.split(",") if v.strip()]
+        if local_rank < len(ids):
+            return ids[local_rank]
+    return str(local_rank)
+
+
+def to_np_bf16(t):
+    import torch
+
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16).copy()
+
+
+def read_traffic(config: int):
+    """dram bytes per decode launch from the committed ncu summary, if present."""
+    path = os.path.join(REPO, "profiles", f"decode_config{config}_traffic.txt")
+    if not os.path.exists(path):
+        return None
+    for ln in open(path):
+        if ln.startswith("traffic_bytes_per_launch:"):
+            return int(float(ln.split(":", 1)[1]))
+    return None
+
+
+def main():
+    args = parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        reference_arm(args, rank, world)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,145 @@
+/*
+ * mini_vllm_b200.h — C ABI of the B200 paged-attention library (libmvb200.so).
+ *
+ * The library replaces the Triton kernels behind mini-vLLM's attention plug-in
+ * (mini_vllm/attention/paged_attention_gpu.py) with hand-written sm_100a CUDA.
+ * Every entry point takes plain pointers, sizes and strides; nothing in these
+ * signatures is a torch type, so ctypes, cgo, JNI or N-API can bind them.
+ *
+ * Conventions shared by all entry points
+ *  - Tensors live in device memory of the current CUDA device.
+ *  - Strides are in ELEMENTS, not bytes; the innermost (head_dim) dimension of
+ *    every tensor must be contiguous.
+ *  - The KV pool tensors have the reference layout
+ *        key_cache[num_blocks][num_kv_heads][block_size][head_dim]
+ *    (mini_vllm/cache/pool.py:93-102), contiguous.
+ *  - `stream` is a cudaStream_t (NULL = legacy default stream). No entry point
+ *    synchronises; all work is enqueued on `stream`.
+ *  - The return value is a host-side status (MVB_OK or a negative MVB_ERR_*)
+ *    and no C++ exception ever crosses the ABI.  Problems that only the device
+ *    can see (a bad slot, a bad block id, kv_len < 1, a duplicate slot) are
+ *    OR-ed as MVB_DEV_* bits into the caller's int32 `error_flags` word in
+ *    device memory; the caller reads it when it wants the check (the Python
+ *    shim reads it after every call in strict mode, which mirrors the host
+ *    syncs the reference performs at paged_attention_gpu.py:128-135,296).
+ */
+#ifndef MINI_VLLM_B200_H
+#define MINI_VLLM_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- element types of the KV pool / query / output ---------------------- */
+#define MVB_DTYPE_F32  0
+#define MVB_DTYPE_F16  1
+#define MVB_DTYPE_BF16 2
+
+/* ---- host-side status codes --------------------------------------------- */
+#define MVB_OK                 0
+#define MVB_ERR_INVALID_ARG   -1  /* shape / size / stride inconsistency       */
+#define MVB_ERR_DTYPE         -2  /* unsupported element type                  */
+#define MVB_ERR_HEAD_DIM      -3  /* head_dim not in {64, 128}                 */
+#define MVB_ERR_BLOCK_SIZE    -4  /* block_size not a positive power of two    */
+#define MVB_ERR_ALIGNMENT     -5  /* pointer or stride breaks the vector width */
+#define MVB_ERR_CUDA          -6  /* a CUDA runtime call or launch failed      */
+#define MVB_ERR_WORKSPACE     -7  /* split-K workspace missing or too small    */
+#define MVB_ERR_TENSOR_MAP    -8  /* cuTensorMapEncodeTiled failed             */
+#define MVB_ERR_VARIANT       -9  /* requested kernel variant cannot run here  */
+#define MVB_ERR_HEADS        -10  /* num_heads not a multiple of num_kv_heads  */
+
+/* ---- device-side error bits (OR-ed into *error_flags) ------------------- */
+#define MVB_DEV_KV_LEN        1   /* some kv_len_after < 1                      */
+#define MVB_DEV_BLOCK_ID      2   /* a block id needed by kv_len is <0 or >=NB  */
+#define MVB_DEV_TABLE_SHORT   4   /* ceil(kv_len/block_size) > max_blocks       */
+#define MVB_DEV_SLOT_RANGE    8   /* slot not -1 and outside [0, NB*BS)         */
+#define MVB_DEV_DUP_SLOT     16   /* two tokens of one write target one slot    */
+#define MVB_DEV_TIMEOUT      32   /* a bounded pipeline wait ran out            */
+
+/* ---- decode kernel variants --------------------------------------------- */
+#define MVB_DECODE_AUTO 0  /* MMA when eligible, else FMA                        */
+#define MVB_DECODE_FMA  1  /* CUDA-core FP32 FMA kernel (any dtype, any BS)      */
+#define MVB_DECODE_MMA  2  /* TMA-staged tensor-core kernel (bf16/f16, BS%16==0) */
+
+/* ABI version; bumped whenever a signature below changes. */
+int mvb_abi_version(void);
+
+/* Human-readable text for a host status code (static storage). */
+const char* mvb_status_string(int status);
+
+/*
+ * KV-cache write: for every token t with slot_mapping[t] != -1,
+ *     key_cache  [slot / BS][h][slot % BS][:] = key  [t][h][:]
+ *     value_cache[slot / BS][h][slot % BS][:] = value[t][h][:]
+ * for all KV heads h.  Replaces triton_cache_write / _cache_write_kernel
+ * (mini_vllm/attention/paged_attention_gpu.py:90-154, :32-87) and computes the
+ * same bytes as the torch oracle write_to_paged_cache
+ * (mini_vllm/cache/cache_write.py:25-74).
+ *
+ * key/value may be strided views (e.g. V as a slice of a fused QKV output);
+ * pass their token and head strides.  A slot outside [0, NB*BS) other than -1
+ * is skipped and sets MVB_DEV_SLOT_RANGE.  When `slot_claims` is non-NULL it
+ * must point to NB*BS zero-initialised uint32 words that persist across calls;
+ * `epoch` must differ from every epoch used before with that array (never 0),
+ * and two tokens that target one slot set MVB_DEV_DUP_SLOT (the reference
+ * forbids duplicates, paged_attention_gpu.py:126-135).
+ */
+int mvb_kv_cache_write(const void* key, int64_t key_stride_token, int64_t key_stride_head,
+                       const void* value, int64_t value_stride_token, int64_t value_stride_head,
+                       void* key_cache, void* value_cache,
+                       const int64_t* slot_mapping, int32_t num_tokens,
+                       int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                       int32_t num_blocks, int32_t dtype,
+                       uint32_t* slot_claims, uint32_t epoch,
+                       int32_t* error_flags, void* stream);
+
+/*
+ * Plan a paged decode: picks the kernel variant and the split-K partition
+ * length for the given shape and returns the split-K workspace size in bytes
+ * (0 when the decode runs unsplit).  `variant` / `partition_tokens` are the
+ * caller's requests (MVB_DECODE_AUTO / 0 = let the library choose).
+ * `cache_ptr` is only inspected for TMA alignment (it may be NULL, in which
+ * case alignment is assumed).
+ */
+int mvb_paged_decode_plan(int32_t num_seqs, int32_t num_heads, int32_t num_kv_heads,
+                          int32_t head_dim, int32_t block_size, int32_t num_blocks,
+                          int32_t max_blocks_per_seq, int32_t dtype,
+                          int32_t variant, int32_t partition_tokens, const void* cache_ptr,
+                          int32_t* variant_out, int32_t* partition_tokens_out,
+                          int32_t* num_partitions_out, int64_t* workspace_bytes_out);
+
+/*
+ * Paged decode attention, one query token per sequence:
+ *   out[s][h][:] = softmax(scale * q[s][h] . K[s][h/G]^T) . V[s][h/G]
+ * over kv_len[s] tokens reached through block_table[s][0 .. ceil(kv_len/BS)).
+ * G = num_heads / num_kv_heads (repeat_interleave GQA mapping).  Replaces
+ * triton_decode_attention / _paged_decode_kernel
+ * (mini_vllm/attention/paged_attention_gpu.py:252-321, :162-249); the math is
+ * that of AttentionBackendRef.decode_attention
+ * (mini_vllm/attention/paged_attention_ref.py:102-161).
+ *
+ * block_table is int64 [num_seqs][max_blocks_per_seq] (-1 padded, row stride
+ * block_table_stride); kv_len is int32 [num_seqs]; query/out are
+ * [num_seqs][num_heads][head_dim] with the given strides; out has the query's
+ * dtype.  When the plan (same arguments) says num_partitions > 1 the call runs
+ * the flash-decoding split-K kernel followed by the cross-partition reduction
+ * and needs `workspace` of at least workspace_bytes (256-byte aligned).
+ */
+int mvb_paged_decode(const void* query, int64_t q_stride_seq, int64_t q_stride_head,
+                     const void* key_cache, const void* value_cache,
+                     const int64_t* block_table, int64_t block_table_stride,
+                     int32_t max_blocks_per_seq, const int32_t* kv_len,
+                     void* out, int64_t out_stride_seq, int64_t out_stride_head,
+                     int32_t num_seqs, int32_t num_heads, int32_t num_kv_heads,
+                     int32_t head_dim, int32_t block_size, int32_t num_blocks,
+                     float scale, int32_t dtype, int32_t variant, int32_t partition_tokens,
+                     void* workspace, int64_t workspace_bytes,
+                     int32_t* error_flags, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MINI_VLLM_B200_H */

@@ -1,0 +1,103 @@
+"""ctypes binding of libmvb200.so — the only door to the CUDA kernels.
+
+Loading fails loudly (``RuntimeError``) when the library has not been built:
+there is no CPU or Triton fallback behind this module.  The argument types
+below mirror ``include/mini_vllm_b200.h`` one to one.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libmvb200.so")
+
+# element-type codes (MVB_DTYPE_*)
+DTYPE_F32 = 0
+DTYPE_F16 = 1
+DTYPE_BF16 = 2
+
+# host status codes (MVB_OK / MVB_ERR_*)
+OK = 0
+ERR_INVALID_ARG = -1
+ERR_DTYPE = -2
+ERR_HEAD_DIM = -3
+ERR_BLOCK_SIZE = -4
+ERR_ALIGNMENT = -5
+ERR_CUDA = -6
+ERR_WORKSPACE = -7
+ERR_TENSOR_MAP = -8
+ERR_VARIANT = -9
+ERR_HEADS = -10
+
+# device error bits (MVB_DEV_*)
+DEV_KV_LEN = 1
+DEV_BLOCK_ID = 2
+DEV_TABLE_SHORT = 4
+DEV_SLOT_RANGE = 8
+DEV_DUP_SLOT = 16
+DEV_TIMEOUT = 32
+
+# decode variants (MVB_DECODE_*)
+DECODE_AUTO = 0
+DECODE_FMA = 1
+DECODE_MMA = 2
+
+ABI_VERSION = 1
+
+# Every symbol include/mini_vllm_b200.h declares, with (restype, argtypes).
+_i32, _i64, _u32, _f32, _vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_uint32, ctypes.c_float, ctypes.c_void_p
+_p_i32, _p_i64 = ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_int64)
+SIGNATURES = {
+    "mvb_abi_version": (_i32, []),
+    "mvb_status_string": (ctypes.c_char_p, [_i32]),
+    "mvb_kv_cache_write": (
+        _i32,
+        [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32,
+         _vp, _u32, _vp, _vp],
+    ),
+    "mvb_paged_decode_plan": (
+        _i32,
+        [_i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _vp,
+         _p_i32, _p_i32, _p_i32, _p_i64],
+    ),
+    "mvb_paged_decode": (
+        _i32,
+        [_vp, _i64, _i64, _vp, _vp, _vp, _i64, _i32, _vp, _vp, _i64, _i64,
+         _i32, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _i32, _i32, _vp, _i64, _vp, _vp],
+    ),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def lib() -> ctypes.CDLL:
+    """Load (once) and return the library with typed entry points."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f"libmvb200.so not found at {LIB_PATH}: build it with "
+                "__graft_entry__.build() (the paged-attention path has no CPU fallback)"
+            )
+        handle = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        if handle.mvb_abi_version() != ABI_VERSION:
+            raise RuntimeError(
+                f"libmvb200.so ABI {handle.mvb_abi_version()} != expected {ABI_VERSION}; rebuild it"
+            )
+        _lib = handle
+        return _lib
+
+
+def status_string(status: int) -> str:
+    return lib().mvb_status_string(status).decode()

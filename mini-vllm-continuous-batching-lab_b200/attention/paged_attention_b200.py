@@ -1,0 +1,506 @@
+"""B200 paged-attention backend: the reference's Triton entry points on sm_100a CUDA.
+
+Free functions with the reference's call signatures
+(mini_vllm/attention/paged_attention_gpu.py):
+
+* ``paged_cache_write(key, value, key_cache, value_cache, slot_mapping, block_size)``
+  replaces ``triton_cache_write`` (:90-154);
+* ``paged_decode_attention(query, key_cache, value_cache, block_table,
+  kv_len_after, block_size, scale=None)`` replaces ``triton_decode_attention``
+  (:252-321), with the optional ``scale`` defaulting to ``head_dim ** -0.5``
+  as at :304.
+
+``triton_cache_write`` / ``triton_decode_attention`` are aliases of the two so
+an import of the reference names keeps working; nothing here uses Triton.
+Both call libmvb200.so through ctypes with raw pointers and strides and launch
+on ``torch.cuda.current_stream()``.
+
+Error behaviour follows the reference:
+
+* argument checks the reference makes with ``assert`` raise ``AssertionError``
+  (the exception also derives from ``ValueError``, the type the torch oracle
+  ``write_to_paged_cache`` raises for the same checks, cache_write.py:82-140);
+* ``kv_len_after < 1`` raises ``ValueError`` (:296-300);
+* a duplicate write slot raises ``AssertionError`` mentioning "Duplicate"
+  (:126-135);
+* a slot outside ``[0, num_blocks * block_size)`` other than -1 raises
+  ``IndexError`` (the oracle's rule, cache_write.py:61-66);
+* a block table too short for ``kv_len`` raises ``IndexError`` (the gather's
+  rule, cache_read.py:62-67).
+
+The device-side conditions are detected by the kernels, which OR a bit into a
+per-device error word.  With ``strict=True`` (the default) every call reads
+that word back — one host sync, as the reference's own checks cost — and
+raises; with ``strict=False`` the word accumulates until
+``check_device_errors`` is called, so a timed loop has no host sync.
+"""
+
+from __future__ import annotations
+
+import threading
+from typing import Any, Dict, Optional, Tuple
+
+import torch
+
+from .. import _native
+from ..cache.pool import KVCachePool
+from .backend import AttentionBackend
+
+_DTYPE_CODES = {
+    torch.float32: _native.DTYPE_F32,
+    torch.float16: _native.DTYPE_F16,
+    torch.bfloat16: _native.DTYPE_BF16,
+}
+_VARIANTS = {"auto": _native.DECODE_AUTO, "fma": _native.DECODE_FMA, "mma": _native.DECODE_MMA}
+_VARIANT_NAMES = {v: k for k, v in _VARIANTS.items()}
+
+
+class ArgumentError(AssertionError, ValueError):
+    """A rejected argument: an ``AssertionError`` like the Triton entry points
+    raise, and a ``ValueError`` like the torch oracle raises."""
+
+
+def _require(cond: bool, msg: str) -> None:
+    if not cond:
+        raise ArgumentError(msg)
+
+
+# ---------------------------------------------------------------------------
+# per-device state: error word, duplicate-slot claim arrays, split-K workspace
+# ---------------------------------------------------------------------------
+class _DeviceState:
+    def __init__(self, device: torch.device) -> None:
+        self.device = device
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        self._claims: Dict[int, Tuple[torch.Tensor, int]] = {}
+        self._workspace: Optional[torch.Tensor] = None
+
+    def next_claims(self, total_slots: int) -> Tuple[torch.Tensor, int]:
+        """Claim array for a pool of ``total_slots`` and a fresh epoch (never 0)."""
+        entry = self._claims.get(total_slots)
+        if entry is None:
+            arr = torch.zeros(total_slots, dtype=torch.int32, device=self.device)
+            epoch = 1
+        else:
+            arr, epoch = entry
+            epoch += 1
+            if epoch >= 0xFFFFFFFF:
+                arr.zero_()
+                epoch = 1
+        self._claims[total_slots] = (arr, epoch)
+        return arr, epoch
+
+    def workspace(self, nbytes: int) -> torch.Tensor:
+        if self._workspace is None or self._workspace.numel() < nbytes:
+            self._workspace = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+        return self._workspace
+
+
+_states: Dict[int, _DeviceState] = {}
+_states_lock = threading.Lock()
+
+
+def _state(device: torch.device) -> _DeviceState:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    st = _states.get(idx)
+    if st is None:
+        with _states_lock:
+            st = _states.get(idx)
+            if st is None:
+                st = _DeviceState(torch.device("cuda", idx))
+                _states[idx] = st
+    return st
+
+
+def _stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _host_status(status: int, what: str) -> None:
+    if status == _native.OK:
+        return
+    msg = f"{what}: {_native.status_string(status)} (status {status})"
+    if status in (_native.ERR_HEAD_DIM, _native.ERR_BLOCK_SIZE, _native.ERR_HEADS,
+                  _native.ERR_INVALID_ARG, _native.ERR_DTYPE):
+        raise ArgumentError(msg)
+    raise RuntimeError(msg)
+
+
+def _take_flags(state: _DeviceState) -> int:
+    flags = int(state.err.item())
+    if flags:
+        state.err.zero_()
+    return flags
+
+
+def check_device_errors(device: Optional[torch.device] = None) -> None:
+    """Raise for device-side errors accumulated by ``strict=False`` calls."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    flags = _take_flags(_state(dev))
+    if flags:
+        _raise_flags(flags, None)
+
+
+def _raise_flags(flags: int, detail: Optional[Dict[str, Any]]) -> None:
+    d = detail or {}
+    if flags & _native.DEV_KV_LEN:
+        kvl = d.get("kv_len_after")
+        got = f", got min={int(kvl.min().item())}" if kvl is not None else ""
+        raise ValueError(f"kv_len_after must be >= 1 for all decode sequences{got}")
+    if flags & _native.DEV_SLOT_RANGE:
+        slots = d.get("slot_mapping")
+        total = d.get("total_slots")
+        msg = "slot_mapping entry out of range"
+        if slots is not None and total is not None:
+            bad = ((slots < -1) | (slots >= total)).nonzero()
+            if bad.numel():
+                t = int(bad[0, 0].item())
+                msg = (f"slot_mapping[{t}] = {int(slots[t].item())} out of range [0, {total}) "
+                       f"(block_size={d.get('block_size')}, num_blocks={d.get('num_blocks')})")
+        raise IndexError(msg)
+    if flags & _native.DEV_TABLE_SHORT:
+        raise IndexError(
+            "block_table length insufficient to cover kv_len_after tokens "
+            f"(max_blocks_per_seq={d.get('max_blocks')}, block_size={d.get('block_size')})"
+        )
+    if flags & _native.DEV_BLOCK_ID:
+        raise IndexError(
+            f"block_table entry out of range [0, {d.get('num_blocks')}) within a sequence's "
+            "kv_len (a -1 pad or a stale id where a block is required)"
+        )
+    if flags & _native.DEV_DUP_SLOT:
+        raise AssertionError(
+            "Duplicate slots in slot_mapping: parallel writes to one slot race, "
+            "so duplicate slots are forbidden."
+        )
+    if flags & _native.DEV_TIMEOUT:
+        raise RuntimeError("paged decode: a bounded pipeline wait timed out on the device")
+    raise RuntimeError(f"unknown device error flags 0x{flags:x}")
+
+
+# ---------------------------------------------------------------------------
+# KV write
+# ---------------------------------------------------------------------------
+def paged_cache_write(
+    key: torch.Tensor,
+    value: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    slot_mapping: torch.Tensor,
+    block_size: int,
+    *,
+    strict: bool = True,
+    check_duplicates: bool = True,
+) -> None:
+    """Scatter-write per-token K/V into one layer's paged cache (in place).
+
+    Same bytes as ``write_to_paged_cache`` (mini_vllm/cache/cache_write.py:25-74)
+    for every input without duplicate slots; the checks mirror
+    ``triton_cache_write`` (paged_attention_gpu.py:109-135).  ``value`` may be
+    a strided view (e.g. of a fused QKV output): its strides are passed to the
+    kernel instead of making it contiguous.
+
+    ``check_duplicates`` stamps every slot with a per-call epoch to detect two
+    tokens writing one slot.  A CUDA graph replays its launch arguments, epoch
+    included, so code that captures this call in a graph passes
+    ``check_duplicates=False`` (out-of-range slots are still flagged).
+    """
+    _require(key.dim() == 3, f"key must be [num_tokens, num_kv_heads, head_dim], got {tuple(key.shape)}")
+    _require(key.shape == value.shape, f"key {tuple(key.shape)} != value {tuple(value.shape)}")
+    _require(key_cache.dim() == 4, f"key_cache must be 4-D, got {tuple(key_cache.shape)}")
+    _require(key_cache.shape == value_cache.shape,
+             f"key_cache shape {tuple(key_cache.shape)} != value_cache shape {tuple(value_cache.shape)}")
+    num_tokens, num_kv_heads, head_dim = key.shape
+    num_blocks = key_cache.shape[0]
+    _require(slot_mapping.dim() == 1 and slot_mapping.shape[0] == num_tokens,
+             f"slot_mapping length {tuple(slot_mapping.shape)} != num_tokens {num_tokens}")
+    _require(num_kv_heads == key_cache.shape[1],
+             f"key num_kv_heads {num_kv_heads} != key_cache num_kv_heads {key_cache.shape[1]}")
+    _require(head_dim == key_cache.shape[3],
+             f"key head_dim {head_dim} != key_cache head_dim {key_cache.shape[3]}")
+    _require(block_size > 0, f"block_size must be > 0, got {block_size}")
+    _require(block_size == key_cache.shape[2],
+             f"block_size {block_size} != cache dim2 {key_cache.shape[2]}")
+    _require(key.dtype == key_cache.dtype, f"key dtype {key.dtype} != cache dtype {key_cache.dtype}")
+    _require(value.dtype == value_cache.dtype,
+             f"value dtype {value.dtype} != value_cache dtype {value_cache.dtype}")
+    _require(key_cache.dtype in _DTYPE_CODES, f"unsupported cache dtype {key_cache.dtype}")
+    _require(key.device == key_cache.device, f"key device {key.device} != cache device {key_cache.device}")
+    _require(value.device == value_cache.device,
+             f"value device {value.device} != value_cache device {value_cache.device}")
+    _require(key.device.type == "cuda", f"key.device must be cuda, got {key.device}")
+    _require(key_cache.is_contiguous() and value_cache.is_contiguous(),
+             "key_cache and value_cache must be contiguous [num_blocks, num_kv_heads, block_size, head_dim]")
+    if num_tokens == 0:
+        return
+    if key.stride(2) != 1:
+        key = key.contiguous()
+    if value.stride(2) != 1:
+        value = value.contiguous()
+    if slot_mapping.dtype != torch.int64 or slot_mapping.device != key.device or not slot_mapping.is_contiguous():
+        slot_mapping = slot_mapping.to(device=key.device, dtype=torch.int64).contiguous()
+
+    state = _state(key.device)
+    total_slots = num_blocks * block_size
+    if check_duplicates:
+        claims, epoch = state.next_claims(total_slots)
+        claims_ptr = claims.data_ptr()
+    else:
+        claims_ptr, epoch = None, 0
+    status = _native.lib().mvb_kv_cache_write(
+        key.data_ptr(), key.stride(0), key.stride(1),
+        value.data_ptr(), value.stride(0), value.stride(1),
+        key_cache.data_ptr(), value_cache.data_ptr(),
+        slot_mapping.data_ptr(), num_tokens, num_kv_heads, head_dim, block_size, num_blocks,
+        _DTYPE_CODES[key_cache.dtype], claims_ptr, epoch,
+        state.err.data_ptr(), _stream_handle(key.device),
+    )
+    _host_status(status, "kv cache write")
+    if strict:
+        flags = _take_flags(state)
+        if flags:
+            _raise_flags(flags, {"slot_mapping": slot_mapping, "total_slots": total_slots,
+                                 "block_size": block_size, "num_blocks": num_blocks})
+
+
+# ---------------------------------------------------------------------------
+# decode
+# ---------------------------------------------------------------------------
+def decode_plan(
+    num_seqs: int,
+    num_heads: int,
+    num_kv_heads: int,
+    head_dim: int,
+    block_size: int,
+    num_blocks: int,
+    max_blocks_per_seq: int,
+    dtype: torch.dtype,
+    variant: str = "auto",
+    partition_tokens: Optional[int] = None,
+    cache_ptr: int = 0,
+) -> Dict[str, Any]:
+    """The library's launch plan for a decode of this shape (no GPU work)."""
+    import ctypes
+
+    v, pt, np_ = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
+    ws = ctypes.c_int64()
+    status = _native.lib().mvb_paged_decode_plan(
+        num_seqs, num_heads, num_kv_heads, head_dim, block_size, num_blocks, max_blocks_per_seq,
+        _DTYPE_CODES[dtype], _VARIANTS[variant], int(partition_tokens or 0), cache_ptr or None,
+        ctypes.byref(v), ctypes.byref(pt), ctypes.byref(np_), ctypes.byref(ws),
+    )
+    _host_status(status, "paged decode plan")
+    return {"variant": _VARIANT_NAMES[v.value], "partition_tokens": pt.value,
+            "num_partitions": np_.value, "workspace_bytes": ws.value}
+
+
+def paged_decode_attention(
+    query: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    block_table: torch.Tensor,
+    kv_len_after: torch.Tensor,
+    block_size: int,
+    scale: Optional[float] = None,
+    *,
+    out: Optional[torch.Tensor] = None,
+    variant: str = "auto",
+    partition_tokens: Optional[int] = None,
+    strict: bool = True,
+) -> torch.Tensor:
+    """Paged decode attention (one query token per sequence) on the B200 kernels.
+
+    Args (as ``triton_decode_attention``, paged_attention_gpu.py:252-321):
+        query: ``[total_decode, num_q_heads, head_dim]`` bf16 / f16 / f32.
+        key_cache, value_cache: ``[num_blocks, num_kv_heads, block_size, head_dim]``.
+        block_table: ``[total_decode, max_blocks_per_seq]`` int64, ``-1`` padded.
+        kv_len_after: ``[total_decode]`` int32 — tokens to attend per sequence.
+        block_size: tokens per block (power of two).
+        scale: softmax scale, default ``head_dim ** -0.5``.
+    Keyword-only extensions: ``out`` (write in place), ``variant``
+    (``"auto" | "mma" | "fma"``), ``partition_tokens`` (split-K partition
+    length; ``None`` lets the library choose), ``strict``.
+
+    Returns ``[total_decode, num_q_heads, head_dim]`` in the query's dtype.
+    """
+    _require(query.dim() == 3, f"query must be [total_decode, num_heads, head_dim], got {tuple(query.shape)}")
+    total_decode, num_q_heads, head_dim = query.shape
+    _require(key_cache.dim() == 4 and key_cache.shape == value_cache.shape,
+             f"key_cache {tuple(key_cache.shape)} / value_cache {tuple(value_cache.shape)} mismatch")
+    num_blocks, num_kv_heads = key_cache.shape[0], key_cache.shape[1]
+    _require(head_dim in (64, 128), f"head_dim {head_dim} not supported (only 64, 128)")
+    _require(block_size > 0 and (block_size & (block_size - 1)) == 0,
+             f"block_size {block_size} must be a power of 2")
+    _require(key_cache.shape[2] == block_size, f"block_size {block_size} != cache dim2 {key_cache.shape[2]}")
+    _require(key_cache.shape[3] == head_dim, f"cache head_dim {key_cache.shape[3]} != query head_dim {head_dim}")
+    _require(num_q_heads % num_kv_heads == 0,
+             f"num_q_heads {num_q_heads} not divisible by num_kv_heads {num_kv_heads}")
+    _require(query.dtype in _DTYPE_CODES, f"query dtype {query.dtype} must be bf16, f16 or f32")
+    _require(key_cache.dtype == query.dtype and value_cache.dtype == query.dtype,
+             f"cache dtype {key_cache.dtype} != query dtype {query.dtype}")
+    _require(query.device.type == "cuda", f"query.device must be cuda, got {query.device}")
+    _require(key_cache.device == query.device and value_cache.device == query.device,
+             "query and caches must share one device")
+    _require(key_cache.is_contiguous() and value_cache.is_contiguous(), "caches must be contiguous")
+    _require(block_table.dim() == 2 and block_table.shape[0] == total_decode,
+             f"block_table rows {tuple(block_table.shape)} != total_decode {total_decode}")
+    _require(kv_len_after.shape == (total_decode,),
+             f"kv_len_after shape {tuple(kv_len_after.shape)} != ({total_decode},)")
+    if scale is None:
+        scale = head_dim ** -0.5
+
+    if out is None:
+        out = torch.empty((total_decode, num_q_heads, head_dim), dtype=query.dtype, device=query.device)
+    else:
+        _require(out.shape == query.shape and out.dtype == query.dtype and out.device == query.device,
+                 "out must match query's shape, dtype and device")
+        _require(out.stride(2) == 1, "out's last dimension must be contiguous")
+    if total_decode == 0:
+        return out
+
+    if query.stride(2) != 1 or query.data_ptr() % 16 or (query.stride(0) * query.element_size()) % 16 \
+            or (query.stride(1) * query.element_size()) % 16:
+        query = query.contiguous()
+    if block_table.dtype != torch.int64 or block_table.device != query.device or block_table.stride(1) != 1:
+        block_table = block_table.to(device=query.device, dtype=torch.int64).contiguous()
+    if kv_len_after.dtype != torch.int32 or kv_len_after.device != query.device or not kv_len_after.is_contiguous():
+        kv_len_after = kv_len_after.to(device=query.device, dtype=torch.int32).contiguous()
+
+    state = _state(query.device)
+    max_blocks = block_table.shape[1]
+    plan = decode_plan(total_decode, num_q_heads, num_kv_heads, head_dim, block_size, num_blocks,
+                       max_blocks, query.dtype, variant, partition_tokens, key_cache.data_ptr())
+    ws_bytes = plan["workspace_bytes"]
+    ws_ptr = state.workspace(ws_bytes).data_ptr() if ws_bytes > 0 else None
+    status = _native.lib().mvb_paged_decode(
+        query.data_ptr(), query.stride(0), query.stride(1),
+        key_cache.data_ptr(), value_cache.data_ptr(),
+        block_table.data_ptr(), block_table.stride(0), max_blocks,
+        kv_len_after.data_ptr(),
+        out.data_ptr(), out.stride(0), out.stride(1),
+        total_decode, num_q_heads, num_kv_heads, head_dim, block_size, num_blocks,
+        float(scale), _DTYPE_CODES[query.dtype], _VARIANTS[variant], int(partition_tokens or 0),
+        ws_ptr, ws_bytes, state.err.data_ptr(), _stream_handle(query.device),
+    )
+    _host_status(status, "paged decode")
+    if strict:
+        flags = _take_flags(state)
+        if flags:
+            _raise_flags(flags, {"kv_len_after": kv_len_after, "max_blocks": max_blocks,
+                                 "block_size": block_size, "num_blocks": num_blocks})
+    return out
+
+
+# Reference names, for code that imports them from the Triton module.
+triton_cache_write = paged_cache_write
+triton_decode_attention = paged_decode_attention
+
+
+# ---------------------------------------------------------------------------
+# backend class
+# ---------------------------------------------------------------------------
+class AttentionBackendB200(AttentionBackend):
+    """``AttentionBackend`` on the B200 kernels (mirror of AttentionBackendGPU,
+    paged_attention_gpu.py:454-661).
+
+    * ``write_kv_cache`` → ``paged_cache_write`` (CUDA scatter kernel);
+    * ``decode_attention`` → ``paged_decode_attention`` (TMA + tensor-core
+      kernel for bf16/f16, FMA kernel otherwise, split-K for long contexts);
+    * ``prefill_attention`` → torch gather of the paged prefix by index
+      tensors plus SDPA (no Triton; the reference's C3 path, :577-661).
+    """
+
+    def __init__(self, config: Any, *, strict: bool = True, decode_variant: str = "auto",
+                 partition_tokens: Optional[int] = None) -> None:
+        hd = getattr(config, "head_dim", 0)
+        if hd not in (64, 128):
+            raise RuntimeError(
+                f"AttentionBackendB200: head_dim={hd} not supported (only 64, 128)."
+            )
+        if decode_variant not in _VARIANTS:
+            raise ValueError(f"decode_variant must be one of {sorted(_VARIANTS)}, got {decode_variant!r}")
+        if not torch.cuda.is_available():
+            raise RuntimeError("attention_backend='b200' requires CUDA, but CUDA is not available.")
+        _native.lib()  # fail here, not at the first step, when the library is missing
+        self._config = config
+        self._pool: Optional[KVCachePool] = None
+        self._block_size = 0
+        self.strict = strict
+        self.decode_variant = decode_variant
+        self.partition_tokens = partition_tokens
+
+    def allocate_pool(self, num_layers: int, num_blocks: int, block_size: int, num_kv_heads: int,
+                      head_dim: int, dtype: torch.dtype, device: torch.device) -> KVCachePool:
+        validate_block_size(block_size)
+        pool = KVCachePool.allocate(num_layers, num_blocks, block_size, num_kv_heads, head_dim,
+                                    dtype, device)
+        self._pool = pool
+        self._block_size = block_size
+        return pool
+
+    def write_kv_cache(self, layer_idx: int, key: torch.Tensor, value: torch.Tensor,
+                       slot_mapping: torch.Tensor) -> None:
+        pool = self._pool
+        assert pool is not None, "allocate_pool must be called first"
+        paged_cache_write(key, value, pool.key_caches[layer_idx], pool.value_caches[layer_idx],
+                          slot_mapping, pool.block_size, strict=self.strict)
+
+    def decode_attention(self, layer_idx: int, query: torch.Tensor, attn_metadata: Any,
+                         pool: Any) -> torch.Tensor:
+        if query.shape[0] == 0:
+            return query
+        group = next((g for g in attn_metadata.groups if g.attention_type == "decode_gpu"), None)
+        if group is None:
+            return query
+        return paged_decode_attention(
+            query, pool.key_caches[layer_idx], pool.value_caches[layer_idx],
+            attn_metadata.decode_block_tables, group.kv_len_after, pool.block_size,
+            variant=self.decode_variant, partition_tokens=self.partition_tokens,
+            strict=self.strict,
+        )
+
+    def prefill_attention(self, layer_idx: int, query: torch.Tensor, key: torch.Tensor,
+                          value: torch.Tensor, attn_metadata: Any, pool: Any) -> torch.Tensor:
+        if query.shape[0] == 0:
+            return query
+        num_heads, head_dim = query.shape[1], query.shape[2]
+        reps = num_heads // pool.num_kv_heads
+        scale = head_dim ** -0.5
+        kc, vc = pool.key_caches[layer_idx], pool.value_caches[layer_idx]
+        bs = pool.block_size
+        parts = []
+        offset = 0
+        for group in attn_metadata.groups:
+            if group.attention_type not in ("prefill_gpu", "prefill_ref"):
+                continue
+            for i, seq_idx in enumerate(group.seq_indices):
+                cached = int(group.cached_len_before[i])
+                q_len = int(group.query_len[i])
+                kv_len = cached + q_len
+                row = attn_metadata.prefill_block_tables[int(seq_idx)].to(kc.device)
+                pos = torch.arange(kv_len, device=kc.device)
+                blk = row[pos // bs]
+                if bool((blk < 0).any()):
+                    raise IndexError(
+                        f"prefill block table insufficient to cover {kv_len} tokens (-1 entry reached)"
+                    )
+                k = kc[blk, :, pos % bs, :].repeat_interleave(reps, dim=1)  # [kv_len, H, D]
+                v = vc[blk, :, pos % bs, :].repeat_interleave(reps, dim=1)
+                qpos = torch.arange(cached, kv_len, device=kc.device)
+                mask = pos.unsqueeze(0) <= qpos.unsqueeze(1)
+                q = query[offset:offset + q_len]
+                o = torch.nn.functional.scaled_dot_product_attention(
+                    q.permute(1, 0, 2).unsqueeze(0), k.permute(1, 0, 2).unsqueeze(0),
+                    v.permute(1, 0, 2).unsqueeze(0), attn_mask=mask, is_causal=False, scale=scale,
+                )
+                parts.append(o.squeeze(0).permute(1, 0, 2))
+                offset += q_len
+        if not parts:
+            return query
+        return torch.cat(parts, dim=0)
+
+
+def validate_block_size(block_size: int) -> None:
+    """The pool rule of ``AttentionBackendGPU.allocate_pool`` (:502-506)."""
+    if block_size <= 0 or (block_size & (block_size - 1)) != 0:
+        raise RuntimeError(f"AttentionBackendB200: block_size={block_size} must be a positive power of 2.")

@@ -1,0 +1,88 @@
+"""Build recipe for libmvb200.so (sm_100a) — nvcc, in-tree.
+
+The shared library is written to ``lib/libmvb200.so`` beside this file so it
+travels with the source tree to the GPU host; nothing is installed into
+site-packages and there is no JIT cache.  ``build_native()`` recompiles only
+the objects whose sources (or shared headers) changed.
+
+Run directly to build:  python <package-dir>/build.py [--force] [--verbose]
+"""
+
+from __future__ import annotations
+
+import concurrent.futures as _cf
+import os
+import shutil
+import subprocess
+import sys
+
+PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join(PKG_DIR, "csrc")
+INCLUDE = os.path.join(os.path.dirname(PKG_DIR), "include")
+LIB_DIR = os.path.join(PKG_DIR, "lib")
+OBJ_DIR = os.path.join(LIB_DIR, "obj")
+LIB_PATH = os.path.join(LIB_DIR, "libmvb200.so")
+
+SOURCES = ["kv_write.cu", "decode_fma.cu", "decode_mma.cu", "capi.cu"]
+HEADERS = ["mvb_common.cuh", "decode_common.cuh"]
+
+ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = [
+    "-O3",
+    "-lineinfo",
+    "-std=c++17",
+    "--expt-relaxed-constexpr",
+    "-Xcompiler",
+    "-fPIC",
+]
+
+
+def nvcc_path() -> str:
+    cand = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if not os.path.exists(cand):
+        raise RuntimeError("nvcc not found: the CUDA toolkit is required to build libmvb200.so")
+    return cand
+
+
+def _deps_mtime() -> float:
+    paths = [os.path.join(CSRC, h) for h in HEADERS]
+    paths.append(os.path.join(INCLUDE, "mini_vllm_b200.h"))
+    return max(os.path.getmtime(p) for p in paths)
+
+
+def _compile(src: str, verbose: bool, force: bool) -> str:
+    obj = os.path.join(OBJ_DIR, os.path.splitext(src)[0] + ".o")
+    src_path = os.path.join(CSRC, src)
+    if (
+        not force
+        and os.path.exists(obj)
+        and os.path.getmtime(obj) >= max(os.path.getmtime(src_path), _deps_mtime())
+    ):
+        return obj
+    cmd = [nvcc_path(), *ARCH_FLAGS, *NVCC_FLAGS, "-I", INCLUDE, "-c", src_path, "-o", obj]
+    if verbose:
+        cmd.insert(1, "-Xptxas=-v")
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"nvcc failed for {src}:\n{res.stdout}\n{res.stderr}")
+    if verbose and res.stderr:
+        sys.stderr.write(res.stderr)
+    return obj
+
+
+def build_native(force: bool = False, verbose: bool = False) -> str:
+    """Compile every CUDA source for sm_100a and link ``lib/libmvb200.so``."""
+    os.makedirs(OBJ_DIR, exist_ok=True)
+    with _cf.ThreadPoolExecutor(max_workers=len(SOURCES)) as ex:
+        objs = list(ex.map(lambda s: _compile(s, verbose, force), SOURCES))
+    newest = max(os.path.getmtime(o) for o in objs)
+    if force or not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < newest:
+        cmd = [nvcc_path(), *ARCH_FLAGS, "-shared", "-o", LIB_PATH, *objs, "-lrt", "-ldl", "-lpthread"]
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if res.returncode != 0:
+            raise RuntimeError(f"link of libmvb200.so failed:\n{res.stdout}\n{res.stderr}")
+    return LIB_PATH
+
+
+if __name__ == "__main__":
+    print(build_native(force="--force" in sys.argv, verbose="--verbose" in sys.argv))

@@ -1,0 +1,343 @@
+// C ABI of libmvb200.so: argument checks, the decode plan (kernel variant and
+// split-K partitioning), the TMA tensor-map cache, and the launches.
+// Declarations and contracts: include/mini_vllm_b200.h.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "mvb_common.cuh"
+
+namespace mvb {
+
+cudaError_t launch_kv_write(const void* key, int64_t k_st, int64_t k_sh, const void* value,
+                            int64_t v_st, int64_t v_sh, void* kc, void* vc, const int64_t* slots,
+                            int num_tokens, int kh, int row_bytes, int esize, int block_size,
+                            int64_t total_slots, uint32_t* claims, uint32_t epoch, int* err,
+                            cudaStream_t stream, int sm_count);
+cudaError_t launch_decode_fma(const DecodeArgs& a, int dtype, int head_dim, int maxg,
+                              cudaStream_t stream);
+cudaError_t launch_decode_reduce(const DecodeArgs& a, int dtype, int head_dim, cudaStream_t stream);
+cudaError_t launch_decode_mma(const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a,
+                              int dtype, int head_dim, int max_bids, cudaStream_t stream);
+
+namespace {
+
+constexpr int kAbiVersion = 1;
+// Longest context the auto plan serves with one CTA per (sequence, KV head);
+// beyond it the flash-decoding split is used.
+constexpr int64_t kUnsplitMaxTokens = 8192;
+// Split-K partition length of the auto plan (the north-star's 512 tokens).
+constexpr int kAutoPartitionTokens = 512;
+// Largest partition an MMA CTA accepts (bounds its block-id cache).
+constexpr int kMmaMaxPartitionTokens = 65536;
+constexpr int kMmaHeadGroup = 16;
+
+int elem_size(int dtype) { return dtype == MVB_DTYPE_F32 ? 4 : 2; }
+bool is_pow2(int v) { return v > 0 && (v & (v - 1)) == 0; }
+int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+int sm_count_current() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+struct Plan {
+  int variant;
+  int part_tokens;
+  int num_parts;
+  int head_groups;
+  int maxg;      // heads per CTA group
+  int max_bids;  // block-table entries one partition can span
+  int64_t ws_bytes;
+  int64_t off_m, off_l;  // workspace offsets of the m / l arrays
+};
+
+int make_plan(int num_seqs, int num_heads, int num_kv_heads, int head_dim, int block_size,
+              int num_blocks, int max_blocks, int dtype, int variant, int partition_tokens,
+              const void* cache_ptr, Plan* pl) {
+  if (dtype != MVB_DTYPE_F32 && dtype != MVB_DTYPE_F16 && dtype != MVB_DTYPE_BF16)
+    return MVB_ERR_DTYPE;
+  if (head_dim != 64 && head_dim != 128) return MVB_ERR_HEAD_DIM;
+  if (!is_pow2(block_size)) return MVB_ERR_BLOCK_SIZE;
+  if (num_seqs < 0 || num_heads <= 0 || num_kv_heads <= 0 || num_blocks <= 0 || max_blocks < 0)
+    return MVB_ERR_INVALID_ARG;
+  if (num_heads % num_kv_heads != 0) return MVB_ERR_HEADS;
+  const int G = num_heads / num_kv_heads;
+  const int64_t rows = (int64_t)num_blocks * num_kv_heads * block_size;
+  if (rows * head_dim >= ((int64_t)1 << 62)) return MVB_ERR_INVALID_ARG;
+
+  const bool aligned = cache_ptr == nullptr || (reinterpret_cast<uintptr_t>(cache_ptr) & 15) == 0;
+  const bool mma_ok =
+      dtype != MVB_DTYPE_F32 && block_size % 16 == 0 && aligned && rows < ((int64_t)1 << 31);
+  int v = variant;
+  if (v == MVB_DECODE_AUTO) v = mma_ok ? MVB_DECODE_MMA : MVB_DECODE_FMA;
+  if (v != MVB_DECODE_FMA && v != MVB_DECODE_MMA) return MVB_ERR_VARIANT;
+  if (v == MVB_DECODE_MMA && !mma_ok) return MVB_ERR_VARIANT;
+
+  int maxg;
+  if (v == MVB_DECODE_MMA)
+    maxg = kMmaHeadGroup;
+  else
+    maxg = G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8;
+  const int head_groups = (G + maxg - 1) / maxg;
+
+  const int64_t max_ctx = (int64_t)max_blocks * block_size;
+  int64_t pt;
+  if (partition_tokens > 0) {
+    pt = partition_tokens;
+  } else {
+    const int64_t ctas = (int64_t)num_seqs * num_kv_heads * head_groups;
+    if (max_ctx <= kUnsplitMaxTokens && ctas >= 2 * (int64_t)sm_count_current())
+      pt = max_ctx;
+    else
+      pt = kAutoPartitionTokens;
+  }
+  pt = round_up(pt < 16 ? 16 : pt, 16);
+  if (v == MVB_DECODE_MMA && pt > kMmaMaxPartitionTokens) pt = kMmaMaxPartitionTokens;
+  if (pt > (int64_t)1 << 30) pt = (int64_t)1 << 30;
+  int64_t parts = max_ctx > 0 ? (max_ctx + pt - 1) / pt : 1;
+  if (parts < 1) parts = 1;
+  if ((int64_t)num_seqs * parts >= ((int64_t)1 << 31)) return MVB_ERR_INVALID_ARG;
+
+  pl->variant = v;
+  pl->part_tokens = (int)pt;
+  pl->num_parts = (int)parts;
+  pl->head_groups = head_groups;
+  pl->maxg = maxg;
+  pl->max_bids = (int)((pt + block_size - 1) / block_size + 2);
+  if (parts > 1) {
+    const int64_t n = (int64_t)num_seqs * num_heads * parts;
+    const int64_t o_bytes = round_up(n * head_dim * 4, 256);
+    const int64_t ml_bytes = round_up(n * 4, 256);
+    pl->off_m = o_bytes;
+    pl->off_l = o_bytes + ml_bytes;
+    pl->ws_bytes = o_bytes + 2 * ml_bytes;
+  } else {
+    pl->off_m = pl->off_l = 0;
+    pl->ws_bytes = 0;
+  }
+  return MVB_OK;
+}
+
+// ---- TMA tensor maps over a pool tensor viewed as [rows, head_dim] ---------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+struct MapEntry {
+  const void* ptr;
+  int64_t rows;
+  int head_dim;
+  int dtype;
+  CUtensorMap map;
+};
+std::mutex g_map_mu;
+MapEntry g_maps[64];
+int g_map_count = 0, g_map_next = 0;
+
+bool pool_tensor_map(const void* base, int64_t rows, int head_dim, int dtype, CUtensorMap* out) {
+  std::lock_guard<std::mutex> lock(g_map_mu);
+  for (int i = 0; i < g_map_count; ++i) {
+    const MapEntry& e = g_maps[i];
+    if (e.ptr == base && e.rows == rows && e.head_dim == head_dim && e.dtype == dtype) {
+      *out = e.map;
+      return true;
+    }
+  }
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  CUtensorMap map;
+  const cuuint64_t dims[2] = {(cuuint64_t)head_dim, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)head_dim * 2};
+  const cuuint32_t box[2] = {64, 16};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r =
+      fn(&map, dtype == MVB_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+         2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return false;
+  MapEntry& slot = g_maps[g_map_next];
+  slot.ptr = base;
+  slot.rows = rows;
+  slot.head_dim = head_dim;
+  slot.dtype = dtype;
+  slot.map = map;
+  g_map_next = (g_map_next + 1) % 64;
+  if (g_map_count < 64) ++g_map_count;
+  *out = map;
+  return true;
+}
+
+bool aligned_to(const void* p, int64_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+}  // namespace
+}  // namespace mvb
+
+using namespace mvb;
+
+extern "C" {
+
+int mvb_abi_version(void) { return kAbiVersion; }
+
+const char* mvb_status_string(int status) {
+  switch (status) {
+    case MVB_OK: return "ok";
+    case MVB_ERR_INVALID_ARG: return "invalid argument (shape, size or stride)";
+    case MVB_ERR_DTYPE: return "unsupported dtype";
+    case MVB_ERR_HEAD_DIM: return "head_dim not supported (only 64, 128)";
+    case MVB_ERR_BLOCK_SIZE: return "block_size must be a positive power of 2";
+    case MVB_ERR_ALIGNMENT: return "pointer or stride not aligned to the vector width";
+    case MVB_ERR_CUDA: return "CUDA runtime error";
+    case MVB_ERR_WORKSPACE: return "split-K workspace missing or too small";
+    case MVB_ERR_TENSOR_MAP: return "cuTensorMapEncodeTiled failed";
+    case MVB_ERR_VARIANT: return "requested decode variant cannot run on these inputs";
+    case MVB_ERR_HEADS: return "num_heads must be a multiple of num_kv_heads";
+    default: return "unknown status";
+  }
+}
+
+int mvb_kv_cache_write(const void* key, int64_t key_stride_token, int64_t key_stride_head,
+                       const void* value, int64_t value_stride_token, int64_t value_stride_head,
+                       void* key_cache, void* value_cache, const int64_t* slot_mapping,
+                       int32_t num_tokens, int32_t num_kv_heads, int32_t head_dim,
+                       int32_t block_size, int32_t num_blocks, int32_t dtype,
+                       uint32_t* slot_claims, uint32_t epoch, int32_t* error_flags, void* stream) {
+  if (dtype != MVB_DTYPE_F32 && dtype != MVB_DTYPE_F16 && dtype != MVB_DTYPE_BF16)
+    return MVB_ERR_DTYPE;
+  if (block_size <= 0) return MVB_ERR_BLOCK_SIZE;
+  if (num_tokens < 0 || num_kv_heads <= 0 || head_dim <= 0 || num_blocks <= 0)
+    return MVB_ERR_INVALID_ARG;
+  if (num_tokens == 0) return MVB_OK;
+  if (!key || !value || !key_cache || !value_cache || !slot_mapping || !error_flags)
+    return MVB_ERR_INVALID_ARG;
+  if (slot_claims != nullptr && epoch == 0) return MVB_ERR_INVALID_ARG;
+  const int es = elem_size(dtype);
+  if (!aligned_to(key, es) || !aligned_to(value, es) || !aligned_to(key_cache, es) ||
+      !aligned_to(value_cache, es))
+    return MVB_ERR_ALIGNMENT;
+  const cudaError_t e = launch_kv_write(
+      key, key_stride_token * es, key_stride_head * es, value, value_stride_token * es,
+      value_stride_head * es, key_cache, value_cache, slot_mapping, num_tokens, num_kv_heads,
+      head_dim * es, es, block_size, (int64_t)num_blocks * block_size, slot_claims, epoch,
+      error_flags, static_cast<cudaStream_t>(stream), sm_count_current());
+  return e == cudaSuccess ? MVB_OK : MVB_ERR_CUDA;
+}
+
+int mvb_paged_decode_plan(int32_t num_seqs, int32_t num_heads, int32_t num_kv_heads,
+                          int32_t head_dim, int32_t block_size, int32_t num_blocks,
+                          int32_t max_blocks_per_seq, int32_t dtype, int32_t variant,
+                          int32_t partition_tokens, const void* cache_ptr, int32_t* variant_out,
+                          int32_t* partition_tokens_out, int32_t* num_partitions_out,
+                          int64_t* workspace_bytes_out) {
+  Plan pl;
+  const int st = make_plan(num_seqs, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
+                           max_blocks_per_seq, dtype, variant, partition_tokens, cache_ptr, &pl);
+  if (st != MVB_OK) return st;
+  if (variant_out) *variant_out = pl.variant;
+  if (partition_tokens_out) *partition_tokens_out = pl.part_tokens;
+  if (num_partitions_out) *num_partitions_out = pl.num_parts;
+  if (workspace_bytes_out) *workspace_bytes_out = pl.ws_bytes;
+  return MVB_OK;
+}
+
+int mvb_paged_decode(const void* query, int64_t q_stride_seq, int64_t q_stride_head,
+                     const void* key_cache, const void* value_cache, const int64_t* block_table,
+                     int64_t block_table_stride, int32_t max_blocks_per_seq,
+                     const int32_t* kv_len, void* out, int64_t out_stride_seq,
+                     int64_t out_stride_head, int32_t num_seqs, int32_t num_heads,
+                     int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                     int32_t num_blocks, float scale, int32_t dtype, int32_t variant,
+                     int32_t partition_tokens, void* workspace, int64_t workspace_bytes,
+                     int32_t* error_flags, void* stream) {
+  Plan pl;
+  const int st = make_plan(num_seqs, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
+                           max_blocks_per_seq, dtype, variant, partition_tokens, key_cache, &pl);
+  if (st != MVB_OK) return st;
+  if (num_seqs == 0) return MVB_OK;
+  if (!query || !key_cache || !value_cache || !block_table || !kv_len || !out || !error_flags)
+    return MVB_ERR_INVALID_ARG;
+  if (max_blocks_per_seq > 0 && block_table_stride < max_blocks_per_seq) return MVB_ERR_INVALID_ARG;
+  if (pl.variant == MVB_DECODE_MMA && !aligned_to(value_cache, 16)) return MVB_ERR_VARIANT;
+
+  const int es = elem_size(dtype);
+  // Query loads: 4-byte pairs in the MMA kernel, 16-byte vectors in the FMA kernel.
+  const int64_t qa = pl.variant == MVB_DECODE_MMA ? 4 : 16;
+  if (!aligned_to(query, qa) || (q_stride_seq * es) % qa != 0 || (q_stride_head * es) % qa != 0)
+    return MVB_ERR_ALIGNMENT;
+  if (pl.variant == MVB_DECODE_FMA && (!aligned_to(key_cache, 16) || !aligned_to(value_cache, 16)))
+    return MVB_ERR_ALIGNMENT;
+  if (!aligned_to(out, es)) return MVB_ERR_ALIGNMENT;
+  if (pl.num_parts > 1) {
+    if (workspace == nullptr || workspace_bytes < pl.ws_bytes || !aligned_to(workspace, 256))
+      return MVB_ERR_WORKSPACE;
+  }
+
+  DecodeArgs a;
+  a.q = query;
+  a.q_s0 = q_stride_seq;
+  a.q_s1 = q_stride_head;
+  a.kc = key_cache;
+  a.vc = value_cache;
+  a.bt = block_table;
+  a.bt_s0 = block_table_stride;
+  a.max_blocks = max_blocks_per_seq;
+  a.kv_len = kv_len;
+  a.out = out;
+  a.o_s0 = out_stride_seq;
+  a.o_s1 = out_stride_head;
+  a.num_seqs = num_seqs;
+  a.num_heads = num_heads;
+  a.num_kv_heads = num_kv_heads;
+  a.G = num_heads / num_kv_heads;
+  a.block_size = block_size;
+  a.num_blocks = num_blocks;
+  a.head_groups = pl.head_groups;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.part_tokens = pl.part_tokens;
+  a.num_parts = pl.num_parts;
+  char* ws = static_cast<char*>(workspace);
+  a.part_o = pl.num_parts > 1 ? reinterpret_cast<float*>(ws) : nullptr;
+  a.part_m = pl.num_parts > 1 ? reinterpret_cast<float*>(ws + pl.off_m) : nullptr;
+  a.part_l = pl.num_parts > 1 ? reinterpret_cast<float*>(ws + pl.off_l) : nullptr;
+  a.err = error_flags;
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (pl.variant == MVB_DECODE_MMA) {
+    const int64_t rows = (int64_t)num_blocks * num_kv_heads * block_size;
+    CUtensorMap tmk, tmv;
+    if (!pool_tensor_map(key_cache, rows, head_dim, dtype, &tmk) ||
+        !pool_tensor_map(value_cache, rows, head_dim, dtype, &tmv))
+      return MVB_ERR_TENSOR_MAP;
+    e = launch_decode_mma(tmk, tmv, a, dtype, head_dim, pl.max_bids, s);
+  } else {
+    e = launch_decode_fma(a, dtype, head_dim, pl.maxg, s);
+  }
+  if (e != cudaSuccess) return MVB_ERR_CUDA;
+  if (pl.num_parts > 1) {
+    e = launch_decode_reduce(a, dtype, head_dim, s);
+    if (e != cudaSuccess) return MVB_ERR_CUDA;
+  }
+  return MVB_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,63 @@
+"""Sequence sharding of a paged decode across GPUs, and the output gather.
+
+Sequences are independent in decode attention and each owns its KV blocks, so
+the batch is partitioned by sequence with no exchange inside attention: every
+rank holds its own KV pool and block tables and runs the kernels on its share.
+The only collective is one all-gather of the per-rank outputs (NCCL over
+NVLink when the group is NCCL; gloo on CPU in the tests), after which rank 0
+(or every rank) reorders rows back to the global sequence order.
+
+Assignment is token-balanced with equal sequence counts: sequences sorted by
+context length (longest first) are dealt to ranks in snake order
+0,1,..,R-1,R-1,..,0,0,1,... so each rank's token total is close to B*mean/R.
+"""
+
+from __future__ import annotations
+
+from typing import List
+
+import numpy as np
+
+
+def snake_assignment(context_lens: np.ndarray, world_size: int) -> List[np.ndarray]:
+    """Global sequence indices owned by each rank (each list sorted ascending)."""
+    ctx = np.asarray(context_lens, dtype=np.int64)
+    if world_size < 1:
+        raise ValueError(f"world_size must be >= 1, got {world_size}")
+    order = np.argsort(-ctx, kind="stable")
+    owners: List[List[int]] = [[] for _ in range(world_size)]
+    for pos, seq in enumerate(order.tolist()):
+        rnd, k = divmod(pos, world_size)
+        rank = k if rnd % 2 == 0 else world_size - 1 - k
+        owners[rank].append(seq)
+    return [np.sort(np.asarray(o, dtype=np.int64)) for o in owners]
+
+
+def gather_outputs(local_out, owned: List[np.ndarray], rank: int, group=None):
+    """All-gather every rank's ``local_out`` ([n_rank, H, D]) and return the
+    ``[B, H, D]`` result in global sequence order (on every rank).
+
+    Ranks with fewer sequences pad to the largest share so one
+    ``all_gather_into_tensor`` moves everything; the padding is dropped when
+    the rows are scattered back into global order.
+    """
+    import torch
+    import torch.distributed as dist
+
+    world = len(owned)
+    counts = [int(o.size) for o in owned]
+    cap = max(counts) if counts else 0
+    h, d = local_out.shape[1], local_out.shape[2]
+    send = local_out
+    if local_out.shape[0] < cap:
+        send = torch.zeros((cap, h, d), dtype=local_out.dtype, device=local_out.device)
+        send[: local_out.shape[0]] = local_out
+    recv = torch.empty((world * cap, h, d), dtype=local_out.dtype, device=local_out.device)
+    dist.all_gather_into_tensor(recv, send.contiguous(), group=group)
+    total = sum(counts)
+    out = torch.empty((total, h, d), dtype=local_out.dtype, device=local_out.device)
+    for r in range(world):
+        if counts[r]:
+            idx = torch.from_numpy(owned[r]).to(local_out.device)
+            out[idx] = recv[r * cap: r * cap + counts[r]]
+    return out

@@ -1,0 +1,204 @@
+"""Python side of the CPU oracle — TEST INFRASTRUCTURE ONLY.
+
+Two restatements of the reference's CPU algorithm for the paged KV path:
+
+* ``paged_oracle.c`` (built into ``liboracle.so`` by ``build_oracle``), C with
+  OpenMP — fast enough to check BASELINE-size workloads and to serve as the
+  timed CPU baseline;
+* ``*_numpy`` functions below, plain numpy / Python loops for small cases, used
+  to cross-check the C restatement.
+
+Both are pinned to the reference by ``tests/golden`` (vectors produced by the
+reference's own ``write_to_paged_cache`` and ``AttentionBackendRef``).
+
+Arrays are numpy.  A bf16 tensor is passed as its raw ``uint16`` bits with
+``dtype="bf16"``; ``"f16"`` arrays are ``float16``, ``"f32"`` arrays ``float32``.
+
+Reference lines restated:
+  cache_write  <- mini_vllm/cache/cache_write.py:25-74   (write_to_paged_cache)
+  gather       <- mini_vllm/cache/cache_read.py:19-84     (gather_paged_kv)
+  decode       <- mini_vllm/attention/paged_attention_ref.py:102-161
+                  (AttentionBackendRef.decode_attention; torch SDPA math)
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+import threading
+from typing import Optional, Tuple
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+SRC = os.path.join(HERE, "paged_oracle.c")
+LIB = os.path.join(HERE, "liboracle.so")
+
+ORACLE_OK = 0
+ORACLE_KV_LEN = 1
+ORACLE_TABLE_SHORT = 2
+ORACLE_BLOCK_ID = 3
+
+_CODES = {"f32": 0, "f16": 1, "bf16": 2}
+_lib = None
+_lock = threading.Lock()
+
+
+def build_oracle(force: bool = False) -> str:
+    """Compile ``paged_oracle.c`` into ``liboracle.so`` with gcc + OpenMP."""
+    if force or not os.path.exists(LIB) or os.path.getmtime(LIB) < os.path.getmtime(SRC):
+        cmd = ["gcc", "-O2", "-std=c11", "-fopenmp", "-fPIC", "-shared", SRC, "-o", LIB, "-lm"]
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if res.returncode != 0:
+            raise RuntimeError(f"oracle build failed:\n{res.stderr}")
+    return LIB
+
+
+def _load() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                build_oracle()
+                h = ctypes.CDLL(LIB)
+                vp, i64, i32, f64 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_double
+                h.oracle_cache_write.restype = i32
+                h.oracle_cache_write.argtypes = [vp, vp, vp, vp, vp, i64, i32, i32, i32, i64, i32]
+                h.oracle_gather.restype = i32
+                h.oracle_gather.argtypes = [vp, vp, vp, i64, i64, i32, i32, i32, i32, vp, vp]
+                h.oracle_decode.restype = i32
+                h.oracle_decode.argtypes = [vp, vp, vp, vp, i64, vp, i64, i32, i32, i32, i32, i64,
+                                            f64, i32, i32, vp, vp]
+                h.oracle_max_threads.restype = i32
+                _lib = h
+    return _lib
+
+
+def max_threads() -> int:
+    return int(_load().oracle_max_threads())
+
+
+def _ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+def to_float32(a: np.ndarray, dtype: str) -> np.ndarray:
+    """Upcast storage values to float32 (bf16 bits are widened by a 16-bit shift)."""
+    if dtype == "bf16":
+        return (a.astype(np.uint32) << 16).view(np.float32)
+    return a.astype(np.float32)
+
+
+def _c(a: np.ndarray, dt=None) -> np.ndarray:
+    return np.ascontiguousarray(a if dt is None else a.astype(dt, copy=False))
+
+
+# ---------------------------------------------------------------------------
+# C restatement
+# ---------------------------------------------------------------------------
+def cache_write(key, value, key_cache, value_cache, slot_mapping, block_size: int, dtype: str) -> None:
+    """In-place sequential scatter, last writer wins (cache_write.py:55-74).
+
+    Raises IndexError for the first slot outside [0, num_blocks*block_size)
+    other than -1, after writing the tokens before it, as the reference does.
+    """
+    assert key_cache.flags["C_CONTIGUOUS"] and value_cache.flags["C_CONTIGUOUS"]
+    key, value = _c(key), _c(value)
+    slots = _c(slot_mapping, np.int64)
+    T, KH, D = key.shape
+    NB = key_cache.shape[0]
+    st = _load().oracle_cache_write(_ptr(key), _ptr(value), _ptr(key_cache), _ptr(value_cache),
+                                    _ptr(slots), T, KH, D, block_size, NB, _CODES[dtype])
+    if st < 0:
+        t = -st - 1
+        raise IndexError(
+            f"slot_mapping[{t}] = {int(slots[t])} out of range [0, {NB * block_size}) "
+            f"(block_size={block_size}, num_blocks={NB})"
+        )
+
+
+def gather(key_cache, value_cache, block_ids, num_tokens: int, block_size: int,
+           dtype: str) -> Tuple[np.ndarray, np.ndarray]:
+    """Contiguous [num_tokens, KH, D] K and V from the blocks in logical order."""
+    NB, KH, BS, D = key_cache.shape
+    ids = _c(np.asarray(block_ids, dtype=np.int64).reshape(-1))
+    out_k = np.empty((num_tokens, KH, D), dtype=key_cache.dtype)
+    out_v = np.empty((num_tokens, KH, D), dtype=key_cache.dtype)
+    if num_tokens == 0:
+        return out_k, out_v
+    st = _load().oracle_gather(_ptr(_c(key_cache)), _ptr(_c(value_cache)), _ptr(ids), ids.size,
+                               num_tokens, KH, D, block_size, _CODES[dtype], _ptr(out_k), _ptr(out_v))
+    if st != 0:
+        raise IndexError(
+            f"block_table length {ids.size} insufficient to cover {num_tokens} tokens "
+            f"(block_size={block_size})"
+        )
+    return out_k, out_v
+
+
+def decode(query, key_cache, value_cache, block_table, kv_len, block_size: int, dtype: str,
+           scale: Optional[float] = None, threads: int = 0) -> Tuple[np.ndarray, np.ndarray]:
+    """Paged decode attention in float64 arithmetic; returns (out float32 [Nd,H,D], status [Nd])."""
+    q = _c(query)
+    Nd, H, D = q.shape
+    NB, KH, BS, _ = key_cache.shape
+    bt = _c(block_table, np.int64)
+    if bt.ndim == 1:
+        bt = bt.reshape(Nd, -1)
+    kvl = _c(kv_len, np.int32)
+    if scale is None:
+        scale = D ** -0.5
+    out = np.zeros((Nd, H, D), dtype=np.float32)
+    status = np.zeros(Nd, dtype=np.int32)
+    _load().oracle_decode(_ptr(q), _ptr(_c(key_cache)), _ptr(_c(value_cache)), _ptr(bt), bt.shape[1],
+                          _ptr(kvl), Nd, H, KH, D, block_size, NB, float(scale), _CODES[dtype],
+                          int(threads), _ptr(out), _ptr(status))
+    return out, status
+
+
+# ---------------------------------------------------------------------------
+# numpy restatement (small cases)
+# ---------------------------------------------------------------------------
+def cache_write_numpy(key, value, key_cache, value_cache, slot_mapping, block_size: int) -> None:
+    """Token loop of write_to_paged_cache (cache_write.py:55-74), on numpy arrays."""
+    total = key_cache.shape[0] * block_size
+    for t, slot in enumerate(np.asarray(slot_mapping).tolist()):
+        if slot == -1:
+            continue
+        if slot < -1 or slot >= total:
+            raise IndexError(f"slot_mapping[{t}] = {slot} out of range [0, {total})")
+        key_cache[slot // block_size, :, slot % block_size, :] = key[t]
+        value_cache[slot // block_size, :, slot % block_size, :] = value[t]
+
+
+def decode_numpy(query, key_cache, value_cache, block_table, kv_len, block_size: int, dtype: str,
+                 scale: Optional[float] = None) -> np.ndarray:
+    """Per-sequence gather + repeat_interleave + softmax attention in float64
+    (paged_attention_ref.py:132-161 with cache_read.py:40-84)."""
+    q = to_float32(np.asarray(query), dtype).astype(np.float64)
+    kc = to_float32(np.asarray(key_cache), dtype)
+    vc = to_float32(np.asarray(value_cache), dtype)
+    Nd, H, D = q.shape
+    KH = kc.shape[1]
+    G = H // KH
+    if scale is None:
+        scale = D ** -0.5
+    out = np.zeros((Nd, H, D), dtype=np.float32)
+    for s in range(Nd):
+        n = int(kv_len[s])
+        ids = [int(b) for b in np.asarray(block_table[s]).tolist() if b != -1]
+        if (n + block_size - 1) // block_size > len(ids):
+            raise IndexError(f"block_table length {len(ids)} insufficient to cover {n} tokens")
+        pos = np.arange(n)
+        blk = np.asarray(ids, dtype=np.int64)[pos // block_size]
+        k = kc[blk, :, pos % block_size, :].astype(np.float64)  # [n, KH, D]
+        v = vc[blk, :, pos % block_size, :].astype(np.float64)
+        k = np.repeat(k, G, axis=1)  # repeat_interleave over heads
+        v = np.repeat(v, G, axis=1)
+        logits = np.einsum("hd,nhd->hn", q[s], k) * scale
+        logits -= logits.max(axis=1, keepdims=True)
+        p = np.exp(logits)
+        p /= p.sum(axis=1, keepdims=True)
+        out[s] = np.einsum("hn,nhd->hd", p, v).astype(np.float32)
+    return out

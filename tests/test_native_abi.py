@@ -1,0 +1,129 @@
+"""The C-ABI library loads without a GPU and exports what include/ declares (CPU only).
+
+No kernel is launched here: only host-side entry points (version, status
+strings, the decode plan, argument rejection) run.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+import mini_vllm_b200 as M
+from mini_vllm_b200 import _native
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include",
+                      "mini_vllm_b200.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(mvb_\w+)\s*\(", text, re.M)))
+
+
+def test_header_declares_the_abi():
+    syms = declared_symbols()
+    assert "mvb_kv_cache_write" in syms and "mvb_paged_decode" in syms
+    assert set(syms) == set(_native.SIGNATURES), "ctypes table and header must list the same symbols"
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _native.lib()
+    raw = ctypes.CDLL(_native.LIB_PATH)
+    for name in declared_symbols():
+        assert hasattr(raw, name), name
+        assert hasattr(lib, name), name
+
+
+def test_abi_version_and_status_strings():
+    lib = _native.lib()
+    assert lib.mvb_abi_version() == _native.ABI_VERSION
+    assert "head_dim" in _native.status_string(_native.ERR_HEAD_DIM)
+    assert "power of 2" in _native.status_string(_native.ERR_BLOCK_SIZE)
+    assert _native.status_string(0) == "ok"
+    assert _native.status_string(-999) == "unknown status"
+
+
+def test_header_constants_match_binding():
+    text = open(HEADER).read()
+    consts = dict((k, int(v)) for k, v in re.findall(r"#define\s+(MVB_\w+)\s+(-?\d+)", text))
+    assert consts["MVB_DTYPE_BF16"] == _native.DTYPE_BF16
+    assert consts["MVB_DTYPE_F16"] == _native.DTYPE_F16
+    assert consts["MVB_DEV_DUP_SLOT"] == _native.DEV_DUP_SLOT
+    assert consts["MVB_DEV_TIMEOUT"] == _native.DEV_TIMEOUT
+    assert consts["MVB_ERR_VARIANT"] == _native.ERR_VARIANT
+    assert consts["MVB_DECODE_MMA"] == _native.DECODE_MMA
+
+
+def _plan(**kw):
+    args = dict(num_seqs=256, num_heads=14, num_kv_heads=2, head_dim=64, block_size=16,
+                num_blocks=20000, max_blocks_per_seq=128, dtype=torch.bfloat16)
+    args.update(kw)
+    return M.decode_plan(**args)
+
+
+def test_plan_headline_config_runs_unsplit_on_tensor_cores():
+    p = _plan()
+    assert p == {"variant": "mma", "partition_tokens": 2048, "num_partitions": 1, "workspace_bytes": 0}
+
+
+def test_plan_long_context_uses_split_k():
+    p = _plan(num_seqs=32, max_blocks_per_seq=2048, num_blocks=72090)
+    assert p["variant"] == "mma" and p["partition_tokens"] == 512 and p["num_partitions"] == 64
+    n = 32 * 14 * 64
+    assert p["workspace_bytes"] >= n * 64 * 4 + 2 * n * 4
+
+
+def test_plan_fp32_and_small_blocks_use_fma():
+    assert _plan(dtype=torch.float32)["variant"] == "fma"
+    assert _plan(block_size=8, max_blocks_per_seq=256)["variant"] == "fma"
+    with pytest.raises(RuntimeError, match="variant"):
+        _plan(dtype=torch.float32, variant="mma")
+
+
+def test_plan_explicit_partition_rounds_to_16():
+    p = _plan(partition_tokens=100)
+    assert p["partition_tokens"] == 112 and p["num_partitions"] == 19
+
+
+@pytest.mark.parametrize("kw,match", [
+    (dict(head_dim=96), "head_dim"),
+    (dict(block_size=3), "power of 2"),
+    (dict(num_heads=14, num_kv_heads=3), "multiple"),
+])
+def test_plan_rejects_bad_shapes(kw, match):
+    with pytest.raises(AssertionError, match=match):
+        _plan(**kw)
+
+
+def test_kv_write_host_checks_without_gpu():
+    lib = _native.lib()
+    # zero tokens: nothing to do, no device touched
+    assert lib.mvb_kv_cache_write(None, 0, 0, None, 0, 0, None, None, None, 0, 2, 64, 16, 4,
+                                  _native.DTYPE_BF16, None, 0, None, None) == _native.OK
+    assert lib.mvb_kv_cache_write(None, 0, 0, None, 0, 0, None, None, None, 1, 2, 64, 16, 4,
+                                  7, None, 0, None, None) == _native.ERR_DTYPE
+    assert lib.mvb_kv_cache_write(None, 0, 0, None, 0, 0, None, None, None, 1, 2, 64, 0, 4,
+                                  _native.DTYPE_BF16, None, 0, None, None) == _native.ERR_BLOCK_SIZE
+    assert lib.mvb_kv_cache_write(None, 0, 0, None, 0, 0, None, None, None, 1, 2, 64, 16, 4,
+                                  _native.DTYPE_BF16, None, 0, None, None) == _native.ERR_INVALID_ARG
+
+
+def test_decode_host_checks_without_gpu():
+    lib = _native.lib()
+    common = dict(bt_stride=8, maxb=8)
+
+    def call(num_seqs, head_dim=64, block_size=16, nh=14, nkv=2, ws=None, wsb=0, variant=0, part=0):
+        return lib.mvb_paged_decode(None, 0, 0, None, None, None, common["bt_stride"], common["maxb"], None,
+                                    None, 0, 0, num_seqs, nh, nkv, head_dim, block_size, 100, 0.125,
+                                    _native.DTYPE_BF16, variant, part, ws, wsb, None, None)
+
+    assert call(0) == _native.OK  # empty batch
+    assert call(1) == _native.ERR_INVALID_ARG  # null pointers
+    assert call(1, head_dim=80) == _native.ERR_HEAD_DIM
+    assert call(1, block_size=12) == _native.ERR_BLOCK_SIZE
+    assert call(1, nh=7, nkv=2) == _native.ERR_HEADS
