@@ -59,9 +59,13 @@ extern "C" {
 #define MVB_DEV_TIMEOUT      32   /* a bounded pipeline wait ran out            */
 
 /* ---- decode kernel variants --------------------------------------------- */
-#define MVB_DECODE_AUTO 0  /* MMA when eligible, else FMA                        */
+#define MVB_DECODE_AUTO 0  /* STREAM when eligible, else MMA, else FMA           */
 #define MVB_DECODE_FMA  1  /* CUDA-core FP32 FMA kernel (any dtype, any BS)      */
-#define MVB_DECODE_MMA  2  /* TMA-staged tensor-core kernel (bf16/f16, BS%16==0) */
+#define MVB_DECODE_MMA  2  /* TMA-staged tensor-core kernel, one CTA per (seq, KV head),
+                              split-K + reduction for long contexts (bf16/f16, BS%16==0) */
+#define MVB_DECODE_STREAM 3 /* persistent stream-K variant of MVB_DECODE_MMA: equal tile
+                              ranges per warp + a fixup kernel merging cut units
+                              (num_seqs <= 4096) */
 
 /* ABI version; bumped whenever a signature below changes. */
 int mvb_abi_version(void);
@@ -97,9 +101,10 @@ int mvb_kv_cache_write(const void* key, int64_t key_stride_token, int64_t key_st
 
 /*
  * Plan a paged decode: picks the kernel variant and the split-K partition
- * length for the given shape and returns the split-K workspace size in bytes
- * (0 when the decode runs unsplit).  `variant` / `partition_tokens` are the
- * caller's requests (MVB_DECODE_AUTO / 0 = let the library choose).
+ * length for the given shape and returns the workspace size in bytes (0 when
+ * the decode needs none).  MVB_DECODE_STREAM reports partition_tokens = 0 and
+ * num_partitions = 0; its workspace needs no initialisation.  `variant` /
+ * `partition_tokens` are the caller's requests (MVB_DECODE_AUTO / 0 = let the library choose).
  * `cache_ptr` is only inspected for TMA alignment (it may be NULL, in which
  * case alignment is assumed).
  */
@@ -126,6 +131,7 @@ int mvb_paged_decode_plan(int32_t num_seqs, int32_t num_heads, int32_t num_kv_he
  * dtype.  When the plan (same arguments) says num_partitions > 1 the call runs
  * the flash-decoding split-K kernel followed by the cross-partition reduction
  * and needs `workspace` of at least workspace_bytes (256-byte aligned).
+ * MVB_DECODE_STREAM also needs the workspace (see mvb_paged_decode_plan).
  */
 int mvb_paged_decode(const void* query, int64_t q_stride_seq, int64_t q_stride_head,
                      const void* key_cache, const void* value_cache,

@@ -43,6 +43,7 @@ DEV_TIMEOUT = 32
 DECODE_AUTO = 0
 DECODE_FMA = 1
 DECODE_MMA = 2
+DECODE_STREAM = 3
 
 ABI_VERSION = 1
 

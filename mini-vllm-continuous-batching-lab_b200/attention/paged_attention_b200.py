@@ -51,7 +51,8 @@ _DTYPE_CODES = {
     torch.float16: _native.DTYPE_F16,
     torch.bfloat16: _native.DTYPE_BF16,
 }
-_VARIANTS = {"auto": _native.DECODE_AUTO, "fma": _native.DECODE_FMA, "mma": _native.DECODE_MMA}
+_VARIANTS = {"auto": _native.DECODE_AUTO, "fma": _native.DECODE_FMA, "mma": _native.DECODE_MMA,
+             "stream": _native.DECODE_STREAM}
 _VARIANT_NAMES = {v: k for k, v in _VARIANTS.items()}
 
 
@@ -73,7 +74,7 @@ class _DeviceState:
         self.device = device
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
         self._claims: Dict[int, Tuple[torch.Tensor, int]] = {}
-        self._workspace: Optional[torch.Tensor] = None
+        self._workspaces: Dict[str, torch.Tensor] = {}
 
     def next_claims(self, total_slots: int) -> Tuple[torch.Tensor, int]:
         """Claim array for a pool of ``total_slots`` and a fresh epoch (never 0)."""
@@ -90,10 +91,16 @@ class _DeviceState:
         self._claims[total_slots] = (arr, epoch)
         return arr, epoch
 
-    def workspace(self, nbytes: int) -> torch.Tensor:
-        if self._workspace is None or self._workspace.numel() < nbytes:
-            self._workspace = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
-        return self._workspace
+    def workspace(self, nbytes: int, variant: str) -> torch.Tensor:
+        """Decode workspace of one kernel variant (the stream kernel and the
+        split-K kernels each keep their own buffer), zero-filled when allocated."""
+        key = "stream" if variant == "stream" else "split"
+        buf = self._workspaces.get(key)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+            self._workspaces[key] = buf
+        return buf
+
 
 
 _states: Dict[int, _DeviceState] = {}
@@ -318,8 +325,9 @@ def paged_decode_attention(
         block_size: tokens per block (power of two).
         scale: softmax scale, default ``head_dim ** -0.5``.
     Keyword-only extensions: ``out`` (write in place), ``variant``
-    (``"auto" | "mma" | "fma"``), ``partition_tokens`` (split-K partition
-    length; ``None`` lets the library choose), ``strict``.
+    (``"auto" | "stream" | "mma" | "fma"``), ``partition_tokens`` (split-K
+    partition length of the ``"mma"`` / ``"fma"`` kernels; ``None`` lets the
+    library choose), ``strict``.
 
     Returns ``[total_decode, num_q_heads, head_dim]`` in the query's dtype.
     """
@@ -338,14 +346,14 @@ def paged_decode_attention(
     _require(query.dtype in _DTYPE_CODES, f"query dtype {query.dtype} must be bf16, f16 or f32")
     _require(key_cache.dtype == query.dtype and value_cache.dtype == query.dtype,
              f"cache dtype {key_cache.dtype} != query dtype {query.dtype}")
-    _require(query.device.type == "cuda", f"query.device must be cuda, got {query.device}")
-    _require(key_cache.device == query.device and value_cache.device == query.device,
-             "query and caches must share one device")
     _require(key_cache.is_contiguous() and value_cache.is_contiguous(), "caches must be contiguous")
     _require(block_table.dim() == 2 and block_table.shape[0] == total_decode,
              f"block_table rows {tuple(block_table.shape)} != total_decode {total_decode}")
     _require(kv_len_after.shape == (total_decode,),
              f"kv_len_after shape {tuple(kv_len_after.shape)} != ({total_decode},)")
+    _require(query.device.type == "cuda", f"query.device must be cuda, got {query.device}")
+    _require(key_cache.device == query.device and value_cache.device == query.device,
+             "query and caches must share one device")
     if scale is None:
         scale = head_dim ** -0.5
 
@@ -371,7 +379,7 @@ def paged_decode_attention(
     plan = decode_plan(total_decode, num_q_heads, num_kv_heads, head_dim, block_size, num_blocks,
                        max_blocks, query.dtype, variant, partition_tokens, key_cache.data_ptr())
     ws_bytes = plan["workspace_bytes"]
-    ws_ptr = state.workspace(ws_bytes).data_ptr() if ws_bytes > 0 else None
+    ws_ptr = state.workspace(ws_bytes, plan["variant"]).data_ptr() if ws_bytes > 0 else None
     status = _native.lib().mvb_paged_decode(
         query.data_ptr(), query.stride(0), query.stride(1),
         key_cache.data_ptr(), value_cache.data_ptr(),

@@ -19,6 +19,11 @@ cudaError_t launch_decode_fma(const DecodeArgs& a, int dtype, int head_dim, int 
 cudaError_t launch_decode_reduce(const DecodeArgs& a, int dtype, int head_dim, cudaStream_t stream);
 cudaError_t launch_decode_mma(const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a,
                               int dtype, int head_dim, int max_bids, cudaStream_t stream);
+cudaError_t launch_decode_stream(const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a,
+                                 int dtype, int head_dim, int* scratch, float* part, int max_warps,
+                                 int sm_count, cudaStream_t stream);
+int stream_warps_per_cta(int head_dim);
+int stream_smem_bytes(int head_dim, int num_seqs);
 
 namespace {
 
@@ -31,6 +36,11 @@ constexpr int kAutoPartitionTokens = 512;
 // Largest partition an MMA CTA accepts (bounds its block-id cache).
 constexpr int kMmaMaxPartitionTokens = 65536;
 constexpr int kMmaHeadGroup = 16;
+// Largest batch the stream kernel serves (its CTAs hold the per-sequence tile prefix in smem).
+constexpr int kStreamMaxSeqs = 4096;
+
+// Shared memory of one B200 SM, used when no device can be queried.
+constexpr int kDefaultSmemPerSm = 233472;
 
 int elem_size(int dtype) { return dtype == MVB_DTYPE_F32 ? 4 : 2; }
 bool is_pow2(int v) { return v > 0 && (v & (v - 1)) == 0; }
@@ -49,6 +59,15 @@ int sm_count_current() {
   return cache[dev];
 }
 
+int smem_per_sm_current() {
+  int dev = 0, v = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess ||
+      v <= 0)
+    return kDefaultSmemPerSm;
+  return v;
+}
+
 struct Plan {
   int variant;
   int part_tokens;
@@ -58,6 +77,8 @@ struct Plan {
   int max_bids;  // block-table entries one partition can span
   int64_t ws_bytes;
   int64_t off_m, off_l;  // workspace offsets of the m / l arrays
+  int max_warps;         // stream variant: warps the partial-state slots cover
+  int64_t off_part;      // stream variant: workspace offset of the partial slots
 };
 
 int make_plan(int num_seqs, int num_heads, int num_kv_heads, int head_dim, int block_size,
@@ -77,10 +98,39 @@ int make_plan(int num_seqs, int num_heads, int num_kv_heads, int head_dim, int b
   const bool aligned = cache_ptr == nullptr || (reinterpret_cast<uintptr_t>(cache_ptr) & 15) == 0;
   const bool mma_ok =
       dtype != MVB_DTYPE_F32 && block_size % 16 == 0 && aligned && rows < ((int64_t)1 << 31);
+  const int64_t max_ctx_tiles = ((int64_t)max_blocks * block_size + 15) / 16;
+  const int khg16 = num_kv_heads * ((G + kMmaHeadGroup - 1) / kMmaHeadGroup);
+  const bool stream_ok = mma_ok && num_seqs <= kStreamMaxSeqs &&
+                         (int64_t)num_seqs * khg16 * max_ctx_tiles < ((int64_t)1 << 31);
   int v = variant;
-  if (v == MVB_DECODE_AUTO) v = mma_ok ? MVB_DECODE_MMA : MVB_DECODE_FMA;
-  if (v != MVB_DECODE_FMA && v != MVB_DECODE_MMA) return MVB_ERR_VARIANT;
+  if (v == MVB_DECODE_AUTO) v = stream_ok ? MVB_DECODE_STREAM : mma_ok ? MVB_DECODE_MMA : MVB_DECODE_FMA;
+  if (v != MVB_DECODE_FMA && v != MVB_DECODE_MMA && v != MVB_DECODE_STREAM) return MVB_ERR_VARIANT;
   if (v == MVB_DECODE_MMA && !mma_ok) return MVB_ERR_VARIANT;
+  if (v == MVB_DECODE_STREAM && !stream_ok) return MVB_ERR_VARIANT;
+
+  if (v == MVB_DECODE_STREAM) {
+    // One contiguous tile range per warp; workspace = the per-sequence tile
+    // prefix and context lengths, then two partial-state slots per warp of the
+    // largest grid the GPU can hold.
+    const int nw = stream_warps_per_cta(head_dim);
+    const int smem = stream_smem_bytes(head_dim, num_seqs);
+    int per_sm = smem_per_sm_current() / (smem + 1024);
+    if (per_sm > 2048 / (nw * 32)) per_sm = 2048 / (nw * 32);
+    if (per_sm < 1) per_sm = 1;
+    pl->variant = v;
+    pl->part_tokens = 0;
+    pl->num_parts = 0;
+    pl->head_groups = (G + kMmaHeadGroup - 1) / kMmaHeadGroup;
+    pl->maxg = kMmaHeadGroup;
+    pl->max_bids = 0;
+    pl->max_warps = per_sm * sm_count_current() * nw;
+    pl->off_m = pl->off_l = 0;
+    pl->off_part = round_up((int64_t)(2 * num_seqs + 1) * 4, 256);
+    pl->ws_bytes = pl->off_part + (int64_t)pl->max_warps * 2 * 16 * (head_dim + 2) * 4;
+    return MVB_OK;
+  }
+  pl->max_warps = 0;
+  pl->off_part = 0;
 
   int maxg;
   if (v == MVB_DECODE_MMA)
@@ -276,17 +326,17 @@ int mvb_paged_decode(const void* query, int64_t q_stride_seq, int64_t q_stride_h
   if (!query || !key_cache || !value_cache || !block_table || !kv_len || !out || !error_flags)
     return MVB_ERR_INVALID_ARG;
   if (max_blocks_per_seq > 0 && block_table_stride < max_blocks_per_seq) return MVB_ERR_INVALID_ARG;
-  if (pl.variant == MVB_DECODE_MMA && !aligned_to(value_cache, 16)) return MVB_ERR_VARIANT;
+  if (pl.variant != MVB_DECODE_FMA && !aligned_to(value_cache, 16)) return MVB_ERR_VARIANT;
 
   const int es = elem_size(dtype);
   // Query loads: 4-byte pairs in the MMA kernel, 16-byte vectors in the FMA kernel.
-  const int64_t qa = pl.variant == MVB_DECODE_MMA ? 4 : 16;
+  const int64_t qa = pl.variant == MVB_DECODE_FMA ? 16 : 4;
   if (!aligned_to(query, qa) || (q_stride_seq * es) % qa != 0 || (q_stride_head * es) % qa != 0)
     return MVB_ERR_ALIGNMENT;
   if (pl.variant == MVB_DECODE_FMA && (!aligned_to(key_cache, 16) || !aligned_to(value_cache, 16)))
     return MVB_ERR_ALIGNMENT;
   if (!aligned_to(out, es)) return MVB_ERR_ALIGNMENT;
-  if (pl.num_parts > 1) {
+  if (pl.ws_bytes > 0) {
     if (workspace == nullptr || workspace_bytes < pl.ws_bytes || !aligned_to(workspace, 256))
       return MVB_ERR_WORKSPACE;
   }
@@ -322,6 +372,17 @@ int mvb_paged_decode(const void* query, int64_t q_stride_seq, int64_t q_stride_h
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e;
+  if (pl.variant == MVB_DECODE_STREAM) {
+    const int64_t rows = (int64_t)num_blocks * num_kv_heads * block_size;
+    CUtensorMap tmk, tmv;
+    if (!pool_tensor_map(key_cache, rows, head_dim, dtype, &tmk) ||
+        !pool_tensor_map(value_cache, rows, head_dim, dtype, &tmv))
+      return MVB_ERR_TENSOR_MAP;
+    e = launch_decode_stream(tmk, tmv, a, dtype, head_dim, reinterpret_cast<int*>(ws),
+                             reinterpret_cast<float*>(ws + pl.off_part), pl.max_warps,
+                             sm_count_current(), s);
+    return e == cudaSuccess ? MVB_OK : MVB_ERR_CUDA;
+  }
   if (pl.variant == MVB_DECODE_MMA) {
     const int64_t rows = (int64_t)num_blocks * num_kv_heads * block_size;
     CUtensorMap tmk, tmv;

@@ -167,6 +167,8 @@ cudaError_t launch_fma_t(const DecodeArgs& a, cudaStream_t stream) {
   constexpr int NW = 4;
   constexpr int smem = fma_smem_bytes<T, D, MAXG, NW>();
   static_assert(smem <= 48 * 1024, "FMA merge scratch must fit the default smem window");
+  const cudaError_t e = ensure_kernel_attrs(decode_fma_kernel<T, D, MAXG, NW>, smem);
+  if (e != cudaSuccess) return e;
   dim3 grid((unsigned)(a.num_seqs * a.num_parts), (unsigned)(a.num_kv_heads * a.head_groups));
   decode_fma_kernel<T, D, MAXG, NW><<<grid, NW * 32, smem, stream>>>(a);
   return cudaGetLastError();
@@ -245,6 +247,9 @@ template <typename T>
 cudaError_t launch_reduce_t(const DecodeArgs& a, int head_dim, cudaStream_t stream) {
   const int64_t pairs = (int64_t)a.num_seqs * a.num_heads;
   const unsigned blocks = (unsigned)((pairs + 3) / 4);
+  cudaError_t e = head_dim == 64 ? ensure_kernel_attrs(decode_reduce_kernel<T, 64>, 0)
+                                 : ensure_kernel_attrs(decode_reduce_kernel<T, 128>, 0);
+  if (e != cudaSuccess) return e;
   if (head_dim == 64)
     decode_reduce_kernel<T, 64><<<blocks, 128, 0, stream>>>(a);
   else

@@ -23,41 +23,15 @@
 // Tokens past kv_len inside the last tile are masked to -inf before the max
 // and their V rows are zeroed in shared memory, because the pool comes from
 // torch.empty (mini_vllm/cache/pool.py:8-13) and 0 * NaN would poison the sum.
-#include "decode_common.cuh"
+#include "mma_tile.cuh"
 
 namespace mvb {
-
-constexpr int kTile = 16;  // tokens per pipeline stage
-
-template <int D> struct MmaGeom {
-  static constexpr int SUB = D / 64;                // 64-column (128-byte) panels per row
-  static constexpr int PANEL_BYTES = kTile * 128;   // one swizzled 16 x 64 panel
-  static constexpr int TILE_BYTES = SUB * PANEL_BYTES;  // one K (or V) tile
-  static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
-  static constexpr int KC = D / 16;                 // k-steps of Q K^T
-  static constexpr int NO = D / 8;                  // n-tiles of P V
-};
-
-// Byte offset of 16-byte chunk `ch` (along D) of tile row `r`, under the TMA
-// 128-byte swizzle: inside each 1 KiB atom the chunk index is XOR-ed with r%8.
-__device__ __forceinline__ uint32_t swz(int r, int ch) {
-  return (uint32_t)((ch >> 3) * (kTile * 128) + r * 128 + (((ch & 7) ^ (r & 7)) << 4));
-}
-
-__device__ __forceinline__ uint32_t ld_u32(const void* p) {
-  return __ldg(reinterpret_cast<const unsigned int*>(p));
-}
-
-__device__ __forceinline__ void st_shared_zero16(uint32_t addr) {
-  asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(addr), "r"(0u) : "memory");
-}
 
 template <typename T, int D, int NW, int STAGES>
 __global__ void __launch_bounds__(NW * 32)
 decode_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                   const DecodeArgs a) {
   using Geo = MmaGeom<D>;
-  using MMA = Mma16816<T>;
   static_assert(NW * 16 * D * 4 + 2 * NW * 16 * 4 <= NW * STAGES * Geo::STAGE_BYTES,
                 "merge scratch aliases the stage ring");
 
@@ -123,6 +97,7 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
     if (bid < 0) return -1;
     return (bid * a.num_kv_heads + kvh) * a.block_size + (tok - bi * a.block_size);
   };
+  const uint64_t kv_policy = l2_policy_evict_first();
   // Lane 0 only: start the loads of this warp's local tile j into its stage.
   auto issue = [&](int j) {
     const int s = j % STAGES;
@@ -137,8 +112,8 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
     const uint32_t dv = dk + Geo::TILE_BYTES;
 #pragma unroll
     for (int p = 0; p < Geo::SUB; ++p) {
-      tma_load_2d(dk + p * Geo::PANEL_BYTES, &tmk, p * 64, row, bar);
-      tma_load_2d(dv + p * Geo::PANEL_BYTES, &tmv, p * 64, row, bar);
+      tma_load_2d(dk + p * Geo::PANEL_BYTES, &tmk, p * 64, row, bar, kv_policy);
+      tma_load_2d(dv + p * Geo::PANEL_BYTES, &tmv, p * 64, row, bar, kv_policy);
     }
   };
 
@@ -151,18 +126,7 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
   // ---- query fragments (A operand, rows = heads of the group) ----
   const int g0 = lane >> 2, qd = lane & 3;
   uint32_t qa[Geo::KC][4];
-  {
-    const T* qp = static_cast<const T*>(a.q) + seq * a.q_s0 + (int64_t)h0 * a.q_s1;
-    const bool r0 = g0 < nh, r1 = g0 + 8 < nh;
-#pragma unroll
-    for (int kc = 0; kc < Geo::KC; ++kc) {
-      const int d = kc * 16 + 2 * qd;
-      qa[kc][0] = r0 ? ld_u32(qp + g0 * a.q_s1 + d) : 0u;
-      qa[kc][1] = r1 ? ld_u32(qp + (g0 + 8) * a.q_s1 + d) : 0u;
-      qa[kc][2] = r0 ? ld_u32(qp + g0 * a.q_s1 + d + 8) : 0u;
-      qa[kc][3] = r1 ? ld_u32(qp + (g0 + 8) * a.q_s1 + d + 8) : 0u;
-    }
-  }
+  load_q_frags<T, D>(a, seq, h0, nh, qa);
 
   float o[Geo::NO][4];
 #pragma unroll
@@ -184,78 +148,7 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
     const int valid = min(kTile, t1 - (t0 + i * kTile));
     if (tile_row(i) >= 0) {
       const uint32_t kb = smem_u32(ring + (warp * STAGES + s) * Geo::STAGE_BYTES);
-      const uint32_t vb = kb + Geo::TILE_BYTES;
-      if (valid < kTile) {
-        const int nchunk = (kTile - valid) * (D / 8);
-        for (int e = lane; e < nchunk; e += 32) {
-          const int r = valid + e / (D / 8), ch = e % (D / 8);
-          st_shared_zero16(vb + (ch >> 3) * Geo::PANEL_BYTES + r * 128 + (ch & 7) * 16);
-        }
-        __syncwarp();
-      }
-
-      // S = Q K^T : s0 holds tokens 0-7, s1 tokens 8-15 of the tile.
-      float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int kc = 0; kc < Geo::KC; ++kc) {
-        const int mi = lane >> 3;
-        const int r = (lane & 7) + ((mi >> 1) << 3);
-        const int ch = 2 * kc + (mi & 1);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(kb + swz(r, ch), b0, b1, b2, b3);
-        MMA::run(s0, qa[kc], b0, b1);
-        MMA::run(s1, qa[kc], b2, b3);
-      }
-
-      // Online softmax.  Thread rows: g0 (c0,c1) and g0+8 (c2,c3); its tokens:
-      // 2qd, 2qd+1 (s0) and 8+2qd, 9+2qd (s1).
-      float x[2][4] = {{s0[0], s0[1], s1[0], s1[1]}, {s0[2], s0[3], s1[2], s1[3]}};
-      const int tk0 = 2 * qd;
-      float p[2][4];
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        float mx = -INFINITY;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int tk = tk0 + (k & 1) + ((k >> 1) << 3);
-          x[r][k] = tk < valid ? x[r][k] * a.scale_log2 : -INFINITY;
-          mx = fmaxf(mx, x[r][k]);
-        }
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        const float mn = fmaxf(mrow[r], mx);
-        const float al = fast_exp2(mrow[r] - mn);
-        float sum = 0.f;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          p[r][k] = fast_exp2(x[r][k] - mn);
-          sum += p[r][k];
-        }
-        lrow[r] = fmaf(lrow[r], al, sum);
-        mrow[r] = mn;
-#pragma unroll
-        for (int n = 0; n < Geo::NO; ++n) {
-          o[n][2 * r] *= al;
-          o[n][2 * r + 1] *= al;
-        }
-      }
-      uint32_t pa[4];
-      pa[0] = MMA::pack(p[0][0], p[0][1]);
-      pa[1] = MMA::pack(p[1][0], p[1][1]);
-      pa[2] = MMA::pack(p[0][2], p[0][3]);
-      pa[3] = MMA::pack(p[1][2], p[1][3]);
-
-      // O += P V
-#pragma unroll
-      for (int n = 0; n < Geo::NO; n += 2) {
-        const int mi = lane >> 3;
-        const int r = (lane & 7) + ((mi & 1) << 3);
-        const int ch = n + (mi >> 1);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4_trans(vb + swz(r, ch), b0, b1, b2, b3);
-        MMA::run(o[n], pa, b0, b1);
-        MMA::run(o[n + 1], pa, b2, b3);
-      }
+      attend_tile<T, D>(kb, kb + Geo::TILE_BYTES, valid, a.scale_log2, qa, o, mrow, lrow);
     }
     __syncwarp();
     if (lane == 0 && j + STAGES < my_tiles) {
@@ -309,12 +202,25 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
 // ---------------------------------------------------------------------------
 // host launch
 // ---------------------------------------------------------------------------
+// Warps per CTA and pipeline stages per warp (overridable at build time for tuning sweeps).
+#ifndef MVB_MMA64_NW
+#define MVB_MMA64_NW 4
+#endif
+#ifndef MVB_MMA64_STAGES
+#define MVB_MMA64_STAGES 4
+#endif
+#ifndef MVB_MMA128_NW
+#define MVB_MMA128_NW 4
+#endif
+#ifndef MVB_MMA128_STAGES
+#define MVB_MMA128_STAGES 3
+#endif
 template <int D> struct MmaConfig;
 template <> struct MmaConfig<64> {
-  static constexpr int NW = 4, STAGES = 4;
+  static constexpr int NW = MVB_MMA64_NW, STAGES = MVB_MMA64_STAGES;
 };
 template <> struct MmaConfig<128> {
-  static constexpr int NW = 4, STAGES = 3;
+  static constexpr int NW = MVB_MMA128_NW, STAGES = MVB_MMA128_STAGES;
 };
 
 template <int D>
@@ -335,15 +241,8 @@ cudaError_t launch_mma_t(const CUtensorMap& tmk, const CUtensorMap& tmv, const D
   constexpr int NW = MmaConfig<D>::NW, STAGES = MmaConfig<D>::STAGES;
   auto kern = decode_mma_kernel<T, D, NW, STAGES>;
   const int smem = mma_smem_bytes(D, max_bids);
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
+  const cudaError_t e = ensure_kernel_attrs(kern, smem);
   if (e != cudaSuccess) return e;
-  static int granted[64] = {0};  // dynamic-smem opt-in already granted, per device
-  if (dev >= 64 || granted[dev] < smem) {
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    if (dev < 64) granted[dev] = smem;
-  }
   dim3 grid((unsigned)(a.num_seqs * a.num_parts), (unsigned)(a.num_kv_heads * a.head_groups));
   kern<<<grid, NW * 32, smem, stream>>>(tmk, tmv, a);
   return cudaGetLastError();

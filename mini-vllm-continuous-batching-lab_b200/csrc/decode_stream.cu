@@ -1,0 +1,487 @@
+// Persistent stream-K paged decode (bf16 / f16, block_size a multiple of 16).
+//
+// The decode's work is a stream of 16-token KV tiles: for every sequence s in
+// order, for every (KV head, head group) unit of s, ceil(kv_len[s] / 16) tiles.
+// The grid is sized to the number of CTAs the GPU holds at once, and the stream
+// is cut into one contiguous, equal-length range per WARP, so every warp of the
+// machine streams the same number of bytes and no second wave or ragged tail
+// exists (one CTA per (sequence, KV head) leaves 1.15 waves on config 2).
+//
+// Each warp runs the TMA ring of decode_mma.cu over its range: lane 0 loads
+// K and V tiles STAGES ahead (2-D tensor-map loads, 128-byte swizzle, one
+// mbarrier per stage), all lanes run attend_tile (mma.sync m16n8k16, online
+// softmax).  When the range crosses a unit boundary the warp flushes the unit:
+//   * a unit that lies wholly inside the warp's range is normalised and
+//     written to `out` directly;
+//   * a unit cut by a range boundary is written as a partial state
+//     (m, l, O per head row) to the warp's first or last slot.
+// decode_stream_fixup_kernel then merges the partials of every cut unit (one
+// warp per unit, contributors in warp order, so the result is deterministic).
+// It is launched as a programmatic dependent of the streaming kernel, so its
+// launch overlaps the streaming kernel's tail; merging inside the streaming
+// kernel instead put 10-20 us of dependent L2 round trips on the critical path
+// of whichever warp finished a unit last.
+// The only CTA-wide synchronisation is the prologue, where the CTA scans
+// kv_len into the per-sequence tile prefix it locates tiles with; CTA 0 also
+// stores that prefix for the fixup kernel.
+#include "mma_tile.cuh"
+
+namespace mvb {
+
+constexpr int kStreamRowBatch = 128;  // tiles whose pool rows a warp resolves at once
+
+struct StreamArgs {
+  int* pre_g;     // [num_seqs + 1] tile prefix per sequence (written by CTA 0)
+  int* ctx_g;     // [num_seqs] servable kv_len, 0 for a rejected sequence
+  float* part;    // [num_warps][2][16][D + 2] partial states (m, l, O[D] per row)
+  int num_warps;  // gridDim.x * NW
+};
+
+// Warp whose range [R(w), R(w+1)), R(w) = floor(w * T / Wtot), holds global
+// tile g: the largest w with R(w) <= g.
+__device__ __forceinline__ int stream_warp_of(int g, int T, int Wtot) {
+  return (int)(((int64_t)(g + 1) * Wtot + T - 1) / T) - 1;
+}
+__device__ __forceinline__ int stream_range_start(int w, int T, int Wtot) {
+  return (int)((int64_t)w * T / Wtot);
+}
+
+template <typename T, int D, int NW, int STAGES>
+__global__ void __launch_bounds__(NW * 32)
+decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                     const DecodeArgs a, const StreamArgs sa) {
+  using Geo = MmaGeom<D>;
+  constexpr int KC = D / 16, NO = D / 8, ROW = D + 2;
+
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ int warp_sums[NW];
+  uint8_t* smem =
+      reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + NW * STAGES * Geo::STAGE_BYTES);
+  int* stage_ok = reinterpret_cast<int*>(bars + NW * STAGES);  // [NW][STAGES]
+  int* rows = stage_ok + NW * STAGES;                           // [NW][kStreamRowBatch]
+  int* pre = rows + NW * kStreamRowBatch;                       // [Nd + 1] tile prefix per sequence
+  int* ctxs = pre + a.num_seqs + 1;                             // [Nd] servable kv_len (0 = skipped)
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int Nd = a.num_seqs;
+  const int KHG = a.num_kv_heads * a.head_groups;
+
+  grid_dependency_wait();      // inputs of the previous kernel in the stream are visible
+  grid_launch_dependents();    // the fixup kernel may be scheduled as CTAs retire
+
+  // ---- prologue: tiles per sequence (all its units) and their exclusive prefix ----
+  {
+    constexpr int NT = NW * 32;
+    const int per = (Nd + NT - 1) / NT;
+    const int i0 = min(Nd, tid * per), i1 = min(Nd, i0 + per);
+    int mine = 0;
+    for (int i = i0; i < i1; ++i) {
+      const int c = __ldg(a.kv_len + i);
+      const int bad = seq_error(a, c);
+      ctxs[i] = bad ? 0 : c;
+      const int t = bad ? 0 : ((c + kTile - 1) / kTile) * KHG;
+      pre[i] = t;
+      mine += t;
+      if (bad && blockIdx.x == 0) {
+        atomicOr(a.err, bad);
+        T* out = static_cast<T*>(a.out) + (int64_t)i * a.o_s0;
+        for (int e = 0; e < a.num_heads * D; ++e) out[(e / D) * a.o_s1 + e % D] = from_f32<T>(0.f);
+      }
+    }
+    int incl = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (lane == 31) warp_sums[warp] = incl;
+    __syncthreads();
+    int run = incl - mine, total = 0;
+    for (int w = 0; w < NW; ++w) {
+      if (w < warp) run += warp_sums[w];
+      total += warp_sums[w];
+    }
+    for (int i = i0; i < i1; ++i) {
+      const int t = pre[i];
+      pre[i] = run;
+      run += t;
+    }
+    if (tid == 0) pre[Nd] = total;
+    __syncthreads();
+    if (blockIdx.x == 0) {
+      for (int i = tid; i <= Nd; i += NT) sa.pre_g[i] = pre[i];
+      for (int i = tid; i < Nd; i += NT) sa.ctx_g[i] = ctxs[i];
+    }
+  }
+
+  const int T_all = pre[Nd];
+  const int Wtot = sa.num_warps;
+  const int W = blockIdx.x * NW + warp;
+  auto range_start = [&](int w) { return stream_range_start(w, T_all, Wtot); };
+  const int r0 = range_start(W), r1 = range_start(W + 1);
+  const int n = r1 - r0;
+  if (n <= 0) return;  // no CTA-wide barrier follows
+
+  uint64_t* mybars = bars + warp * STAGES;
+  int* myok = stage_ok + warp * STAGES;
+  int* myrows = rows + warp * kStreamRowBatch;
+  uint8_t* myring = ring + warp * STAGES * Geo::STAGE_BYTES;
+  if (lane == 0) {
+#pragma unroll
+    for (int s = 0; s < STAGES; ++s) mbar_init(smem_u32(mybars + s), 1);
+    fence_mbar_init();
+  }
+  if (lane == 0 && warp == 0) {
+    prefetch_tensormap(&tmk);
+    prefetch_tensormap(&tmv);
+  }
+  __syncwarp();
+
+  // global tile g -> sequence s, unit k of s, tile t of the unit
+  auto locate = [&](int g, int& s, int& k, int& t) {
+    int lo = 0, hi = Nd;  // pre[lo] <= g < pre[hi]
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (pre[mid] <= g)
+        lo = mid;
+      else
+        hi = mid;
+    }
+    s = lo;
+    const int ut = (ctxs[s] + kTile - 1) / kTile;
+    const int off = g - pre[s];
+    k = off / ut;
+    t = off - k * ut;
+  };
+  // All lanes: resolve the pool rows of tiles [j0, j0 + kStreamRowBatch) of this range.
+  auto fill_rows = [&](int j0) {
+    for (int i = lane; i < kStreamRowBatch; i += 32) {
+      const int j = j0 + i;
+      int row = -1;
+      if (j < n) {
+        int s, k, t;
+        locate(r0 + j, s, k, t);
+        const int kvh = k / a.head_groups;
+        const int tok = t * kTile;
+        const int bi = tok / a.block_size;
+        const int64_t b = __ldg(a.bt + (int64_t)s * a.bt_s0 + bi);
+        if (b >= 0 && b < a.num_blocks)
+          row = ((int)b * a.num_kv_heads + kvh) * a.block_size + (tok - bi * a.block_size);
+        else
+          atomicOr(a.err, MVB_DEV_BLOCK_ID);
+      }
+      myrows[i] = row;
+    }
+    __syncwarp();
+  };
+  const uint64_t kv_policy = l2_policy_evict_first();
+  // Lane 0: start the loads of local tile j into its stage.
+  auto issue = [&](int j) {
+    const int st = j % STAGES;
+    const uint32_t bar = smem_u32(mybars + st);
+    const int row = myrows[j % kStreamRowBatch];
+    myok[st] = row >= 0;
+    if (row < 0) {
+      mbar_arrive(bar);
+      return;
+    }
+    mbar_arrive_expect_tx(bar, Geo::STAGE_BYTES);
+    const uint32_t dk = smem_u32(myring + st * Geo::STAGE_BYTES);
+#pragma unroll
+    for (int p = 0; p < Geo::SUB; ++p) {
+      tma_load_2d(dk + p * Geo::PANEL_BYTES, &tmk, p * 64, row, bar, kv_policy);
+      tma_load_2d(dk + Geo::TILE_BYTES + p * Geo::PANEL_BYTES, &tmv, p * 64, row, bar, kv_policy);
+    }
+  };
+
+  fill_rows(0);
+  if (lane == 0) {
+    const int n0 = n < STAGES ? n : STAGES;
+    for (int j = 0; j < n0; ++j) issue(j);
+  }
+
+  const int g0 = lane >> 2, qd = lane & 3;
+  uint32_t qa[KC][4], qa_next[KC][4];
+  float o[NO][4] = {};
+  float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+  int u_start = 0, u_end = -1, u_seq = 0, u_k = 0, u_ctx = 0, h0 = 0, nh = 0;
+  // head group of the next unit of this range, whose Q fragments are prefetched
+  int n_h0 = 0, n_nh = 0;
+
+  // Write the finished unit: normalised into `out` when this warp holds all of
+  // it, else as a partial state for the fixup kernel.
+  auto flush = [&]() {
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 1);
+      lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 2);
+    }
+    T* out = static_cast<T*>(a.out) + (int64_t)u_seq * a.o_s0;
+    if (u_start >= r0 && u_end <= r1) {
+      const float inv0 = 1.f / lrow[0], inv1 = 1.f / lrow[1];
+#pragma unroll
+      for (int nn = 0; nn < NO; ++nn) {
+        const int d = nn * 8 + 2 * qd;
+        if (g0 < nh) {
+          T* p = out + (int64_t)(h0 + g0) * a.o_s1 + d;
+          p[0] = from_f32<T>(o[nn][0] * inv0);
+          p[1] = from_f32<T>(o[nn][1] * inv0);
+        }
+        if (g0 + 8 < nh) {
+          T* p = out + (int64_t)(h0 + g0 + 8) * a.o_s1 + d;
+          p[0] = from_f32<T>(o[nn][2] * inv1);
+          p[1] = from_f32<T>(o[nn][3] * inv1);
+        }
+      }
+      return;
+    }
+    const int slot = u_start < r0 ? 0 : 1;
+    float* P = sa.part + ((int64_t)W * 2 + slot) * 16 * ROW;
+    const bool row0 = g0 < nh, row1 = g0 + 8 < nh;  // rows past the group are padding
+#pragma unroll
+    for (int nn = 0; nn < NO; ++nn) {
+      const int d = 2 + nn * 8 + 2 * qd;
+      if (row0) *reinterpret_cast<float2*>(P + g0 * ROW + d) = make_float2(o[nn][0], o[nn][1]);
+      if (row1) *reinterpret_cast<float2*>(P + (g0 + 8) * ROW + d) = make_float2(o[nn][2], o[nn][3]);
+    }
+    if (qd == 0) {
+      if (row0) *reinterpret_cast<float2*>(P + g0 * ROW) = make_float2(mrow[0], lrow[0]);
+      if (row1) *reinterpret_cast<float2*>(P + (g0 + 8) * ROW) = make_float2(mrow[1], lrow[1]);
+    }
+  };
+
+  // Look up the unit holding global tile g (when g < r1) and prefetch its Q.
+  auto prefetch_next = [&](int g) {
+    if (g >= r1) return;
+    int s, k, t;
+    locate(g, s, k, t);
+    const int kvh = k / a.head_groups, hg = k - kvh * a.head_groups;
+    n_h0 = kvh * a.G + hg * 16;
+    n_nh = min(16, a.G - hg * 16);
+    load_q_frags<T, D>(a, s, n_h0, n_nh, qa_next);
+  };
+
+  prefetch_next(r0);  // the range's first unit (it may start before r0: locate handles it)
+  bool failed = false;
+  int j = 0;
+  for (; j < n; ++j) {
+    const int g = r0 + j;
+    if (g >= u_end) {  // warp-uniform: entering the prefetched unit
+      if (j > 0) flush();
+      {
+        int s, k, t;
+        locate(g, s, k, t);
+        u_start = g - t;
+        u_ctx = ctxs[s];
+        u_seq = s;
+        u_k = k;
+      }
+      u_end = u_start + (u_ctx + kTile - 1) / kTile;
+      h0 = n_h0;
+      nh = n_nh;
+#pragma unroll
+      for (int kc = 0; kc < KC; ++kc)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) qa[kc][e] = qa_next[kc][e];
+      prefetch_next(u_end);
+#pragma unroll
+      for (int nn = 0; nn < NO; ++nn) o[nn][0] = o[nn][1] = o[nn][2] = o[nn][3] = 0.f;
+      mrow[0] = mrow[1] = -INFINITY;
+      lrow[0] = lrow[1] = 0.f;
+    }
+    const int st = j % STAGES;
+    const bool got = mbar_wait_bounded(smem_u32(mybars + st), (uint32_t)((j / STAGES) & 1));
+    if (__any_sync(0xffffffffu, !got)) {
+      failed = true;
+      break;
+    }
+    if (myok[st]) {
+      const int valid = min(kTile, u_ctx - (g - u_start) * kTile);
+      const uint32_t kb = smem_u32(myring + st * Geo::STAGE_BYTES);
+      attend_tile<T, D>(kb, kb + Geo::TILE_BYTES, valid, a.scale_log2, qa, o, mrow, lrow);
+    }
+    __syncwarp();
+    if (j + STAGES < n) {
+      if ((j + STAGES) % kStreamRowBatch == 0) fill_rows(j + STAGES);
+      if (lane == 0) {
+        fence_proxy_async_smem();
+        issue(j + STAGES);
+      }
+    }
+  }
+  if (failed) {
+    if (lane == 0) atomicOr(a.err, MVB_DEV_TIMEOUT);
+    const int issued = min(n, j + STAGES);
+    for (int jj = j; jj < issued; ++jj)
+      mbar_wait_bounded(smem_u32(mybars + jj % STAGES), (uint32_t)((jj / STAGES) & 1));
+    return;  // the unit's output stays unwritten; the error flag reports it
+  }
+  flush();
+}
+
+// ---------------------------------------------------------------------------
+// fixup: merge the partial states of every unit cut by a warp-range boundary
+// ---------------------------------------------------------------------------
+// One warp per (unit, head row) — unit = sequence x KV head x head group.
+// Lane c holds contributor c's (m, l) of the row; M and L come from warp
+// reductions, and each lane accumulates its D/32 columns over the contributors
+// with coefficients broadcast from the owning lane:
+//   out[r][d] = sum_c O_c[r][d] 2^(m_c - M) / L.
+// Contributors are the warps w_first..w_last whose ranges hold tiles of the
+// unit, in warp order, so the result does not depend on timing.
+template <typename T, int D>
+__global__ void __launch_bounds__(128) decode_stream_fixup_kernel(const DecodeArgs a, const StreamArgs sa) {
+  constexpr int ROW = D + 2, DPL = D / 32;
+  grid_dependency_wait();  // the streaming kernel's partials and prefix are visible
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int KHG = a.num_kv_heads * a.head_groups;
+  const int rows = min(16, a.G);  // head rows of a full group
+  const int64_t item = (int64_t)blockIdx.x * 4 + warp;
+  const int64_t u = item / rows;
+  const int r = (int)(item - u * rows);
+  if (u >= (int64_t)a.num_seqs * KHG) return;
+  const int s = (int)(u / KHG), k = (int)(u - (int64_t)s * KHG);
+  const int kvh = k / a.head_groups, hg = k - kvh * a.head_groups;
+  if (r >= min(16, a.G - hg * 16)) return;  // the last head group may be short
+  const int ctx = sa.ctx_g[s];
+  if (ctx <= 0) return;
+  const int T_all = sa.pre_g[a.num_seqs], Wtot = sa.num_warps;
+  const int ut = (ctx + kTile - 1) / kTile;
+  const int us = sa.pre_g[s] + k * ut, ue = us + ut;
+  const int w_first = stream_warp_of(us, T_all, Wtot), w_last = stream_warp_of(ue - 1, T_all, Wtot);
+  if (w_first == w_last) return;  // one warp held the whole unit and wrote it
+  const bool dense = T_all >= Wtot;  // then every warp in [w_first, w_last] has tiles of the unit
+  auto has_tiles = [&](int w) {
+    return dense || stream_range_start(w + 1, T_all, Wtot) > stream_range_start(w, T_all, Wtot);
+  };
+  // w_first keeps the unit in its "last" slot (1), later contributors in slot 0
+  auto row_of = [&](int w) {
+    return sa.part + ((int64_t)w * 2 + (w == w_first ? 1 : 0)) * 16 * ROW + r * ROW;
+  };
+  const int span = w_last - w_first + 1;
+
+  // pass 1: M and L over the contributors (one per lane, chunks of 32 warps)
+  float M = -INFINITY;
+  for (int c0 = 0; c0 < span; c0 += 32) {
+    const int w = w_first + c0 + lane;
+    if (c0 + lane < span && has_tiles(w)) M = fmaxf(M, __ldcg(row_of(w)));
+  }
+#pragma unroll
+  for (int sh = 16; sh > 0; sh >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, sh));
+  float L = 0.f;
+  for (int c0 = 0; c0 < span; c0 += 32) {
+    const int w = w_first + c0 + lane;
+    if (c0 + lane < span && has_tiles(w)) {
+      const float2 ml = __ldcg(reinterpret_cast<const float2*>(row_of(w)));
+      L = fmaf(ml.y, fast_exp2(ml.x - M), L);
+    }
+  }
+#pragma unroll
+  for (int sh = 16; sh > 0; sh >>= 1) L += __shfl_xor_sync(0xffffffffu, L, sh);
+  const float inv = 1.f / L;
+
+  // pass 2: columns, contributors broadcast lane by lane
+  float acc[DPL];
+#pragma unroll
+  for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
+  for (int c0 = 0; c0 < span; c0 += 32) {
+    const int w_mine = w_first + c0 + lane;
+    float coef = 0.f;
+    if (c0 + lane < span && has_tiles(w_mine)) coef = fast_exp2(__ldcg(row_of(w_mine)) - M) * inv;
+    const int nc = min(32, span - c0);
+#pragma unroll 4
+    for (int c = 0; c < nc; ++c) {
+      const float wt = __shfl_sync(0xffffffffu, coef, c);
+      if (wt != 0.f) {
+        const float* P = row_of(w_first + c0 + c) + 2 + lane;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) acc[i] = fmaf(__ldcg(P + 32 * i), wt, acc[i]);
+      }
+    }
+  }
+  T* out = static_cast<T*>(a.out) + (int64_t)s * a.o_s0 + (int64_t)(kvh * a.G + hg * 16 + r) * a.o_s1;
+#pragma unroll
+  for (int i = 0; i < DPL; ++i) out[lane + 32 * i] = from_f32<T>(acc[i]);
+}
+
+// ---------------------------------------------------------------------------
+// host launch
+// ---------------------------------------------------------------------------
+// Warps per CTA and pipeline stages per warp (overridable at build time for tuning sweeps).
+#ifndef MVB_STREAM64_NW
+#define MVB_STREAM64_NW 4
+#endif
+#ifndef MVB_STREAM64_STAGES
+#define MVB_STREAM64_STAGES 4
+#endif
+#ifndef MVB_STREAM128_NW
+#define MVB_STREAM128_NW 4
+#endif
+#ifndef MVB_STREAM128_STAGES
+#define MVB_STREAM128_STAGES 3
+#endif
+template <int D> struct StreamConfig;
+template <> struct StreamConfig<64> {
+  static constexpr int NW = MVB_STREAM64_NW, STAGES = MVB_STREAM64_STAGES;
+};
+template <> struct StreamConfig<128> {
+  static constexpr int NW = MVB_STREAM128_NW, STAGES = MVB_STREAM128_STAGES;
+};
+
+int stream_warps_per_cta(int head_dim) {
+  return head_dim == 64 ? StreamConfig<64>::NW : StreamConfig<128>::NW;
+}
+
+int stream_smem_bytes(int head_dim, int num_seqs) {
+  const int nw = stream_warps_per_cta(head_dim);
+  const int stages = head_dim == 64 ? StreamConfig<64>::STAGES : StreamConfig<128>::STAGES;
+  const int stage_bytes = head_dim == 64 ? MmaGeom<64>::STAGE_BYTES : MmaGeom<128>::STAGE_BYTES;
+  return 1024 + nw * stages * (stage_bytes + 8 + 4) + nw * kStreamRowBatch * 4 +
+         (2 * num_seqs + 1) * 4;
+}
+
+template <typename T, int D>
+cudaError_t launch_stream_t(const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a,
+                            int* scratch, float* part, int max_warps, int sm_count,
+                            cudaStream_t stream) {
+  constexpr int NW = StreamConfig<D>::NW, STAGES = StreamConfig<D>::STAGES;
+  auto kern = decode_stream_kernel<T, D, NW, STAGES>;
+  const int smem = stream_smem_bytes(D, a.num_seqs);
+  cudaError_t e = ensure_kernel_attrs(kern, smem);
+  if (e != cudaSuccess) return e;
+  e = ensure_kernel_attrs(decode_stream_fixup_kernel<T, D>, 0);
+  if (e != cudaSuccess) return e;
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, NW * 32, smem);
+  if (e != cudaSuccess) return e;
+  if (per_sm < 1) per_sm = 1;
+  int ctas = per_sm * sm_count;
+  if (ctas * NW > max_warps) ctas = max_warps / NW;
+  if (ctas < 1) return cudaErrorInvalidConfiguration;
+  StreamArgs sa;
+  sa.pre_g = scratch;
+  sa.ctx_g = scratch + a.num_seqs + 1;
+  sa.part = part;
+  sa.num_warps = ctas * NW;
+  e = launch_pdl(kern, dim3(ctas), dim3(NW * 32), smem, stream, tmk, tmv, a, sa);
+  if (e != cudaSuccess) return e;
+  const int64_t items = (int64_t)a.num_seqs * a.num_kv_heads * a.head_groups * (a.G < 16 ? a.G : 16);
+  return launch_pdl(decode_stream_fixup_kernel<T, D>, dim3((unsigned)((items + 3) / 4)), dim3(128), 0,
+                    stream, a, sa);
+}
+
+cudaError_t launch_decode_stream(const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a,
+                                 int dtype, int head_dim, int* scratch, float* part, int max_warps,
+                                 int sm_count, cudaStream_t stream) {
+  if (dtype == MVB_DTYPE_BF16)
+    return head_dim == 64
+               ? launch_stream_t<__nv_bfloat16, 64>(tmk, tmv, a, scratch, part, max_warps, sm_count, stream)
+               : launch_stream_t<__nv_bfloat16, 128>(tmk, tmv, a, scratch, part, max_warps, sm_count, stream);
+  return head_dim == 64
+             ? launch_stream_t<__half, 64>(tmk, tmv, a, scratch, part, max_warps, sm_count, stream)
+             : launch_stream_t<__half, 128>(tmk, tmv, a, scratch, part, max_warps, sm_count, stream);
+}
+
+}  // namespace mvb

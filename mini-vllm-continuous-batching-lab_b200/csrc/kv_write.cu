@@ -31,6 +31,8 @@ kv_write_kernel(const char* __restrict__ key, int64_t k_st, int64_t k_sh,
                 int block_size, int64_t total_slots, uint32_t* __restrict__ claims, uint32_t epoch,
                 int* __restrict__ err) {
   using V = typename VecType<VB>::type;
+  grid_dependency_wait();    // key/value/slots of the previous kernel are visible
+  grid_launch_dependents();  // the decode that follows may be scheduled early
   const int chunks = row_bytes / VB;
   const int64_t items = (int64_t)num_tokens * kh * chunks;
   for (int64_t it = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; it < items;
@@ -60,7 +62,7 @@ kv_write_kernel(const char* __restrict__ key, int64_t k_st, int64_t k_sh,
   }
 }
 
-// Host launcher; byte strides.  Returns a cudaError_t.
+// Host launcher (programmatic dependent launch); byte strides.  Returns a cudaError_t.
 cudaError_t launch_kv_write(const void* key, int64_t k_st, int64_t k_sh, const void* value,
                             int64_t v_st, int64_t v_sh, void* kc, void* vc, const int64_t* slots,
                             int num_tokens, int kh, int row_bytes, int esize, int block_size,
@@ -81,27 +83,24 @@ cudaError_t launch_kv_write(const void* key, int64_t k_st, int64_t k_sh, const v
   const char* v = static_cast<const char*>(value);
   char* kcc = static_cast<char*>(kc);
   char* vcc = static_cast<char*>(vc);
+  cudaError_t e = vb == 16 ? ensure_kernel_attrs(kv_write_kernel<16>, 0)
+                  : vb == 4 ? ensure_kernel_attrs(kv_write_kernel<4>, 0)
+                            : ensure_kernel_attrs(kv_write_kernel<2>, 0);
+  if (e != cudaSuccess) return e;
   switch (vb) {
     case 16:
-      kv_write_kernel<16><<<(unsigned)blocks, 256, 0, stream>>>(k, k_st, k_sh, v, v_st, v_sh, kcc, vcc,
-                                                                slots, num_tokens, kh, row_bytes,
-                                                                block_size, total_slots, claims,
-                                                                epoch, err);
-      break;
+      return launch_pdl(kv_write_kernel<16>, dim3((unsigned)blocks), dim3(256), 0, stream, k, k_st,
+                        k_sh, v, v_st, v_sh, kcc, vcc, slots, num_tokens, kh, row_bytes, block_size,
+                        total_slots, claims, epoch, err);
     case 4:
-      kv_write_kernel<4><<<(unsigned)blocks, 256, 0, stream>>>(k, k_st, k_sh, v, v_st, v_sh, kcc, vcc,
-                                                               slots, num_tokens, kh, row_bytes,
-                                                               block_size, total_slots, claims,
-                                                               epoch, err);
-      break;
+      return launch_pdl(kv_write_kernel<4>, dim3((unsigned)blocks), dim3(256), 0, stream, k, k_st,
+                        k_sh, v, v_st, v_sh, kcc, vcc, slots, num_tokens, kh, row_bytes, block_size,
+                        total_slots, claims, epoch, err);
     default:
-      kv_write_kernel<2><<<(unsigned)blocks, 256, 0, stream>>>(k, k_st, k_sh, v, v_st, v_sh, kcc, vcc,
-                                                               slots, num_tokens, kh, row_bytes,
-                                                               block_size, total_slots, claims,
-                                                               epoch, err);
-      break;
+      return launch_pdl(kv_write_kernel<2>, dim3((unsigned)blocks), dim3(256), 0, stream, k, k_st,
+                        k_sh, v, v_st, v_sh, kcc, vcc, slots, num_tokens, kh, row_bytes, block_size,
+                        total_slots, claims, epoch, err);
   }
-  return cudaGetLastError();
 }
 
 }  // namespace mvb

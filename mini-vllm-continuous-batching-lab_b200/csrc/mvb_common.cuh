@@ -11,7 +11,10 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
-#include "../../include/mini_vllm_b200.h"
+#include <mutex>
+#include <utility>
+
+#include "mini_vllm_b200.h"  // include/ (the build passes -I include)
 
 namespace mvb {
 
@@ -96,6 +99,18 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Programmatic dependent launch.  A kernel launched with the programmatic
+// stream-serialization attribute may start while the previous kernel in the
+// stream finishes; grid_dependency_wait() blocks until that kernel has
+// completed and its memory is visible (it returns at once for a normal launch).
+// grid_launch_dependents() lets the next such kernel be scheduled early.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
@@ -124,13 +139,23 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity)
   return false;
 }
 
-// 2-D TMA tile load (no multicast) completing on an mbarrier.
+// L2 policy for data read exactly once (KV tiles): evict first, so the
+// stream of K/V does not push small, re-read data (partial states, tables,
+// outputs) out of L2.
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// 2-D TMA tile load (no multicast) completing on an mbarrier, with an L2
+// cache policy.
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
-                                            uint32_t bar) {
+                                            uint32_t bar, uint64_t policy) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar), "l"(policy)
       : "memory");
 }
 
@@ -169,6 +194,10 @@ template <> struct Mma16816<__nv_bfloat16> {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&v);
   }
+  // x rounded to the operand type, as a float
+  static __device__ __forceinline__ float round(float x) {
+    return __bfloat162float(__float2bfloat16_rn(x));
+  }
 };
 
 template <> struct Mma16816<__half> {
@@ -183,6 +212,79 @@ template <> struct Mma16816<__half> {
     __half2 v = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&v);
   }
+  static __device__ __forceinline__ float round(float x) { return __half2float(__float2half_rn(x)); }
 };
+
+// One-time per-device kernel attributes: the dynamic shared memory the launch
+// needs, and the maximum shared-memory carveout.  Every kernel of the library
+// asks for the same (max-shared) L1/shared split, so consecutive launches —
+// KV write, decode, split-K reduction or stream fixup — never make an SM drain
+// to reconfigure its carveout between kernels.
+// Records which (kernel, device) pairs already carry their attributes.
+struct KernelAttrCache {
+  const void* fn[256];
+  int dev[256];
+  int smem[256];
+  int count;
+};
+inline KernelAttrCache& kernel_attr_cache() {
+  static KernelAttrCache c = {};
+  return c;
+}
+inline std::mutex& kernel_attr_mutex() {
+  static std::mutex mu;
+  return mu;
+}
+
+template <typename K>
+cudaError_t ensure_kernel_attrs(K kern, int smem_bytes) {
+  std::lock_guard<std::mutex> lock(kernel_attr_mutex());
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  KernelAttrCache& c = kernel_attr_cache();
+  const void* fn = reinterpret_cast<const void*>(kern);
+  int i = 0;
+  while (i < c.count && !(c.fn[i] == fn && c.dev[i] == dev)) ++i;
+  const bool known = i < c.count;
+  if (known && c.smem[i] >= smem_bytes) return cudaSuccess;
+  if (!known) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             (int)cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return e;
+  }
+  if (smem_bytes > 48 * 1024) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+    if (e != cudaSuccess) return e;
+  }
+  if (!known && c.count < 256) {
+    c.fn[c.count] = fn;
+    c.dev[c.count] = dev;
+    c.smem[c.count] = smem_bytes;
+    ++c.count;
+  } else if (known) {
+    c.smem[i] = smem_bytes;
+  }
+  return cudaSuccess;
+}
+
+// Launch `kern` with the programmatic stream-serialization attribute (the
+// kernel must call grid_dependency_wait() before touching the previous
+// kernel's outputs).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, int smem, cudaStream_t stream,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 }  // namespace mvb

@@ -47,7 +47,7 @@ def assert_close(gpu: torch.Tensor, ref: np.ndarray, dtype: str, msg: str = ""):
 def variants_for(dtype: str, block_size: int, head_dim: int):
     v = ["auto", "fma"]
     if dtype != "f32" and block_size % 16 == 0 and head_dim in (64, 128):
-        v.append("mma")
+        v += ["mma", "stream"]
     return v
 
 
@@ -80,8 +80,10 @@ def test_golden_decodes_all_variants(golden, kind):
     assert ran > 0
 
 
-@pytest.mark.parametrize("variant", ["mma", "fma"])
-@pytest.mark.parametrize("partition_tokens", [None, 16, 48, 512, 1024])
+@pytest.mark.parametrize("variant,partition_tokens", [
+    ("stream", None), ("mma", None), ("mma", 16), ("mma", 48), ("mma", 512), ("mma", 1024),
+    ("fma", None), ("fma", 512),
+])
 def test_config2_full_size_vs_oracle(variant, partition_tokens):
     """BASELINE config 2 (256 seqs, ctx U[128,2048], 14/2/64, bf16) at full size."""
     spec = W.make_spec(2, seed=21)
@@ -97,21 +99,24 @@ def test_config2_full_size_vs_oracle(variant, partition_tokens):
 
 
 def test_config3_long_context_split_k_vs_oracle():
-    """32 x 32768 tokens, flash-decoding 512-token partitions."""
+    """32 x 32768 tokens — flash-decoding 512-token partitions
+    plus the reduction kernel, and the stream kernel."""
     spec = W.make_spec(3, seed=0)
-    plan = M.decode_plan(spec.num_seqs, 14, 2, 64, 16, spec.num_blocks, spec.max_blocks, torch.bfloat16)
+    plan = M.decode_plan(spec.num_seqs, 14, 2, 64, 16, spec.num_blocks, spec.max_blocks, torch.bfloat16,
+                         variant="mma")
     assert plan["num_partitions"] == 64 and plan["partition_tokens"] == 512
     t = W.torch_tensors(spec, torch.bfloat16, DEV)
-    out = M.paged_decode_attention(t["query"], t["key_caches"][0], t["value_caches"][0], t["block_tables"],
-                                   t["kv_len"], spec.block_size)
     ref, st = oracle.decode(torch_to_np(t["query"], "bf16"), torch_to_np(t["key_caches"][0], "bf16"),
                             torch_to_np(t["value_caches"][0], "bf16"), spec.block_tables,
                             spec.context_lens, spec.block_size, "bf16")
     assert (st == 0).all()
-    assert_close(out, ref, "bf16", "config3")
+    for v in ("mma", "stream"):
+        out = M.paged_decode_attention(t["query"], t["key_caches"][0], t["value_caches"][0],
+                                       t["block_tables"], t["kv_len"], spec.block_size, variant=v)
+        assert_close(out, ref, "bf16", f"config3 {v}")
 
 
-@pytest.mark.parametrize("variant", ["mma", "fma"])
+@pytest.mark.parametrize("variant", ["stream", "mma", "fma"])
 def test_config4_gqa4_d128_vs_oracle(variant):
     """BASELINE config 4 shape (32/8/128, lognormal ctx), a 96-sequence shard."""
     spec = W.make_spec(4, seed=2, num_seqs=96)
@@ -161,7 +166,7 @@ def test_gqa_group_sizes(heads):
     ref, _ = oracle.decode(torch_to_np(t["query"], "f16"), torch_to_np(t["key_caches"][0], "f16"),
                            torch_to_np(t["value_caches"][0], "f16"), spec.block_tables, spec.context_lens,
                            16, "f16")
-    for v in ("mma", "fma"):
+    for v in ("stream", "mma", "fma"):
         out = M.paged_decode_attention(t["query"], t["key_caches"][0], t["value_caches"][0],
                                        t["block_tables"], t["kv_len"], 16, variant=v)
         assert_close(out, ref, "f16", f"G={h // kh} {v}")
@@ -206,7 +211,7 @@ def test_nan_garbage_past_context_is_never_used():
         last = int(spec.block_tables[s][(n - 1) // 16])
         kc[last, :, (n % 16 or 16):] = float("nan")
         vc[last, :, (n % 16 or 16):] = float("inf")
-    for v in ("mma", "fma"):
+    for v in ("stream", "mma", "fma"):
         out = M.paged_decode_attention(t["query"], kc, vc, t["block_tables"], t["kv_len"], 16, variant=v)
         assert torch.isfinite(out.float()).all(), v
     ref, _ = oracle.decode(torch_to_np(t["query"], "bf16"), torch_to_np(kc, "bf16"), torch_to_np(vc, "bf16"),
@@ -214,13 +219,32 @@ def test_nan_garbage_past_context_is_never_used():
     assert_close(out, ref, "bf16", "nan garbage")
 
 
-def test_deterministic_bits():
+@pytest.mark.parametrize("variant", ["stream", "mma", "fma"])
+def test_deterministic_bits(variant):
     spec = W.make_spec(2, seed=8, num_seqs=64)
     t = W.torch_tensors(spec, torch.bfloat16, DEV)
     args = (t["query"], t["key_caches"][0], t["value_caches"][0], t["block_tables"], t["kv_len"], 16)
-    a = M.paged_decode_attention(*args)
-    b = M.paged_decode_attention(*args)
-    assert torch.equal(a, b)
+    a = M.paged_decode_attention(*args, variant=variant)
+    for _ in range(3):
+        assert torch.equal(a, M.paged_decode_attention(*args, variant=variant))
+
+
+@pytest.mark.parametrize("num_seqs", [1, 2, 5, 37, 300, 1500, 4000, 64])
+def test_stream_kernel_batch_sizes(num_seqs):
+    """Few sequences (fewer tiles than warps: empty warp ranges), one sequence
+    split across many warps, and large batches (many units per warp)."""
+    ctx = W.context_lengths(2, seed=num_seqs, num_seqs=num_seqs)
+    if num_seqs <= 2:
+        ctx[:] = [3000, 1][:num_seqs]
+    spec = W.build_spec("b", ctx, 14, 2, 64, 16, seed=num_seqs)
+    t = W.torch_tensors(spec, torch.bfloat16, DEV)
+    ref, _ = oracle.decode(torch_to_np(t["query"], "bf16"), torch_to_np(t["key_caches"][0], "bf16"),
+                           torch_to_np(t["value_caches"][0], "bf16"), spec.block_tables, spec.context_lens,
+                           16, "bf16")
+    for _ in range(2):  # the second call reuses the counters the first left at zero
+        out = M.paged_decode_attention(t["query"], t["key_caches"][0], t["value_caches"][0],
+                                       t["block_tables"], t["kv_len"], 16, variant="stream")
+        assert_close(out, ref, "bf16", f"stream n={num_seqs}")
 
 
 # --------------------------------------------------------------------------- errors
@@ -230,7 +254,7 @@ def _small():
     return q, kc, kc.clone()
 
 
-@pytest.mark.parametrize("variant", ["mma", "fma"])
+@pytest.mark.parametrize("variant", ["stream", "mma", "fma"])
 def test_kv_len_zero_raises_value_error(variant):
     q, kc, vc = _small()
     bt = torch.tensor([[0, -1], [1, 2]], device=DEV)
@@ -239,7 +263,7 @@ def test_kv_len_zero_raises_value_error(variant):
         M.triton_decode_attention(q, kc, vc, bt, kvl, 16, variant=variant)
 
 
-@pytest.mark.parametrize("variant", ["mma", "fma"])
+@pytest.mark.parametrize("variant", ["stream", "mma", "fma"])
 def test_table_too_short_raises_index_error(variant):
     q, kc, vc = _small()
     bt = torch.tensor([[0], [1]], device=DEV)
@@ -248,7 +272,7 @@ def test_table_too_short_raises_index_error(variant):
         M.paged_decode_attention(q, kc, vc, bt, kvl, 16, variant=variant)
 
 
-@pytest.mark.parametrize("variant", ["mma", "fma"])
+@pytest.mark.parametrize("variant", ["stream", "mma", "fma"])
 @pytest.mark.parametrize("bad", [-1, 8, 1 << 40])
 def test_bad_block_id_within_context_raises(variant, bad):
     q, kc, vc = _small()
@@ -289,3 +313,17 @@ def test_int64_kv_len_and_cpu_metadata_are_accepted():
     a = M.paged_decode_attention(q, kc, vc, bt, kvl, 16)
     b = M.paged_decode_attention(q, kc, vc, bt.to(DEV), kvl.to(DEV, torch.int32), 16)
     assert torch.equal(a, b)
+
+
+def test_stream_and_split_k_calls_interleave():
+    """Split-K partials and the stream kernel's arrival counters live in separate
+    workspaces: a split call between two stream calls must not disturb them."""
+    spec = W.make_spec(2, seed=30, num_seqs=16)
+    t = W.torch_tensors(spec, torch.bfloat16, DEV)
+    ref, _ = oracle.decode(torch_to_np(t["query"], "bf16"), torch_to_np(t["key_caches"][0], "bf16"),
+                           torch_to_np(t["value_caches"][0], "bf16"), spec.block_tables, spec.context_lens,
+                           16, "bf16")
+    for v, pt in [("stream", None), ("mma", 256), ("stream", None), ("fma", 128), ("stream", None)]:
+        out = M.paged_decode_attention(t["query"], t["key_caches"][0], t["value_caches"][0],
+                                       t["block_tables"], t["kv_len"], 16, variant=v, partition_tokens=pt)
+        assert_close(out, ref, "bf16", f"{v} pt={pt}")

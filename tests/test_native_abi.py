@@ -57,6 +57,7 @@ def test_header_constants_match_binding():
     assert consts["MVB_DEV_TIMEOUT"] == _native.DEV_TIMEOUT
     assert consts["MVB_ERR_VARIANT"] == _native.ERR_VARIANT
     assert consts["MVB_DECODE_MMA"] == _native.DECODE_MMA
+    assert consts["MVB_DECODE_STREAM"] == _native.DECODE_STREAM
 
 
 def _plan(**kw):
@@ -66,13 +67,27 @@ def _plan(**kw):
     return M.decode_plan(**args)
 
 
-def test_plan_headline_config_runs_unsplit_on_tensor_cores():
+def test_plan_headline_config_uses_the_stream_kernel():
     p = _plan()
+    assert p["variant"] == "stream" and p["num_partitions"] == 0
+    # tile prefix + context lengths, then two partial slots (16 rows x (64 + 2) floats) per warp
+    assert p["workspace_bytes"] >= (2 * 256 + 1) * 4 + 2 * 16 * 66 * 4 * 148
+
+
+def test_plan_one_cta_per_sequence_and_kv_head_when_asked():
+    p = _plan(variant="mma")
     assert p == {"variant": "mma", "partition_tokens": 2048, "num_partitions": 1, "workspace_bytes": 0}
 
 
+def test_plan_stream_limits():
+    assert _plan(num_seqs=4096)["variant"] == "stream"
+    assert _plan(num_seqs=4097)["variant"] == "mma"
+    with pytest.raises(RuntimeError, match="variant"):
+        _plan(num_seqs=4097, variant="stream")
+
+
 def test_plan_long_context_uses_split_k():
-    p = _plan(num_seqs=32, max_blocks_per_seq=2048, num_blocks=72090)
+    p = _plan(num_seqs=32, max_blocks_per_seq=2048, num_blocks=72090, variant="mma")
     assert p["variant"] == "mma" and p["partition_tokens"] == 512 and p["num_partitions"] == 64
     n = 32 * 14 * 64
     assert p["workspace_bytes"] >= n * 64 * 4 + 2 * n * 4
@@ -82,11 +97,13 @@ def test_plan_fp32_and_small_blocks_use_fma():
     assert _plan(dtype=torch.float32)["variant"] == "fma"
     assert _plan(block_size=8, max_blocks_per_seq=256)["variant"] == "fma"
     with pytest.raises(RuntimeError, match="variant"):
+        _plan(dtype=torch.float32, variant="stream")
+    with pytest.raises(RuntimeError, match="variant"):
         _plan(dtype=torch.float32, variant="mma")
 
 
 def test_plan_explicit_partition_rounds_to_16():
-    p = _plan(partition_tokens=100)
+    p = _plan(partition_tokens=100, variant="mma")
     assert p["partition_tokens"] == 112 and p["num_partitions"] == 19
 
 
