@@ -144,6 +144,36 @@ int mvb_paged_decode(const void* query, int64_t q_stride_seq, int64_t q_stride_h
                      void* workspace, int64_t workspace_bytes,
                      int32_t* error_flags, void* stream);
 
+/*
+ * Paged decode without a caller workspace.  This entry point has no
+ * counterpart in the reference; it exists for callers that cannot allocate
+ * device memory at decode time — a serving process that gives all free HBM to
+ * the KV pool at start-up and allows no allocation afterwards, or a host
+ * binding (cgo, JNI, a C runtime) with no device allocator of its own.
+ *
+ * Same arguments and results as mvb_paged_decode without `workspace` /
+ * `workspace_bytes`.  It runs the split-K family only (variant MVB_DECODE_AUTO
+ * picks MVB_DECODE_MMA when eligible, else MVB_DECODE_FMA; MVB_DECODE_STREAM
+ * returns MVB_ERR_VARIANT) and keeps the partial states in a 16 MiB device
+ * array inside the library: a shape whose workspace (mvb_paged_decode_plan)
+ * exceeds 16 MiB returns MVB_ERR_WORKSPACE.  It calls no cudaMalloc, cudaFree
+ * or allocating library routine.  Every GPU that loads the library holds the
+ * array until exit; the first call on a device looks up its address
+ * (cudaGetSymbolAddress), so make that first call before any stream capture.
+ * All calls share the one array: calls that overlap on the GPU (different
+ * streams, or devices sharing nothing else) race on it and must be ordered
+ * by the caller.
+ */
+int mvb_paged_decode_noalloc(const void* query, int64_t q_stride_seq, int64_t q_stride_head,
+                             const void* key_cache, const void* value_cache,
+                             const int64_t* block_table, int64_t block_table_stride,
+                             int32_t max_blocks_per_seq, const int32_t* kv_len,
+                             void* out, int64_t out_stride_seq, int64_t out_stride_head,
+                             int32_t num_seqs, int32_t num_heads, int32_t num_kv_heads,
+                             int32_t head_dim, int32_t block_size, int32_t num_blocks,
+                             float scale, int32_t dtype, int32_t variant, int32_t partition_tokens,
+                             int32_t* error_flags, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
