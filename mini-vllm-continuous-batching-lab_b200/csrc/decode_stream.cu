@@ -362,16 +362,23 @@ __global__ void __launch_bounds__(128) decode_stream_fixup_kernel(const DecodeAr
   };
   const int span = w_last - w_first + 1;
 
-  // pass 1: M and L over the contributors (one per lane, chunks of 32 warps)
+  // pass 1: each lane loads (m, l) of one contributor per chunk of 32 warps;
+  // M and L are warp reductions.  Units spanning more than 32 warps (only
+  // tiny-range launches) take further chunks.
   float M = -INFINITY;
+  float2 ml_first = make_float2(-INFINITY, 0.f);  // this lane's contributor in chunk 0
   for (int c0 = 0; c0 < span; c0 += 32) {
     const int w = w_first + c0 + lane;
-    if (c0 + lane < span && has_tiles(w)) M = fmaxf(M, __ldcg(row_of(w)));
+    if (c0 + lane < span && has_tiles(w)) {
+      const float2 ml = __ldcg(reinterpret_cast<const float2*>(row_of(w)));
+      if (c0 == 0) ml_first = ml;
+      M = fmaxf(M, ml.x);
+    }
   }
 #pragma unroll
   for (int sh = 16; sh > 0; sh >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, sh));
-  float L = 0.f;
-  for (int c0 = 0; c0 < span; c0 += 32) {
+  float L = ml_first.y * fast_exp2(ml_first.x - M);
+  for (int c0 = 32; c0 < span; c0 += 32) {
     const int w = w_first + c0 + lane;
     if (c0 + lane < span && has_tiles(w)) {
       const float2 ml = __ldcg(reinterpret_cast<const float2*>(row_of(w)));
@@ -382,14 +389,19 @@ __global__ void __launch_bounds__(128) decode_stream_fixup_kernel(const DecodeAr
   for (int sh = 16; sh > 0; sh >>= 1) L += __shfl_xor_sync(0xffffffffu, L, sh);
   const float inv = 1.f / L;
 
-  // pass 2: columns, contributors broadcast lane by lane
+  // pass 2: columns; contributor c's weight is broadcast from lane c
   float acc[DPL];
 #pragma unroll
   for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
   for (int c0 = 0; c0 < span; c0 += 32) {
-    const int w_mine = w_first + c0 + lane;
-    float coef = 0.f;
-    if (c0 + lane < span && has_tiles(w_mine)) coef = fast_exp2(__ldcg(row_of(w_mine)) - M) * inv;
+    float coef;
+    if (c0 == 0) {
+      coef = fast_exp2(ml_first.x - M) * inv;  // 0 for lanes without a contributor
+    } else {
+      const int w_mine = w_first + c0 + lane;
+      coef = 0.f;
+      if (c0 + lane < span && has_tiles(w_mine)) coef = fast_exp2(__ldcg(row_of(w_mine)) - M) * inv;
+    }
     const int nc = min(32, span - c0);
 #pragma unroll 4
     for (int c = 0; c < nc; ++c) {
