@@ -6,8 +6,10 @@
 One *step* is one pass of the hot path over one batch: the KV write of the
 batch's new tokens (one per sequence) into one layer's pool, then the paged
 decode of every sequence against that layer.  Steps rotate over L layers
-(independent K/V pools, default 4 x 149 MB for config 2), so each step streams
-a pool that is not in the 126 MB L2: "inputs larger than L2".
+(independent K/V pools; default 24, the layer count of the Qwen2-0.5B model
+config 2 is shaped after: 24 x 164 MB), so each step streams a pool that is not
+in the 126 MB L2: "inputs larger than L2".  With N GPUs the outputs are
+all-gathered once per L layers, i.e. once per model decode step.
 
 Workload (default): config 2 — 256 sequences per GPU, context lengths
 U[128, 2048], 14 query / 2 KV heads, head_dim 64, block 16, bf16, seeded
@@ -59,7 +61,7 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=200)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--config", type=int, default=2, choices=[2, 3, 4])
-    p.add_argument("--layers", type=int, default=4)
+    p.add_argument("--layers", type=int, default=24)
     p.add_argument("--variant", default="auto", choices=["auto", "mma", "fma"])
     p.add_argument("--partition-tokens", type=int, default=0)
     p.add_argument("--e2e-steps", type=int, default=400)
@@ -158,10 +160,20 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # CPU side: the oracle port of the reference's CPU path
 # ---------------------------------------------------------------------------
+def host_threads() -> int:
+    """Host cores this process may use (torchrun sets OMP_NUM_THREADS=1 per rank;
+    the CPU baseline asks OpenMP for every core explicitly)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_port_run(spec, tensors_np, steps: int, budget_s: float):
     """Time write + decode of the oracle on the host cores; returns (s/step, threads, reps)."""
     import oracle
 
+    threads = host_threads()
     kc, vc = tensors_np["key_cache"].copy(), tensors_np["value_cache"].copy()
     times = []
     t_end = time.perf_counter() + budget_s
@@ -170,11 +182,11 @@ def cpu_port_run(spec, tensors_np, steps: int, budget_s: float):
         oracle.cache_write(tensors_np["new_key"], tensors_np["new_value"], kc, vc, spec.slot_mapping,
                            spec.block_size, "bf16")
         oracle.decode(tensors_np["query"], kc, vc, spec.block_tables, spec.context_lens, spec.block_size,
-                      "bf16", threads=0)
+                      "bf16", threads=threads)
         times.append(time.perf_counter() - t0)
         if time.perf_counter() > t_end and i >= 2:
             break
-    return statistics.median(times), oracle.max_threads(), len(times)
+    return statistics.median(times), threads, len(times)
 
 
 def reference_arm(args, rank, world):
@@ -226,11 +238,12 @@ def ours(args, rank, world, local_rank):
     bt, kvl, slots = t["block_tables"], t["kv_len"], t["slot_mapping"]
     out = torch.empty_like(q)
     pt = args.partition_tokens or None
-    owned_all = None
+    gather = None
     if world > 1:
         counts = [None] * world
         dist.all_gather_object(counts, owned.tolist())
         owned_all = [np.asarray(c, dtype=np.int64) for c in counts]
+        gather = sharding.OutputGather(owned_all, spec.num_heads, spec.head_dim, torch.bfloat16, dev)
 
     def step(layer):
         M.paged_cache_write(nk, nv, kcs[layer], vcs[layer], slots, spec.block_size, strict=False,
@@ -249,27 +262,29 @@ def ours(args, rank, world, local_rank):
                              partition_tokens=pt)
     torch.cuda.synchronize()
 
-    # ---- CUDA graph of L layer-steps (the gather stays outside the graph) ----
+    # ---- CUDA graph of L layer-steps; with N GPUs it ends with the NCCL
+    # all-gather of the outputs (one model step = L layers, then the gather) ----
     s = torch.cuda.Stream(device=dev)
     s.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.stream(s):
         for layer in range(L):
             step(layer)
+        if gather is not None:
+            gather(out)
     torch.cuda.current_stream(dev).wait_stream(s)
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
         for layer in range(L):
             step(layer)
+        if gather is not None:
+            gather(out)
     replays = max(1, args.steps // L)
     warm = max(1, args.warmup // L)
-    gather_every = world > 1
 
     def run_replays(n):
         for _ in range(n):
             graph.replay()
-            if gather_every:
-                sharding.gather_outputs(out, owned_all, rank)
 
     run_replays(warm)
     torch.cuda.synchronize()
@@ -336,26 +351,35 @@ def ours(args, rank, world, local_rank):
                          dev, torch.bfloat16)
     backend._pool = pool
     backend._block_size = spec.block_size
-    h = {k: v.cpu().pin_memory() for k, v in (("q", q), ("nk", nk), ("nv", nv), ("bt", bt), ("slots", slots))}
-    h["kv_len_after"] = spec.context_lens.copy()
-    h_kvl = torch.from_numpy(h.pop("kv_len_after")).pin_memory()
+    # The step's inputs are staged in ONE pinned host buffer (q, new K/V, slots,
+    # block tables, kv_len, each 256-byte aligned) and copied with one H2D
+    # transfer into typed views of one device buffer; the output comes back
+    # with one D2H copy.
+    parts = [("q", q), ("nk", nk), ("nv", nv), ("slots", slots), ("bt", bt),
+             ("kvl", torch.from_numpy(spec.context_lens.astype(np.int32)).to(dev))]
+    offs, total = {}, 0
+    for name, ten in parts:
+        offs[name] = total
+        total += (ten.numel() * ten.element_size() + 255) // 256 * 256
+    host_buf = torch.empty(total, dtype=torch.uint8).pin_memory()
+    dev_buf = torch.empty(total, dtype=torch.uint8, device=dev)
+    views = {}
+    for name, ten in parts:
+        nbytes = ten.numel() * ten.element_size()
+        host_buf[offs[name]:offs[name] + nbytes].copy_(ten.detach().cpu().contiguous().view(-1).view(torch.uint8))
+        views[name] = dev_buf[offs[name]:offs[name] + nbytes].view(ten.dtype).view(ten.shape)
     out_host = torch.empty(q.shape, dtype=q.dtype).pin_memory()
-    h2d = sum(x.numel() * x.element_size() for x in h.values()) + h_kvl.numel() * h_kvl.element_size()
+    h2d = total
     d2h = out_host.numel() * out_host.element_size()
     meta_group = M.AttentionGroup(seq_indices=list(range(spec.num_seqs)), attention_type="decode_gpu",
-                                  cached_len_before=None, query_len=None, kv_len_after=None)
-    meta = M.AttentionMetadata(groups=[meta_group], block_size=spec.block_size,
+                                  cached_len_before=None, query_len=None, kv_len_after=views["kvl"])
+    meta = M.AttentionMetadata(groups=[meta_group], decode_block_tables=views["bt"], block_size=spec.block_size,
                                num_kv_heads=spec.num_kv_heads, head_dim=spec.head_dim)
 
     def e2e_step(layer):
-        qd = h["q"].to(dev, non_blocking=True)
-        kd = h["nk"].to(dev, non_blocking=True)
-        vd = h["nv"].to(dev, non_blocking=True)
-        sd = h["slots"].to(dev, non_blocking=True)
-        meta.decode_block_tables = h["bt"].to(dev, non_blocking=True)
-        meta_group.kv_len_after = h_kvl.to(dev, non_blocking=True)
-        backend.write_kv_cache(layer, kd, vd, sd)
-        o = backend.decode_attention(layer, qd, meta, pool)
+        dev_buf.copy_(host_buf, non_blocking=True)
+        backend.write_kv_cache(layer, views["nk"], views["nv"], views["slots"])
+        o = backend.decode_attention(layer, views["q"], meta, pool)
         out_host.copy_(o, non_blocking=True)
 
     e2e_n = max(L, args.e2e_steps)
@@ -368,8 +392,8 @@ def ours(args, rank, world, local_rank):
     e0.record()
     for i in range(e2e_n):
         e2e_step(i % L)
-        if world > 1:
-            sharding.gather_outputs(out, owned_all, rank)
+        if gather is not None and i % L == L - 1:
+            gather(out)
     e1.record()
     torch.cuda.synchronize()
     e2e_sec = e0.elapsed_time(e1) / 1e3 / e2e_n
@@ -423,7 +447,7 @@ def ours(args, rank, world, local_rank):
             "clocks": clocks.summary(),
         }
         print(json.dumps(line), flush=True)
-    del graph, dec_graphs
+    del graph, dec_graphs  # release graphs holding NCCL work before the group is destroyed
 
 
 def physical_gpu(local_rank: int) -> str:

@@ -61,9 +61,11 @@ class ArgumentError(AssertionError, ValueError):
     raise, and a ``ValueError`` like the torch oracle raises."""
 
 
-def _require(cond: bool, msg: str) -> None:
+def _require(cond: bool, msg) -> None:
+    """Raise ArgumentError unless `cond`; `msg` is a string or a zero-argument
+    callable producing one (so the hot path formats nothing)."""
     if not cond:
-        raise ArgumentError(msg)
+        raise ArgumentError(msg() if callable(msg) else msg)
 
 
 # ---------------------------------------------------------------------------
@@ -100,7 +102,6 @@ class _DeviceState:
             buf = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
             self._workspaces[key] = buf
         return buf
-
 
 
 _states: Dict[int, _DeviceState] = {}
@@ -212,30 +213,33 @@ def paged_cache_write(
     included, so code that captures this call in a graph passes
     ``check_duplicates=False`` (out-of-range slots are still flagged).
     """
-    _require(key.dim() == 3, f"key must be [num_tokens, num_kv_heads, head_dim], got {tuple(key.shape)}")
-    _require(key.shape == value.shape, f"key {tuple(key.shape)} != value {tuple(value.shape)}")
-    _require(key_cache.dim() == 4, f"key_cache must be 4-D, got {tuple(key_cache.shape)}")
+    _require(key.dim() == 3,
+             lambda: f"key must be [num_tokens, num_kv_heads, head_dim], got {tuple(key.shape)}")
+    _require(key.shape == value.shape, lambda: f"key {tuple(key.shape)} != value {tuple(value.shape)}")
+    _require(key_cache.dim() == 4, lambda: f"key_cache must be 4-D, got {tuple(key_cache.shape)}")
     _require(key_cache.shape == value_cache.shape,
-             f"key_cache shape {tuple(key_cache.shape)} != value_cache shape {tuple(value_cache.shape)}")
+             lambda: f"key_cache shape {tuple(key_cache.shape)} != value_cache shape {tuple(value_cache.shape)}")
     num_tokens, num_kv_heads, head_dim = key.shape
     num_blocks = key_cache.shape[0]
     _require(slot_mapping.dim() == 1 and slot_mapping.shape[0] == num_tokens,
-             f"slot_mapping length {tuple(slot_mapping.shape)} != num_tokens {num_tokens}")
+             lambda: f"slot_mapping length {tuple(slot_mapping.shape)} != num_tokens {num_tokens}")
     _require(num_kv_heads == key_cache.shape[1],
-             f"key num_kv_heads {num_kv_heads} != key_cache num_kv_heads {key_cache.shape[1]}")
+             lambda: f"key num_kv_heads {num_kv_heads} != key_cache num_kv_heads {key_cache.shape[1]}")
     _require(head_dim == key_cache.shape[3],
-             f"key head_dim {head_dim} != key_cache head_dim {key_cache.shape[3]}")
-    _require(block_size > 0, f"block_size must be > 0, got {block_size}")
+             lambda: f"key head_dim {head_dim} != key_cache head_dim {key_cache.shape[3]}")
+    _require(block_size > 0, lambda: f"block_size must be > 0, got {block_size}")
     _require(block_size == key_cache.shape[2],
-             f"block_size {block_size} != cache dim2 {key_cache.shape[2]}")
-    _require(key.dtype == key_cache.dtype, f"key dtype {key.dtype} != cache dtype {key_cache.dtype}")
+             lambda: f"block_size {block_size} != cache dim2 {key_cache.shape[2]}")
+    _require(key.dtype == key_cache.dtype,
+             lambda: f"key dtype {key.dtype} != cache dtype {key_cache.dtype}")
     _require(value.dtype == value_cache.dtype,
-             f"value dtype {value.dtype} != value_cache dtype {value_cache.dtype}")
-    _require(key_cache.dtype in _DTYPE_CODES, f"unsupported cache dtype {key_cache.dtype}")
-    _require(key.device == key_cache.device, f"key device {key.device} != cache device {key_cache.device}")
+             lambda: f"value dtype {value.dtype} != value_cache dtype {value_cache.dtype}")
+    _require(key_cache.dtype in _DTYPE_CODES, lambda: f"unsupported cache dtype {key_cache.dtype}")
+    _require(key.device == key_cache.device,
+             lambda: f"key device {key.device} != cache device {key_cache.device}")
     _require(value.device == value_cache.device,
-             f"value device {value.device} != value_cache device {value_cache.device}")
-    _require(key.device.type == "cuda", f"key.device must be cuda, got {key.device}")
+             lambda: f"value device {value.device} != value_cache device {value_cache.device}")
+    _require(key.device.type == "cuda", lambda: f"key.device must be cuda, got {key.device}")
     _require(key_cache.is_contiguous() and value_cache.is_contiguous(),
              "key_cache and value_cache must be contiguous [num_blocks, num_kv_heads, block_size, head_dim]")
     if num_tokens == 0:
@@ -273,6 +277,22 @@ def paged_cache_write(
 # ---------------------------------------------------------------------------
 # decode
 # ---------------------------------------------------------------------------
+_plan_cache: Dict[tuple, Dict[str, Any]] = {}
+
+
+def _cached_plan(device_index: int, *args) -> Dict[str, Any]:
+    """decode_plan memoised per device and shape (the plan is a pure function of
+    them), so the per-step host path makes one library call, not two."""
+    key = (device_index,) + args
+    plan = _plan_cache.get(key)
+    if plan is None:
+        if len(_plan_cache) > 256:
+            _plan_cache.clear()
+        plan = decode_plan(*args)
+        _plan_cache[key] = plan
+    return plan
+
+
 def decode_plan(
     num_seqs: int,
     num_heads: int,
@@ -331,27 +351,30 @@ def paged_decode_attention(
 
     Returns ``[total_decode, num_q_heads, head_dim]`` in the query's dtype.
     """
-    _require(query.dim() == 3, f"query must be [total_decode, num_heads, head_dim], got {tuple(query.shape)}")
+    _require(query.dim() == 3,
+             lambda: f"query must be [total_decode, num_heads, head_dim], got {tuple(query.shape)}")
     total_decode, num_q_heads, head_dim = query.shape
     _require(key_cache.dim() == 4 and key_cache.shape == value_cache.shape,
-             f"key_cache {tuple(key_cache.shape)} / value_cache {tuple(value_cache.shape)} mismatch")
+             lambda: f"key_cache {tuple(key_cache.shape)} / value_cache {tuple(value_cache.shape)} mismatch")
     num_blocks, num_kv_heads = key_cache.shape[0], key_cache.shape[1]
-    _require(head_dim in (64, 128), f"head_dim {head_dim} not supported (only 64, 128)")
+    _require(head_dim in (64, 128), lambda: f"head_dim {head_dim} not supported (only 64, 128)")
     _require(block_size > 0 and (block_size & (block_size - 1)) == 0,
              f"block_size {block_size} must be a power of 2")
-    _require(key_cache.shape[2] == block_size, f"block_size {block_size} != cache dim2 {key_cache.shape[2]}")
-    _require(key_cache.shape[3] == head_dim, f"cache head_dim {key_cache.shape[3]} != query head_dim {head_dim}")
+    _require(key_cache.shape[2] == block_size,
+             lambda: f"block_size {block_size} != cache dim2 {key_cache.shape[2]}")
+    _require(key_cache.shape[3] == head_dim,
+             lambda: f"cache head_dim {key_cache.shape[3]} != query head_dim {head_dim}")
     _require(num_q_heads % num_kv_heads == 0,
-             f"num_q_heads {num_q_heads} not divisible by num_kv_heads {num_kv_heads}")
-    _require(query.dtype in _DTYPE_CODES, f"query dtype {query.dtype} must be bf16, f16 or f32")
+             lambda: f"num_q_heads {num_q_heads} not divisible by num_kv_heads {num_kv_heads}")
+    _require(query.dtype in _DTYPE_CODES, lambda: f"query dtype {query.dtype} must be bf16, f16 or f32")
     _require(key_cache.dtype == query.dtype and value_cache.dtype == query.dtype,
-             f"cache dtype {key_cache.dtype} != query dtype {query.dtype}")
+             lambda: f"cache dtype {key_cache.dtype} != query dtype {query.dtype}")
     _require(key_cache.is_contiguous() and value_cache.is_contiguous(), "caches must be contiguous")
     _require(block_table.dim() == 2 and block_table.shape[0] == total_decode,
-             f"block_table rows {tuple(block_table.shape)} != total_decode {total_decode}")
+             lambda: f"block_table rows {tuple(block_table.shape)} != total_decode {total_decode}")
     _require(kv_len_after.shape == (total_decode,),
-             f"kv_len_after shape {tuple(kv_len_after.shape)} != ({total_decode},)")
-    _require(query.device.type == "cuda", f"query.device must be cuda, got {query.device}")
+             lambda: f"kv_len_after shape {tuple(kv_len_after.shape)} != ({total_decode},)")
+    _require(query.device.type == "cuda", lambda: f"query.device must be cuda, got {query.device}")
     _require(key_cache.device == query.device and value_cache.device == query.device,
              "query and caches must share one device")
     if scale is None:
@@ -376,8 +399,10 @@ def paged_decode_attention(
 
     state = _state(query.device)
     max_blocks = block_table.shape[1]
-    plan = decode_plan(total_decode, num_q_heads, num_kv_heads, head_dim, block_size, num_blocks,
-                       max_blocks, query.dtype, variant, partition_tokens, key_cache.data_ptr())
+    # the plan only inspects the cache pointer's 16-byte alignment
+    plan = _cached_plan(state.device.index, total_decode, num_q_heads, num_kv_heads, head_dim, block_size,
+                        num_blocks, max_blocks, query.dtype, variant, partition_tokens,
+                        16 if key_cache.data_ptr() % 16 == 0 else 8)
     ws_bytes = plan["workspace_bytes"]
     ws_ptr = state.workspace(ws_bytes, plan["variant"]).data_ptr() if ws_bytes > 0 else None
     status = _native.lib().mvb_paged_decode(

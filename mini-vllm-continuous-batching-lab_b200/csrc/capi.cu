@@ -109,9 +109,9 @@ int make_plan(int num_seqs, int num_heads, int num_kv_heads, int head_dim, int b
   if (v == MVB_DECODE_STREAM && !stream_ok) return MVB_ERR_VARIANT;
 
   if (v == MVB_DECODE_STREAM) {
-    // One contiguous tile range per warp; workspace = the per-sequence tile
-    // prefix and context lengths, then two partial-state slots per warp of the
-    // largest grid the GPU can hold.
+    // One contiguous tile range per warp; workspace = one 32-byte cut-unit
+    // descriptor and two partial-state slots per warp of the largest grid the
+    // GPU can hold.
     const int nw = stream_warps_per_cta(head_dim);
     const int smem = stream_smem_bytes(head_dim, num_seqs);
     int per_sm = smem_per_sm_current() / (smem + 1024);
@@ -125,7 +125,7 @@ int make_plan(int num_seqs, int num_heads, int num_kv_heads, int head_dim, int b
     pl->max_bids = 0;
     pl->max_warps = per_sm * sm_count_current() * nw;
     pl->off_m = pl->off_l = 0;
-    pl->off_part = round_up((int64_t)(2 * num_seqs + 1) * 4, 256);
+    pl->off_part = round_up((int64_t)per_sm * sm_count_current() * nw * 32, 256);
     pl->ws_bytes = pl->off_part + (int64_t)pl->max_warps * 2 * 16 * (head_dim + 2) * 4;
     return MVB_OK;
   }

@@ -31,8 +31,9 @@ namespace mvb {
 constexpr int kStreamRowBatch = 128;  // tiles whose pool rows a warp resolves at once
 
 struct StreamArgs {
-  int* pre_g;     // [num_seqs + 1] tile prefix per sequence (written by CTA 0)
-  int* ctx_g;     // [num_seqs] servable kv_len, 0 for a rejected sequence
+  int4* desc;     // [num_warps][2] the cut unit each warp begins, for the fixup:
+                  // {first tile, end tile, sequence, T_all}, {first head, heads, 0, 0};
+                  // first tile = -1 when the warp begins no cut unit
   float* part;    // [num_warps][2][16][D + 2] partial states (m, l, O[D] per row)
   int num_warps;  // gridDim.x * NW
 };
@@ -110,10 +111,6 @@ decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
     }
     if (tid == 0) pre[Nd] = total;
     __syncthreads();
-    if (blockIdx.x == 0) {
-      for (int i = tid; i <= Nd; i += NT) sa.pre_g[i] = pre[i];
-      for (int i = tid; i < Nd; i += NT) sa.ctx_g[i] = ctxs[i];
-    }
   }
 
   const int T_all = pre[Nd];
@@ -122,7 +119,10 @@ decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
   auto range_start = [&](int w) { return stream_range_start(w, T_all, Wtot); };
   const int r0 = range_start(W), r1 = range_start(W + 1);
   const int n = r1 - r0;
-  if (n <= 0) return;  // no CTA-wide barrier follows
+  if (n <= 0) {  // no CTA-wide barrier follows
+    if (lane == 0) sa.desc[2 * W] = make_int4(-1, 0, 0, 0);
+    return;
+  }
 
   uint64_t* mybars = bars + warp * STAGES;
   int* myok = stage_ok + warp * STAGES;
@@ -316,106 +316,143 @@ decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
     const int issued = min(n, j + STAGES);
     for (int jj = j; jj < issued; ++jj)
       mbar_wait_bounded(smem_u32(mybars + jj % STAGES), (uint32_t)((jj / STAGES) & 1));
+    if (lane == 0) sa.desc[2 * W] = make_int4(-1, 0, 0, 0);
     return;  // the unit's output stays unwritten; the error flag reports it
   }
   flush();
+  // A unit that starts in this range and ends past it was begun here: this
+  // warp is its first contributor, and the fixup finds the unit through it.
+  if (lane == 0) {
+    const bool begins_cut = u_start >= r0 && u_end > r1;
+    sa.desc[2 * W] = begins_cut ? make_int4(u_start, u_end, u_seq, T_all) : make_int4(-1, 0, 0, 0);
+    if (begins_cut) sa.desc[2 * W + 1] = make_int4(h0, nh, 0, 0);
+  }
 }
 
 // ---------------------------------------------------------------------------
 // fixup: merge the partial states of every unit cut by a warp-range boundary
 // ---------------------------------------------------------------------------
-// One warp per (unit, head row) — unit = sequence x KV head x head group.
-// Lane c holds contributor c's (m, l) of the row; M and L come from warp
-// reductions, and each lane accumulates its D/32 columns over the contributors
-// with coefficients broadcast from the owning lane:
-//   out[r][d] = sum_c O_c[r][d] 2^(m_c - M) / L.
-// Contributors are the warps w_first..w_last whose ranges hold tiles of the
-// unit, in warp order, so the result does not depend on timing.
+// One warp per warp w of the stream grid: when w begins a cut unit (its
+// descriptor says which), the warp merges every head row of that unit, RP rows
+// per pass.  Lane c holds contributor c's (m, l) of each row; M and L come
+// from warp reductions, and each lane accumulates its D/32 columns over the
+// contributors with coefficients broadcast from the owning lane:
+//   out[r][d] = sum_c O_c[r][d] 2^(m_c - M_r) / L_r.
+// The O columns of the first CB contributors are requested together with the
+// (m, l) values, so a pass over a unit cut into at most CB pieces costs one L2
+// round trip after the descriptor's.  Contributors are the warps holding tiles
+// of the unit, in warp order, so the result does not depend on timing: warps
+// w..w_last when every warp has tiles (T_all >= warps), else (one tile per
+// non-empty warp) the warps holding tiles us, us + 1, ...
 template <typename T, int D>
 __global__ void __launch_bounds__(128) decode_stream_fixup_kernel(const DecodeArgs a, const StreamArgs sa) {
   constexpr int ROW = D + 2, DPL = D / 32;
-  grid_dependency_wait();  // the streaming kernel's partials and prefix are visible
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int KHG = a.num_kv_heads * a.head_groups;
-  const int rows = min(16, a.G);  // head rows of a full group
-  const int64_t item = (int64_t)blockIdx.x * 4 + warp;
-  const int64_t u = item / rows;
-  const int r = (int)(item - u * rows);
-  if (u >= (int64_t)a.num_seqs * KHG) return;
-  const int s = (int)(u / KHG), k = (int)(u - (int64_t)s * KHG);
-  const int kvh = k / a.head_groups, hg = k - kvh * a.head_groups;
-  if (r >= min(16, a.G - hg * 16)) return;  // the last head group may be short
-  const int ctx = sa.ctx_g[s];
-  if (ctx <= 0) return;
-  const int T_all = sa.pre_g[a.num_seqs], Wtot = sa.num_warps;
-  const int ut = (ctx + kTile - 1) / kTile;
-  const int us = sa.pre_g[s] + k * ut, ue = us + ut;
-  const int w_first = stream_warp_of(us, T_all, Wtot), w_last = stream_warp_of(ue - 1, T_all, Wtot);
-  if (w_first == w_last) return;  // one warp held the whole unit and wrote it
-  const bool dense = T_all >= Wtot;  // then every warp in [w_first, w_last] has tiles of the unit
-  auto has_tiles = [&](int w) {
-    return dense || stream_range_start(w + 1, T_all, Wtot) > stream_range_start(w, T_all, Wtot);
-  };
+  constexpr int RP = D == 64 ? 8 : 4;  // head rows per pass
+  constexpr int CB = 4;                // contributors per batch of O loads (divides 32)
+  grid_dependency_wait();  // the streaming kernel's partials and descriptors are visible
+  const int lane = threadIdx.x & 31;
+  const int w_first = blockIdx.x * 4 + (threadIdx.x >> 5);
+  const int Wtot = sa.num_warps;
+  if (w_first >= Wtot) return;
+  const int4 d0 = __ldcg(sa.desc + 2 * w_first);
+  if (d0.x < 0) return;
+  const int4 d1 = __ldcg(sa.desc + 2 * w_first + 1);
+  const int us = d0.x, ue = d0.y, seq = d0.z, T_all = d0.w, h0 = d1.x, nrows = d1.y;
+  const bool dense = T_all >= Wtot;
+  const int nct = dense ? stream_warp_of(ue - 1, T_all, Wtot) - w_first + 1 : ue - us;
+  auto contributor = [&](int c) { return dense ? w_first + c : stream_warp_of(us + c, T_all, Wtot); };
   // w_first keeps the unit in its "last" slot (1), later contributors in slot 0
-  auto row_of = [&](int w) {
+  auto row_ptr = [&](int w, int r) -> const float* {
     return sa.part + ((int64_t)w * 2 + (w == w_first ? 1 : 0)) * 16 * ROW + r * ROW;
   };
-  const int span = w_last - w_first + 1;
+  T* out = static_cast<T*>(a.out) + (int64_t)seq * a.o_s0;
 
-  // pass 1: each lane loads (m, l) of one contributor per chunk of 32 warps;
-  // M and L are warp reductions.  Units spanning more than 32 warps (only
-  // tiny-range launches) take further chunks.
-  float M = -INFINITY;
-  float2 ml_first = make_float2(-INFINITY, 0.f);  // this lane's contributor in chunk 0
-  for (int c0 = 0; c0 < span; c0 += 32) {
-    const int w = w_first + c0 + lane;
-    if (c0 + lane < span && has_tiles(w)) {
-      const float2 ml = __ldcg(reinterpret_cast<const float2*>(row_of(w)));
-      if (c0 == 0) ml_first = ml;
-      M = fmaxf(M, ml.x);
-    }
-  }
+  for (int rb = 0; rb < nrows; rb += RP) {
+    float x[CB][RP][DPL];  // O columns of contributors c0 .. c0 + CB - 1 (0 past the last)
+    auto load_batch = [&](int c0) {
 #pragma unroll
-  for (int sh = 16; sh > 0; sh >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, sh));
-  float L = ml_first.y * fast_exp2(ml_first.x - M);
-  for (int c0 = 32; c0 < span; c0 += 32) {
-    const int w = w_first + c0 + lane;
-    if (c0 + lane < span && has_tiles(w)) {
-      const float2 ml = __ldcg(reinterpret_cast<const float2*>(row_of(w)));
-      L = fmaf(ml.y, fast_exp2(ml.x - M), L);
-    }
-  }
+      for (int c = 0; c < CB; ++c) {
+        const int w = c0 + c < nct ? contributor(c0 + c) : -1;
 #pragma unroll
-  for (int sh = 16; sh > 0; sh >>= 1) L += __shfl_xor_sync(0xffffffffu, L, sh);
-  const float inv = 1.f / L;
-
-  // pass 2: columns; contributor c's weight is broadcast from lane c
-  float acc[DPL];
+        for (int r = 0; r < RP; ++r)
 #pragma unroll
-  for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
-  for (int c0 = 0; c0 < span; c0 += 32) {
-    float coef;
-    if (c0 == 0) {
-      coef = fast_exp2(ml_first.x - M) * inv;  // 0 for lanes without a contributor
-    } else {
-      const int w_mine = w_first + c0 + lane;
-      coef = 0.f;
-      if (c0 + lane < span && has_tiles(w_mine)) coef = fast_exp2(__ldcg(row_of(w_mine)) - M) * inv;
-    }
-    const int nc = min(32, span - c0);
-#pragma unroll 4
-    for (int c = 0; c < nc; ++c) {
-      const float wt = __shfl_sync(0xffffffffu, coef, c);
-      if (wt != 0.f) {
-        const float* P = row_of(w_first + c0 + c) + 2 + lane;
-#pragma unroll
-        for (int i = 0; i < DPL; ++i) acc[i] = fmaf(__ldcg(P + 32 * i), wt, acc[i]);
+          for (int i = 0; i < DPL; ++i)
+            x[c][r][i] = w >= 0 && rb + r < nrows ? __ldcg(row_ptr(w, rb + r) + 2 + lane + 32 * i) : 0.f;
       }
-    }
-  }
-  T* out = static_cast<T*>(a.out) + (int64_t)s * a.o_s0 + (int64_t)(kvh * a.G + hg * 16 + r) * a.o_s1;
+    };
+    float2 ml[RP];  // (m, l) of contributor c32 + lane
+    bool ok;        // ... which exists
+    auto load_ml = [&](int c32) {
+      const int w = c32 + lane < nct ? contributor(c32 + lane) : -1;
+      ok = w >= 0;
 #pragma unroll
-  for (int i = 0; i < DPL; ++i) out[lane + 32 * i] = from_f32<T>(acc[i]);
+      for (int r = 0; r < RP; ++r)
+        ml[r] = ok && rb + r < nrows ? __ldcg(reinterpret_cast<const float2*>(row_ptr(w, rb + r)))
+                                     : make_float2(-INFINITY, 0.f);
+    };
+    load_batch(0);  // in flight during the (m, l) pass
+    load_ml(0);
+    // M_r = max_c m_c and L_r = sum_c l_c 2^(m_c - M_r), 32 contributors per step
+    float M[RP], L[RP];
+#pragma unroll
+    for (int r = 0; r < RP; ++r) M[r] = -INFINITY, L[r] = 0.f;
+    for (int c32 = 0;;) {
+#pragma unroll
+      for (int r = 0; r < RP; ++r) {
+        float bm = ml[r].x;
+#pragma unroll
+        for (int sh = 16; sh > 0; sh >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, sh));
+        const float nm = fmaxf(M[r], bm);
+        float sum = ok ? ml[r].y * fast_exp2(ml[r].x - nm) : 0.f;
+#pragma unroll
+        for (int sh = 16; sh > 0; sh >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, sh);
+        L[r] = L[r] * fast_exp2(M[r] - nm) + sum;
+        M[r] = nm;
+      }
+      c32 += 32;
+      if (c32 >= nct) break;
+      load_ml(c32);
+    }
+    float inv[RP], cf[RP];  // cf: coefficient of contributor cf_base + lane
+#pragma unroll
+    for (int r = 0; r < RP; ++r) inv[r] = 1.f / L[r];
+    auto coeffs = [&]() {
+#pragma unroll
+      for (int r = 0; r < RP; ++r) cf[r] = ok ? fast_exp2(ml[r].x - M[r]) * inv[r] : 0.f;
+    };
+    if (nct > 32) load_ml(0);  // the pass above left a later group of contributors in ml
+    coeffs();
+    int cf_base = 0;
+    float acc[RP][DPL];
+#pragma unroll
+    for (int r = 0; r < RP; ++r)
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) acc[r][i] = 0.f;
+    for (int c0 = 0;; c0 += CB) {
+      if (c0 - cf_base >= 32) {  // next group of 32 contributors
+        cf_base += 32;
+        load_ml(cf_base);
+        coeffs();
+      }
+#pragma unroll
+      for (int c = 0; c < CB; ++c)
+#pragma unroll
+        for (int r = 0; r < RP; ++r) {
+          const float wt = __shfl_sync(0xffffffffu, cf[r], c0 - cf_base + c);
+#pragma unroll
+          for (int i = 0; i < DPL; ++i) acc[r][i] = fmaf(x[c][r][i], wt, acc[r][i]);
+        }
+      if (c0 + CB >= nct) break;
+      load_batch(c0 + CB);
+    }
+#pragma unroll
+    for (int r = 0; r < RP; ++r)
+      if (rb + r < nrows) {
+        T* po = out + (int64_t)(h0 + rb + r) * a.o_s1;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) po[lane + 32 * i] = from_f32<T>(acc[r][i]);
+      }
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -473,14 +510,12 @@ cudaError_t launch_stream_t(const CUtensorMap& tmk, const CUtensorMap& tmv, cons
   if (ctas * NW > max_warps) ctas = max_warps / NW;
   if (ctas < 1) return cudaErrorInvalidConfiguration;
   StreamArgs sa;
-  sa.pre_g = scratch;
-  sa.ctx_g = scratch + a.num_seqs + 1;
+  sa.desc = reinterpret_cast<int4*>(scratch);
   sa.part = part;
   sa.num_warps = ctas * NW;
   e = launch_pdl(kern, dim3(ctas), dim3(NW * 32), smem, stream, tmk, tmv, a, sa);
   if (e != cudaSuccess) return e;
-  const int64_t items = (int64_t)a.num_seqs * a.num_kv_heads * a.head_groups * (a.G < 16 ? a.G : 16);
-  return launch_pdl(decode_stream_fixup_kernel<T, D>, dim3((unsigned)((items + 3) / 4)), dim3(128), 0,
+  return launch_pdl(decode_stream_fixup_kernel<T, D>, dim3((unsigned)((sa.num_warps + 3) / 4)), dim3(128), 0,
                     stream, a, sa);
 }
 

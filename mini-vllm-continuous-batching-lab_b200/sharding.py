@@ -33,6 +33,41 @@ def snake_assignment(context_lens: np.ndarray, world_size: int) -> List[np.ndarr
     return [np.sort(np.asarray(o, dtype=np.int64)) for o in owners]
 
 
+class OutputGather:
+    """Reusable all-gather of per-rank ``[n_rank, H, D]`` outputs into global order.
+
+    The receive buffer and the per-rank index tensors are built once on the
+    device, so one call is a single ``all_gather_into_tensor`` plus one
+    ``index_copy_`` — no host work, no allocation, capturable in a CUDA graph.
+    """
+
+    def __init__(self, owned: List[np.ndarray], heads: int, head_dim: int, dtype, device, group=None):
+        import torch
+
+        self.world = len(owned)
+        self.counts = [int(o.size) for o in owned]
+        self.cap = max(self.counts) if self.counts else 0
+        self.group = group
+        self.total = sum(self.counts)
+        self.send = torch.zeros((self.cap, heads, head_dim), dtype=dtype, device=device)
+        self.recv = torch.empty((self.world * self.cap, heads, head_dim), dtype=dtype, device=device)
+        self.out = torch.empty((self.total, heads, head_dim), dtype=dtype, device=device)
+        # rows of `recv` that hold real sequences, and their global indices
+        src = np.concatenate([r * self.cap + np.arange(c) for r, c in enumerate(self.counts)])
+        dst = np.concatenate(owned) if owned else np.zeros(0, np.int64)
+        self.src = torch.from_numpy(src.astype(np.int64)).to(device)
+        self.dst = torch.from_numpy(dst.astype(np.int64)).to(device)
+
+    def __call__(self, local_out):
+        import torch.distributed as dist
+
+        n = local_out.shape[0]
+        self.send[:n].copy_(local_out)
+        dist.all_gather_into_tensor(self.recv, self.send, group=self.group)
+        self.out.index_copy_(0, self.dst, self.recv.index_select(0, self.src))
+        return self.out
+
+
 def gather_outputs(local_out, owned: List[np.ndarray], rank: int, group=None):
     """All-gather every rank's ``local_out`` ([n_rank, H, D]) and return the
     ``[B, H, D]`` result in global sequence order (on every rank).

@@ -247,6 +247,23 @@ def test_stream_kernel_batch_sizes(num_seqs):
         assert_close(out, ref, "bf16", f"stream n={num_seqs}")
 
 
+@pytest.mark.parametrize("head_dim,heads,kv_heads", [(64, 14, 2), (128, 32, 8)])
+def test_stream_long_units_many_contributors(head_dim, heads, kv_heads):
+    """More tiles than warps, and units thousands of tiles long: each is cut
+    into hundreds of warp ranges, so the fixup merges more contributors than a
+    warp has lanes, in several groups of 32."""
+    ctx = np.array([40000, 5, 30001, 17], np.int64)
+    spec = W.build_spec("long", ctx, heads, kv_heads, head_dim, 16, seed=41)
+    t = W.torch_tensors(spec, torch.bfloat16, DEV)
+    ref, _ = oracle.decode(torch_to_np(t["query"], "bf16"), torch_to_np(t["key_caches"][0], "bf16"),
+                           torch_to_np(t["value_caches"][0], "bf16"), spec.block_tables, spec.context_lens,
+                           16, "bf16")
+    for _ in range(2):
+        out = M.paged_decode_attention(t["query"], t["key_caches"][0], t["value_caches"][0],
+                                       t["block_tables"], t["kv_len"], 16, variant="stream")
+        assert_close(out, ref, "bf16", f"stream long D={head_dim}")
+
+
 # --------------------------------------------------------------------------- errors
 def _small():
     kc = torch.randn(8, 2, 16, 64, device=DEV).to(torch.bfloat16)

@@ -67,6 +67,11 @@ def _rank_main(rank: int, world: int, port: int, result_path: str):
                                       c["block_size"], "bf16")
         assert (st == 0).all()
         gathered = sharding.gather_outputs(torch.from_numpy(out_local), owned, rank)
+        reusable = sharding.OutputGather(owned, c["num_heads"], c["head_dim"], torch.float32,
+                                         torch.device("cpu"))
+        for _ in range(2):  # the buffers are reused call after call
+            again = reusable(torch.from_numpy(out_local))
+            assert torch.equal(again, gathered)
         if rank == 0:
             np.save(result_path, gathered.numpy())
     finally:
@@ -97,7 +102,7 @@ def _unsharded_reference():
     return out
 
 
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", [2, 3])
 def test_sharded_decode_with_gloo_gather_matches_unsharded(tmp_path, world):
     result = str(tmp_path / "gathered.npy")
     ctx = mp.get_context("spawn")
