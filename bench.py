@@ -25,7 +25,8 @@ Printed (rank 0, one JSON line):
               replayed from a CUDA graph;
   e2e         the same metric through the public backend API with the step's
               inputs copied from pinned host memory each step and the output
-              copied back;
+              copied back (copies on a side stream, double-buffered, so they
+              overlap the neighbouring steps' attention as in a serving loop);
   roofline    the decode kernel alone: algorithmic bytes per launch / mean
               CUDA-event launch duration, against MEASURED_PEAKS.json hbm_gbs;
   cpu_baseline  the CPU oracle (C/OpenMP port of the reference's torch path)
@@ -64,7 +65,7 @@ def parse_args():
     p.add_argument("--layers", type=int, default=24)
     p.add_argument("--variant", default="auto", choices=["auto", "mma", "fma"])
     p.add_argument("--partition-tokens", type=int, default=0)
-    p.add_argument("--e2e-steps", type=int, default=400)
+    p.add_argument("--e2e-steps", type=int, default=2000)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--seed", type=int, default=0)
     return p.parse_args()
@@ -353,8 +354,12 @@ def ours(args, rank, world, local_rank):
     backend._block_size = spec.block_size
     # The step's inputs are staged in ONE pinned host buffer (q, new K/V, slots,
     # block tables, kv_len, each 256-byte aligned) and copied with one H2D
-    # transfer into typed views of one device buffer; the output comes back
-    # with one D2H copy.
+    # transfer into typed views of a device buffer; the output comes back with
+    # one D2H copy.  As in a serving loop, the copies run on a side stream and
+    # overlap the attention of the neighbouring steps: two device input slots
+    # and two pinned output buffers alternate, and events order every reuse.
+    # Per step the side stream gets the H2D of this step (after the step that
+    # last read the slot is done) and the D2H of the previous step's output.
     parts = [("q", q), ("nk", nk), ("nv", nv), ("slots", slots), ("bt", bt),
              ("kvl", torch.from_numpy(spec.context_lens.astype(np.int32)).to(dev))]
     offs, total = {}, 0
@@ -362,39 +367,90 @@ def ours(args, rank, world, local_rank):
         offs[name] = total
         total += (ten.numel() * ten.element_size() + 255) // 256 * 256
     host_buf = torch.empty(total, dtype=torch.uint8).pin_memory()
-    dev_buf = torch.empty(total, dtype=torch.uint8, device=dev)
-    views = {}
     for name, ten in parts:
         nbytes = ten.numel() * ten.element_size()
         host_buf[offs[name]:offs[name] + nbytes].copy_(ten.detach().cpu().contiguous().view(-1).view(torch.uint8))
-        views[name] = dev_buf[offs[name]:offs[name] + nbytes].view(ten.dtype).view(ten.shape)
-    out_host = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    slots_e2e = []
+    for _ in range(2):
+        dev_buf = torch.empty(total, dtype=torch.uint8, device=dev)
+        views = {}
+        for name, ten in parts:
+            nbytes = ten.numel() * ten.element_size()
+            views[name] = dev_buf[offs[name]:offs[name] + nbytes].view(ten.dtype).view(ten.shape)
+        group = M.AttentionGroup(seq_indices=list(range(spec.num_seqs)), attention_type="decode_gpu",
+                                 cached_len_before=None, query_len=None, kv_len_after=views["kvl"])
+        meta = M.AttentionMetadata(groups=[group], decode_block_tables=views["bt"], block_size=spec.block_size,
+                                   num_kv_heads=spec.num_kv_heads, head_dim=spec.head_dim)
+        slots_e2e.append({"buf": dev_buf, "views": views, "meta": meta,
+                          "out_host": torch.empty(q.shape, dtype=q.dtype).pin_memory(),
+                          "in_ready": torch.cuda.Event(), "done": torch.cuda.Event(),
+                          "copied": torch.cuda.Event()})
     h2d = total
-    d2h = out_host.numel() * out_host.element_size()
-    meta_group = M.AttentionGroup(seq_indices=list(range(spec.num_seqs)), attention_type="decode_gpu",
-                                  cached_len_before=None, query_len=None, kv_len_after=views["kvl"])
-    meta = M.AttentionMetadata(groups=[meta_group], decode_block_tables=views["bt"], block_size=spec.block_size,
-                               num_kv_heads=spec.num_kv_heads, head_dim=spec.head_dim)
+    d2h = slots_e2e[0]["out_host"].numel() * slots_e2e[0]["out_host"].element_size()
+    compute = torch.cuda.current_stream(dev)
+    side = torch.cuda.Stream(dev)
+    to_copy = []     # (slot, output) of the previous step: D2H not issued yet
+    to_release = []  # (slot, output) whose D2H is issued: freed once compute waited for it
 
-    def e2e_step(layer):
-        dev_buf.copy_(host_buf, non_blocking=True)
-        backend.write_kv_cache(layer, views["nk"], views["nv"], views["slots"])
-        o = backend.decode_attention(layer, views["q"], meta, pool)
-        out_host.copy_(o, non_blocking=True)
+    def e2e_step(i):
+        sl = slots_e2e[i & 1]
+        v = sl["views"]
+        torch.cuda.set_stream(side)
+        side.wait_event(sl["done"])  # the step that last read this slot has finished
+        sl["buf"].copy_(host_buf, non_blocking=True)
+        sl["in_ready"].record(side)
+        if to_copy:
+            ps, po = to_copy.pop()
+            side.wait_event(ps["done"])
+            ps["out_host"].copy_(po, non_blocking=True)
+            ps["copied"].record(side)
+            to_release.append((ps, po))
+        torch.cuda.set_stream(compute)
+        compute.wait_event(sl["in_ready"])
+        if len(to_release) > 1:
+            # An output is freed only after the compute stream has waited for
+            # its D2H (two steps later, so the wait never stalls): the
+            # allocator's next use of that memory on this stream is ordered
+            # after the copy.
+            rs, ro = to_release.pop(0)
+            compute.wait_event(rs["copied"])
+            del ro
+        layer = i % L
+        backend.write_kv_cache(layer, v["nk"], v["nv"], v["slots"])
+        o = backend.decode_attention(layer, v["q"], sl["meta"], pool)
+        sl["done"].record(compute)
+        to_copy.append((sl, o))
+
+    def e2e_flush():
+        torch.cuda.set_stream(side)
+        while to_copy:
+            ps, po = to_copy.pop()
+            side.wait_event(ps["done"])
+            ps["out_host"].copy_(po, non_blocking=True)
+            ps["copied"].record(side)
+            to_release.append((ps, po))
+        torch.cuda.set_stream(compute)
+        compute.wait_stream(side)
+        to_release.clear()
 
     e2e_n = max(L, args.e2e_steps)
     for i in range(min(10, e2e_n)):
-        e2e_step(i % L)
+        e2e_step(i)
+    e2e_flush()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
+    e0.record(compute)
+    side.wait_stream(compute)
+    h0 = time.perf_counter()
     for i in range(e2e_n):
-        e2e_step(i % L)
+        e2e_step(i)
         if gather is not None and i % L == L - 1:
             gather(out)
-    e1.record()
+    e2e_flush()
+    e1.record(compute)
+    e2e_host_us = (time.perf_counter() - h0) / e2e_n * 1e6  # host time to issue a step
     torch.cuda.synchronize()
     e2e_sec = e0.elapsed_time(e1) / 1e3 / e2e_n
     if world > 1:
@@ -442,6 +498,8 @@ def ours(args, rank, world, local_rank):
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h), "ms_per_step": round(e2e_sec * 1e3, 4),
+                    "copies": "H2D and D2H on a side stream, double-buffered, overlapping compute",
+                    "host_us_per_step": round(e2e_host_us, 1),
                     "decode_tok_s": round(seqs_all / e2e_sec, 1)},
             "gpu_launches": n_steps * launches_per_step,
             "clocks": clocks.summary(),

@@ -105,5 +105,36 @@ def lib() -> ctypes.CDLL:
         return _lib
 
 
+TORCH_BINDING_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "_mvb_torch.so")
+_DEFAULT_LIB_PATH = LIB_PATH
+_fast = None
+
+
+def fast():
+    """The direct binding of the per-step calls (``lib/_mvb_torch.so``), or
+    None when another ``libmvb200.so`` than the in-tree one is selected (the
+    binding is linked against the in-tree library; calls then go through
+    ctypes).  Raises when the binding has not been built."""
+    global _fast
+    if _fast is not None:
+        return _fast
+    if LIB_PATH != _DEFAULT_LIB_PATH:
+        return None
+    lib()  # the library the binding links, loaded and version-checked first
+    with _lock:
+        if _fast is None:
+            if not os.path.exists(TORCH_BINDING_PATH):
+                raise RuntimeError(
+                    f"_mvb_torch.so not found at {TORCH_BINDING_PATH}: build it with __graft_entry__.build()"
+                )
+            import importlib.util
+
+            spec = importlib.util.spec_from_file_location("_mvb_torch", TORCH_BINDING_PATH)
+            mod = importlib.util.module_from_spec(spec)
+            spec.loader.exec_module(mod)
+            _fast = mod
+    return _fast
+
+
 def status_string(status: int) -> str:
     return lib().mvb_status_string(status).decode()

@@ -75,6 +75,7 @@ class _DeviceState:
     def __init__(self, device: torch.device) -> None:
         self.device = device
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        self.err_ptr = self.err.data_ptr()
         self._claims: Dict[int, Tuple[torch.Tensor, int]] = {}
         self._workspaces: Dict[str, torch.Tensor] = {}
 
@@ -108,8 +109,12 @@ _states: Dict[int, _DeviceState] = {}
 _states_lock = threading.Lock()
 
 
-def _state(device: torch.device) -> _DeviceState:
-    idx = device.index if device.index is not None else torch.cuda.current_device()
+def _state(device) -> _DeviceState:
+    """Per-device state; `device` is a torch.device or a CUDA device index."""
+    if isinstance(device, int):
+        idx = device
+    else:
+        idx = device.index if device.index is not None else torch.cuda.current_device()
     st = _states.get(idx)
     if st is None:
         with _states_lock:
@@ -120,8 +125,21 @@ def _state(device: torch.device) -> _DeviceState:
     return st
 
 
-def _stream_handle(device: torch.device) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+try:  # the raw handle without building a torch.cuda.Stream object per call
+    _raw_stream = torch._C._cuda_getCurrentRawStream
+except AttributeError:  # pragma: no cover - older torch
+    _raw_stream = None
+
+
+def _stream_handle(device) -> int:
+    """Current stream of `device` (a torch.device or a CUDA device index)."""
+    if isinstance(device, int):
+        idx = device
+    else:
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+    if _raw_stream is not None:
+        return _raw_stream(idx)
+    return torch.cuda.current_stream(idx).cuda_stream
 
 
 def _host_status(status: int, what: str) -> None:
@@ -189,30 +207,10 @@ def _raise_flags(flags: int, detail: Optional[Dict[str, Any]]) -> None:
 # ---------------------------------------------------------------------------
 # KV write
 # ---------------------------------------------------------------------------
-def paged_cache_write(
-    key: torch.Tensor,
-    value: torch.Tensor,
-    key_cache: torch.Tensor,
-    value_cache: torch.Tensor,
-    slot_mapping: torch.Tensor,
-    block_size: int,
-    *,
-    strict: bool = True,
-    check_duplicates: bool = True,
-) -> None:
-    """Scatter-write per-token K/V into one layer's paged cache (in place).
-
-    Same bytes as ``write_to_paged_cache`` (mini_vllm/cache/cache_write.py:25-74)
-    for every input without duplicate slots; the checks mirror
-    ``triton_cache_write`` (paged_attention_gpu.py:109-135).  ``value`` may be
-    a strided view (e.g. of a fused QKV output): its strides are passed to the
-    kernel instead of making it contiguous.
-
-    ``check_duplicates`` stamps every slot with a per-call epoch to detect two
-    tokens writing one slot.  A CUDA graph replays its launch arguments, epoch
-    included, so code that captures this call in a graph passes
-    ``check_duplicates=False`` (out-of-range slots are still flagged).
-    """
+def _diagnose_write(key, value, key_cache, value_cache, slot_mapping, block_size) -> None:
+    """Raise the error of the first failed check of ``paged_cache_write``, in
+    the order the checks are documented (the call's fast path tests them all
+    at once)."""
     _require(key.dim() == 3,
              lambda: f"key must be [num_tokens, num_kv_heads, head_dim], got {tuple(key.shape)}")
     _require(key.shape == value.shape, lambda: f"key {tuple(key.shape)} != value {tuple(value.shape)}")
@@ -240,18 +238,74 @@ def paged_cache_write(
     _require(value.device == value_cache.device,
              lambda: f"value device {value.device} != value_cache device {value_cache.device}")
     _require(key.device.type == "cuda", lambda: f"key.device must be cuda, got {key.device}")
+    _require(value_cache.device == key_cache.device,
+             lambda: f"value_cache device {value_cache.device} != key_cache device {key_cache.device}")
     _require(key_cache.is_contiguous() and value_cache.is_contiguous(),
              "key_cache and value_cache must be contiguous [num_blocks, num_kv_heads, block_size, head_dim]")
+    raise ArgumentError("invalid paged_cache_write arguments")
+
+
+def paged_cache_write(
+    key: torch.Tensor,
+    value: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    slot_mapping: torch.Tensor,
+    block_size: int,
+    *,
+    strict: bool = True,
+    check_duplicates: bool = True,
+) -> None:
+    """Scatter-write per-token K/V into one layer's paged cache (in place).
+
+    Same bytes as ``write_to_paged_cache`` (mini_vllm/cache/cache_write.py:25-74)
+    for every input without duplicate slots; the checks mirror
+    ``triton_cache_write`` (paged_attention_gpu.py:109-135).  ``value`` may be
+    a strided view (e.g. of a fused QKV output): its strides are passed to the
+    kernel instead of making it contiguous.
+
+    ``check_duplicates`` stamps every slot with a per-call epoch to detect two
+    tokens writing one slot.  A CUDA graph replays its launch arguments, epoch
+    included, so code that captures this call in a graph passes
+    ``check_duplicates=False`` (out-of-range slots are still flagged).
+    """
+    if key.is_cuda:  # direct binding: the common case in one C++ call
+        state = _state(key.get_device())
+        status = _native.fast().kv_write(key, value, key_cache, value_cache, slot_mapping, block_size,
+                                         check_duplicates, state.err_ptr)
+        if status == _native.OK:
+            if strict:
+                flags = _take_flags(state)
+                if flags:
+                    _raise_flags(flags, {"slot_mapping": slot_mapping,
+                                         "total_slots": key_cache.shape[0] * block_size,
+                                         "block_size": block_size, "num_blocks": key_cache.shape[0]})
+            return
+        # anything else (a conversion to make, an argument to reject, a failed
+        # call to report) takes the full path below
+    if not (key.dim() == 3 and key.shape == value.shape and key_cache.dim() == 4
+            and key_cache.shape == value_cache.shape and slot_mapping.dim() == 1
+            and slot_mapping.shape[0] == key.shape[0] and key.shape[1] == key_cache.shape[1]
+            and key.shape[2] == key_cache.shape[3] and block_size > 0 and block_size == key_cache.shape[2]
+            and key.dtype == key_cache.dtype and value.dtype == value_cache.dtype
+            and key_cache.dtype in _DTYPE_CODES and key.is_cuda
+            and key.get_device() == key_cache.get_device() and value.get_device() == value_cache.get_device()
+            and value_cache.get_device() == key_cache.get_device()
+            and key_cache.is_contiguous() and value_cache.is_contiguous()):
+        _diagnose_write(key, value, key_cache, value_cache, slot_mapping, block_size)
+    num_tokens, num_kv_heads, head_dim = key.shape
+    num_blocks = key_cache.shape[0]
     if num_tokens == 0:
         return
     if key.stride(2) != 1:
         key = key.contiguous()
     if value.stride(2) != 1:
         value = value.contiguous()
-    if slot_mapping.dtype != torch.int64 or slot_mapping.device != key.device or not slot_mapping.is_contiguous():
+    if slot_mapping.dtype != torch.int64 or slot_mapping.get_device() != key.get_device() or not slot_mapping.is_contiguous():
         slot_mapping = slot_mapping.to(device=key.device, dtype=torch.int64).contiguous()
 
-    state = _state(key.device)
+    dev_idx = key.get_device()
+    state = _state(dev_idx)
     total_slots = num_blocks * block_size
     if check_duplicates:
         claims, epoch = state.next_claims(total_slots)
@@ -264,7 +318,7 @@ def paged_cache_write(
         key_cache.data_ptr(), value_cache.data_ptr(),
         slot_mapping.data_ptr(), num_tokens, num_kv_heads, head_dim, block_size, num_blocks,
         _DTYPE_CODES[key_cache.dtype], claims_ptr, epoch,
-        state.err.data_ptr(), _stream_handle(key.device),
+        state.err.data_ptr(), _stream_handle(dev_idx),
     )
     _host_status(status, "kv cache write")
     if strict:
@@ -277,6 +331,38 @@ def paged_cache_write(
 # ---------------------------------------------------------------------------
 # decode
 # ---------------------------------------------------------------------------
+def _diagnose_decode(query, key_cache, value_cache, block_table, kv_len_after, block_size) -> None:
+    """Raise the error of the first failed check of ``paged_decode_attention``,
+    in the documented order (the call's fast path tests them all at once)."""
+    _require(query.dim() == 3,
+             lambda: f"query must be [total_decode, num_heads, head_dim], got {tuple(query.shape)}")
+    total_decode, num_q_heads, head_dim = query.shape
+    _require(key_cache.dim() == 4 and key_cache.shape == value_cache.shape,
+             lambda: f"key_cache {tuple(key_cache.shape)} / value_cache {tuple(value_cache.shape)} mismatch")
+    num_blocks, num_kv_heads = key_cache.shape[0], key_cache.shape[1]
+    _require(head_dim in (64, 128), lambda: f"head_dim {head_dim} not supported (only 64, 128)")
+    _require(block_size > 0 and (block_size & (block_size - 1)) == 0,
+             f"block_size {block_size} must be a power of 2")
+    _require(key_cache.shape[2] == block_size,
+             lambda: f"block_size {block_size} != cache dim2 {key_cache.shape[2]}")
+    _require(key_cache.shape[3] == head_dim,
+             lambda: f"cache head_dim {key_cache.shape[3]} != query head_dim {head_dim}")
+    _require(num_q_heads % num_kv_heads == 0,
+             lambda: f"num_q_heads {num_q_heads} not divisible by num_kv_heads {num_kv_heads}")
+    _require(query.dtype in _DTYPE_CODES, lambda: f"query dtype {query.dtype} must be bf16, f16 or f32")
+    _require(key_cache.dtype == query.dtype and value_cache.dtype == query.dtype,
+             lambda: f"cache dtype {key_cache.dtype} != query dtype {query.dtype}")
+    _require(key_cache.is_contiguous() and value_cache.is_contiguous(), "caches must be contiguous")
+    _require(block_table.dim() == 2 and block_table.shape[0] == total_decode,
+             lambda: f"block_table rows {tuple(block_table.shape)} != total_decode {total_decode}")
+    _require(kv_len_after.shape == (total_decode,),
+             lambda: f"kv_len_after shape {tuple(kv_len_after.shape)} != ({total_decode},)")
+    _require(query.device.type == "cuda", lambda: f"query.device must be cuda, got {query.device}")
+    _require(key_cache.device == query.device and value_cache.device == query.device,
+             "query and caches must share one device")
+    raise ArgumentError("invalid paged_decode_attention arguments")
+
+
 _plan_cache: Dict[tuple, Dict[str, Any]] = {}
 
 
@@ -351,39 +437,38 @@ def paged_decode_attention(
 
     Returns ``[total_decode, num_q_heads, head_dim]`` in the query's dtype.
     """
-    _require(query.dim() == 3,
-             lambda: f"query must be [total_decode, num_heads, head_dim], got {tuple(query.shape)}")
+    if query.is_cuda:  # direct binding: the common case in one C++ call
+        state = _state(query.get_device())
+        status, res = _native.fast().decode(query, key_cache, value_cache, block_table, kv_len_after, block_size,
+                                            -1.0 if scale is None else float(scale), out, _VARIANTS.get(variant, -1),
+                                            int(partition_tokens or 0), state.err_ptr)
+        if status == _native.OK:
+            if strict:
+                flags = _take_flags(state)
+                if flags:
+                    _raise_flags(flags, {"kv_len_after": kv_len_after, "max_blocks": block_table.shape[1],
+                                         "block_size": block_size, "num_blocks": key_cache.shape[0]})
+            return res
+        # anything else takes the full path below
+    if not (query.dim() == 3 and key_cache.dim() == 4 and key_cache.shape == value_cache.shape
+            and query.shape[2] in (64, 128) and block_size > 0 and (block_size & (block_size - 1)) == 0
+            and key_cache.shape[2] == block_size and key_cache.shape[3] == query.shape[2]
+            and key_cache.shape[1] > 0 and query.shape[1] % key_cache.shape[1] == 0
+            and query.dtype in _DTYPE_CODES and key_cache.dtype == query.dtype
+            and value_cache.dtype == query.dtype and key_cache.is_contiguous() and value_cache.is_contiguous()
+            and block_table.dim() == 2 and block_table.shape[0] == query.shape[0]
+            and kv_len_after.shape == (query.shape[0],) and query.is_cuda
+            and key_cache.get_device() == query.get_device() and value_cache.get_device() == query.get_device()):
+        _diagnose_decode(query, key_cache, value_cache, block_table, kv_len_after, block_size)
     total_decode, num_q_heads, head_dim = query.shape
-    _require(key_cache.dim() == 4 and key_cache.shape == value_cache.shape,
-             lambda: f"key_cache {tuple(key_cache.shape)} / value_cache {tuple(value_cache.shape)} mismatch")
     num_blocks, num_kv_heads = key_cache.shape[0], key_cache.shape[1]
-    _require(head_dim in (64, 128), lambda: f"head_dim {head_dim} not supported (only 64, 128)")
-    _require(block_size > 0 and (block_size & (block_size - 1)) == 0,
-             f"block_size {block_size} must be a power of 2")
-    _require(key_cache.shape[2] == block_size,
-             lambda: f"block_size {block_size} != cache dim2 {key_cache.shape[2]}")
-    _require(key_cache.shape[3] == head_dim,
-             lambda: f"cache head_dim {key_cache.shape[3]} != query head_dim {head_dim}")
-    _require(num_q_heads % num_kv_heads == 0,
-             lambda: f"num_q_heads {num_q_heads} not divisible by num_kv_heads {num_kv_heads}")
-    _require(query.dtype in _DTYPE_CODES, lambda: f"query dtype {query.dtype} must be bf16, f16 or f32")
-    _require(key_cache.dtype == query.dtype and value_cache.dtype == query.dtype,
-             lambda: f"cache dtype {key_cache.dtype} != query dtype {query.dtype}")
-    _require(key_cache.is_contiguous() and value_cache.is_contiguous(), "caches must be contiguous")
-    _require(block_table.dim() == 2 and block_table.shape[0] == total_decode,
-             lambda: f"block_table rows {tuple(block_table.shape)} != total_decode {total_decode}")
-    _require(kv_len_after.shape == (total_decode,),
-             lambda: f"kv_len_after shape {tuple(kv_len_after.shape)} != ({total_decode},)")
-    _require(query.device.type == "cuda", lambda: f"query.device must be cuda, got {query.device}")
-    _require(key_cache.device == query.device and value_cache.device == query.device,
-             "query and caches must share one device")
     if scale is None:
         scale = head_dim ** -0.5
 
     if out is None:
         out = torch.empty((total_decode, num_q_heads, head_dim), dtype=query.dtype, device=query.device)
     else:
-        _require(out.shape == query.shape and out.dtype == query.dtype and out.device == query.device,
+        _require(out.shape == query.shape and out.dtype == query.dtype and out.get_device() == query.get_device(),
                  "out must match query's shape, dtype and device")
         _require(out.stride(2) == 1, "out's last dimension must be contiguous")
     if total_decode == 0:
@@ -392,15 +477,16 @@ def paged_decode_attention(
     if query.stride(2) != 1 or query.data_ptr() % 16 or (query.stride(0) * query.element_size()) % 16 \
             or (query.stride(1) * query.element_size()) % 16:
         query = query.contiguous()
-    if block_table.dtype != torch.int64 or block_table.device != query.device or block_table.stride(1) != 1:
+    if block_table.dtype != torch.int64 or block_table.get_device() != query.get_device() or block_table.stride(1) != 1:
         block_table = block_table.to(device=query.device, dtype=torch.int64).contiguous()
-    if kv_len_after.dtype != torch.int32 or kv_len_after.device != query.device or not kv_len_after.is_contiguous():
+    if kv_len_after.dtype != torch.int32 or kv_len_after.get_device() != query.get_device() or not kv_len_after.is_contiguous():
         kv_len_after = kv_len_after.to(device=query.device, dtype=torch.int32).contiguous()
 
-    state = _state(query.device)
+    dev_idx = query.get_device()
+    state = _state(dev_idx)
     max_blocks = block_table.shape[1]
     # the plan only inspects the cache pointer's 16-byte alignment
-    plan = _cached_plan(state.device.index, total_decode, num_q_heads, num_kv_heads, head_dim, block_size,
+    plan = _cached_plan(dev_idx, total_decode, num_q_heads, num_kv_heads, head_dim, block_size,
                         num_blocks, max_blocks, query.dtype, variant, partition_tokens,
                         16 if key_cache.data_ptr() % 16 == 0 else 8)
     ws_bytes = plan["workspace_bytes"]
@@ -413,7 +499,7 @@ def paged_decode_attention(
         out.data_ptr(), out.stride(0), out.stride(1),
         total_decode, num_q_heads, num_kv_heads, head_dim, block_size, num_blocks,
         float(scale), _DTYPE_CODES[query.dtype], _VARIANTS[variant], int(partition_tokens or 0),
-        ws_ptr, ws_bytes, state.err.data_ptr(), _stream_handle(query.device),
+        ws_ptr, ws_bytes, state.err.data_ptr(), _stream_handle(dev_idx),
     )
     _host_status(status, "paged decode")
     if strict:

@@ -78,12 +78,48 @@ def build_native(force: bool = False, verbose: bool = False) -> str:
         objs = list(ex.map(lambda s: _compile(s, verbose, force), SOURCES))
     newest = max(os.path.getmtime(o) for o in objs)
     if force or not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < newest:
-        cmd = [nvcc_path(), *ARCH_FLAGS, "-shared", "-o", LIB_PATH, *objs, "-lrt", "-ldl", "-lpthread"]
+        cmd = [nvcc_path(), *ARCH_FLAGS, "-shared", "-Xlinker", "-soname=libmvb200.so", "-o", LIB_PATH, *objs,
+               "-lrt", "-ldl", "-lpthread"]
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             raise RuntimeError(f"link of libmvb200.so failed:\n{res.stdout}\n{res.stderr}")
     return LIB_PATH
 
 
+TORCH_BINDING_SRC = os.path.join(CSRC, "torch_binding.cpp")
+TORCH_BINDING_PATH = os.path.join(LIB_DIR, "_mvb_torch.so")
+
+
+def build_torch_binding(force: bool = False) -> str:
+    """Compile the direct Python binding of the per-step calls (g++ against
+    torch's headers; links ``libmvb200.so`` from the same directory)."""
+    import sysconfig
+
+    import torch
+    from torch.utils import cpp_extension
+
+    lib = build_native(force=force)
+    deps = [TORCH_BINDING_SRC, os.path.join(INCLUDE, "mini_vllm_b200.h"), lib]
+    if (not force and os.path.exists(TORCH_BINDING_PATH)
+            and os.path.getmtime(TORCH_BINDING_PATH) >= max(os.path.getmtime(d) for d in deps)):
+        return TORCH_BINDING_PATH
+    torch_lib = cpp_extension.library_paths()[0]
+    cuda_home = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    cmd = ["g++", "-O2", "-std=c++17", "-shared", "-fPIC", "-w",
+           "-DTORCH_EXTENSION_NAME=_mvb_torch", "-DTORCH_API_INCLUDE_EXTENSION_H",
+           f"-D_GLIBCXX_USE_CXX11_ABI={int(torch._C._GLIBCXX_USE_CXX11_ABI)}"]
+    for inc in cpp_extension.include_paths() + [os.path.join(cuda_home, "include"),
+                                               sysconfig.get_paths()["include"], INCLUDE]:
+        cmd += ["-I", inc]
+    cmd += [TORCH_BINDING_SRC, "-o", TORCH_BINDING_PATH,
+            "-L", torch_lib, "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-ltorch_python",
+            "-L", LIB_DIR, "-lmvb200", "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{torch_lib}"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"g++ failed for torch_binding.cpp:\n{res.stdout}\n{res.stderr}")
+    return TORCH_BINDING_PATH
+
+
 if __name__ == "__main__":
     print(build_native(force="--force" in sys.argv, verbose="--verbose" in sys.argv))
+    print(build_torch_binding(force="--force" in sys.argv))

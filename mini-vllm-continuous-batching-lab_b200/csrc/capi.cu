@@ -60,12 +60,16 @@ int sm_count_current() {
 }
 
 int smem_per_sm_current() {
-  int dev = 0, v = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess ||
-      cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess ||
-      v <= 0)
-    return kDefaultSmemPerSm;
-  return v;
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return kDefaultSmemPerSm;
+  if (cache[dev] == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess || v <= 0)
+      v = kDefaultSmemPerSm;
+    cache[dev] = v;
+  }
+  return cache[dev];
 }
 
 struct Plan {

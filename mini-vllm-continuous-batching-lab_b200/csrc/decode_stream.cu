@@ -502,10 +502,28 @@ cudaError_t launch_stream_t(const CUtensorMap& tmk, const CUtensorMap& tmv, cons
   if (e != cudaSuccess) return e;
   e = ensure_kernel_attrs(decode_stream_fixup_kernel<T, D>, 0);
   if (e != cudaSuccess) return e;
-  int per_sm = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, NW * 32, smem);
+  // Resident CTAs per SM, queried once per (device, shared-memory size): the
+  // query costs microseconds of host time, and this runs once per layer-step.
+  static std::mutex occ_mu;
+  static int occ_dev[16], occ_smem[16], occ_val[16], occ_n = 0;
+  int dev = 0;
+  e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  if (per_sm < 1) per_sm = 1;
+  int per_sm = 0;
+  {
+    std::lock_guard<std::mutex> lock(occ_mu);
+    for (int i = 0; i < occ_n; ++i)
+      if (occ_dev[i] == dev && occ_smem[i] == smem) per_sm = occ_val[i];
+    if (per_sm == 0) {
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, NW * 32, smem);
+      if (e != cudaSuccess) return e;
+      if (per_sm < 1) per_sm = 1;
+      const int slot = occ_n < 16 ? occ_n++ : (dev + smem) & 15;
+      occ_dev[slot] = dev;
+      occ_smem[slot] = smem;
+      occ_val[slot] = per_sm;
+    }
+  }
   int ctas = per_sm * sm_count;
   if (ctas * NW > max_warps) ctas = max_warps / NW;
   if (ctas < 1) return cudaErrorInvalidConfiguration;

@@ -33,6 +33,7 @@ def _built_libraries():
     import oracle
 
     build.build_native()
+    build.build_torch_binding()
     oracle.build_oracle()
     yield
 

@@ -344,3 +344,35 @@ def test_stream_and_split_k_calls_interleave():
         out = M.paged_decode_attention(t["query"], t["key_caches"][0], t["value_caches"][0],
                                        t["block_tables"], t["kv_len"], 16, variant=v, partition_tokens=pt)
         assert_close(out, ref, "bf16", f"{v} pt={pt}")
+
+
+def test_direct_binding_and_ctypes_route_agree(monkeypatch):
+    """The C++ binding (the common case) and the ctypes route (taken when the
+    binding declines) launch the same kernels: identical bytes for the write
+    and the decode, and the binding is what ran first."""
+    from mini_vllm_b200 import _native
+
+    spec = W.make_spec(2, seed=5, num_seqs=64)
+    t = W.torch_tensors(spec, torch.bfloat16, DEV)
+    kc_a, vc_a = t["key_caches"][0].clone(), t["value_caches"][0].clone()
+    M.paged_cache_write(t["new_key"], t["new_value"], kc_a, vc_a, t["slot_mapping"], 16)
+    a = M.paged_decode_attention(t["query"], kc_a, vc_a, t["block_tables"], t["kv_len"], 16)
+    assert _native._fast is not None
+
+    class Declines:
+        SLOW_PATH = -1000
+
+        @staticmethod
+        def kv_write(*args):
+            return Declines.SLOW_PATH
+
+        @staticmethod
+        def decode(*args):
+            return Declines.SLOW_PATH, None
+
+    monkeypatch.setattr(_native, "fast", lambda: Declines)
+    kc_b, vc_b = t["key_caches"][0].clone(), t["value_caches"][0].clone()
+    M.paged_cache_write(t["new_key"], t["new_value"], kc_b, vc_b, t["slot_mapping"], 16)
+    b = M.paged_decode_attention(t["query"], kc_b, vc_b, t["block_tables"], t["kv_len"], 16)
+    assert torch.equal(kc_a, kc_b) and torch.equal(vc_a, vc_b)
+    assert torch.equal(a, b)

@@ -144,3 +144,18 @@ def test_decode_host_checks_without_gpu():
     assert call(1, head_dim=80) == _native.ERR_HEAD_DIM
     assert call(1, block_size=12) == _native.ERR_BLOCK_SIZE
     assert call(1, nh=7, nkv=2) == _native.ERR_HEADS
+
+
+def test_direct_binding_loads_and_routes_cpu_tensors_to_the_full_path():
+    """The C++ binding of the per-step calls loads without a GPU and declines
+    (SLOW_PATH) anything but CUDA tensors, leaving the Python wrapper's checks
+    to raise the documented errors."""
+    fast = _native.fast()
+    assert fast.SLOW_PATH == -1000
+    k = torch.zeros(2, 2, 64, dtype=torch.bfloat16)
+    kc = torch.zeros(4, 2, 16, 64, dtype=torch.bfloat16)
+    assert fast.kv_write(k, k, kc, kc, torch.zeros(2, dtype=torch.int64), 16, True, 0) == fast.SLOW_PATH
+    q = torch.zeros(2, 4, 64, dtype=torch.bfloat16)
+    st, out = fast.decode(q, kc, kc, torch.zeros(2, 1, dtype=torch.int64), torch.ones(2, dtype=torch.int32), 16,
+                          -1.0, None, _native.DECODE_AUTO, 0, 0)
+    assert st == fast.SLOW_PATH and out is None
