@@ -269,9 +269,10 @@ def paged_cache_write(
     included, so code that captures this call in a graph passes
     ``check_duplicates=False`` (out-of-range slots are still flagged).
     """
-    if key.is_cuda:  # direct binding: the common case in one C++ call
+    fast = _native.fast()
+    if fast is not None and key.is_cuda:  # direct binding: the common case in one C++ call
         state = _state(key.get_device())
-        status = _native.fast().kv_write(key, value, key_cache, value_cache, slot_mapping, block_size,
+        status = fast.kv_write(key, value, key_cache, value_cache, slot_mapping, block_size,
                                          check_duplicates, state.err_ptr)
         if status == _native.OK:
             if strict:
@@ -437,9 +438,10 @@ def paged_decode_attention(
 
     Returns ``[total_decode, num_q_heads, head_dim]`` in the query's dtype.
     """
-    if query.is_cuda:  # direct binding: the common case in one C++ call
+    fast = _native.fast()
+    if fast is not None and query.is_cuda:  # direct binding: the common case in one C++ call
         state = _state(query.get_device())
-        status, res = _native.fast().decode(query, key_cache, value_cache, block_table, kv_len_after, block_size,
+        status, res = fast.decode(query, key_cache, value_cache, block_table, kv_len_after, block_size,
                                             -1.0 if scale is None else float(scale), out, _VARIANTS.get(variant, -1),
                                             int(partition_tokens or 0), state.err_ptr)
         if status == _native.OK:
