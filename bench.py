@@ -250,7 +250,7 @@ def ours(args, rank, world, local_rank):
         M.paged_cache_write(nk, nv, kcs[layer], vcs[layer], slots, spec.block_size, strict=False,
                             check_duplicates=False)
         M.paged_decode_attention(q, kcs[layer], vcs[layer], bt, kvl, spec.block_size, out=out,
-                                 variant=args.variant, partition_tokens=pt, strict=False)
+                                 variant=args.variant, partition_tokens=pt, strict=False, after_write=True)
 
     plan = M.decode_plan(spec.num_seqs, spec.num_heads, spec.num_kv_heads, spec.head_dim, spec.block_size,
                          spec.num_blocks, spec.max_blocks, torch.bfloat16, args.variant, pt,
@@ -347,7 +347,7 @@ def ours(args, rank, world, local_rank):
     # ---- e2e: public API, host buffers in, output back to host ----
     backend = M.AttentionBackendB200(M.ModelConfig(num_heads=spec.num_heads, num_kv_heads=spec.num_kv_heads,
                                                    head_dim=spec.head_dim), strict=False,
-                                     decode_variant=args.variant, partition_tokens=pt)
+                                     decode_variant=args.variant, partition_tokens=pt, overlap_after_write=True)
     pool = M.KVCachePool(kcs, vcs, spec.num_blocks, spec.block_size, L, spec.num_kv_heads, spec.head_dim,
                          dev, torch.bfloat16)
     backend._pool = pool

@@ -67,6 +67,17 @@ extern "C" {
                               ranges per warp + a fixup kernel merging cut units
                               (num_seqs <= 4096) */
 
+/* Flag ORed into `variant` of mvb_paged_decode (ignored by the plan): the
+ * kernel launched immediately before this call on `stream` is
+ * mvb_kv_cache_write (or a kernel that signals its dependents only when it
+ * finishes).  The stream kernel then reads query, block_table and kv_len and
+ * resolves its first tiles BEFORE waiting for that kernel, overlapping its
+ * set-up with the write; only the cache reads wait.  Without the flag every
+ * input is read after the wait.  A preceding kernel that signals its
+ * dependents early and still writes query, block_table or kv_len afterwards
+ * must not be followed by a call with this flag. */
+#define MVB_DECODE_AFTER_WRITE 0x100
+
 /* ABI version; bumped whenever a signature below changes. */
 int mvb_abi_version(void);
 

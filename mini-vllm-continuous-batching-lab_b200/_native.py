@@ -44,6 +44,8 @@ DECODE_AUTO = 0
 DECODE_FMA = 1
 DECODE_MMA = 2
 DECODE_STREAM = 3
+# flag ORed into the decode variant (MVB_DECODE_AFTER_WRITE)
+DECODE_AFTER_WRITE = 0x100
 
 ABI_VERSION = 1
 

@@ -421,6 +421,7 @@ def paged_decode_attention(
     variant: str = "auto",
     partition_tokens: Optional[int] = None,
     strict: bool = True,
+    after_write: bool = False,
 ) -> torch.Tensor:
     """Paged decode attention (one query token per sequence) on the B200 kernels.
 
@@ -434,7 +435,11 @@ def paged_decode_attention(
     Keyword-only extensions: ``out`` (write in place), ``variant``
     (``"auto" | "stream" | "mma" | "fma"``), ``partition_tokens`` (split-K
     partition length of the ``"mma"`` / ``"fma"`` kernels; ``None`` lets the
-    library choose), ``strict``.
+    library choose), ``strict``, ``after_write`` (the kernel launched just
+    before this call on the current stream is ``paged_cache_write``: the stream
+    kernel then reads query, block table and kv_len while the write is still
+    running and waits only before its cache loads; leave it False when any
+    other kernel may run in between and signal its dependents early).
 
     Returns ``[total_decode, num_q_heads, head_dim]`` in the query's dtype.
     """
@@ -442,7 +447,8 @@ def paged_decode_attention(
     if fast is not None and query.is_cuda:  # direct binding: the common case in one C++ call
         state = _state(query.get_device())
         status, res = fast.decode(query, key_cache, value_cache, block_table, kv_len_after, block_size,
-                                            -1.0 if scale is None else float(scale), out, _VARIANTS.get(variant, -1),
+                                            -1.0 if scale is None else float(scale), out,
+                                            _VARIANTS.get(variant, -1) | (_native.DECODE_AFTER_WRITE if after_write else 0),
                                             int(partition_tokens or 0), state.err_ptr)
         if status == _native.OK:
             if strict:
@@ -500,7 +506,8 @@ def paged_decode_attention(
         kv_len_after.data_ptr(),
         out.data_ptr(), out.stride(0), out.stride(1),
         total_decode, num_q_heads, num_kv_heads, head_dim, block_size, num_blocks,
-        float(scale), _DTYPE_CODES[query.dtype], _VARIANTS[variant], int(partition_tokens or 0),
+        float(scale), _DTYPE_CODES[query.dtype],
+        _VARIANTS[variant] | (_native.DECODE_AFTER_WRITE if after_write else 0), int(partition_tokens or 0),
         ws_ptr, ws_bytes, state.err.data_ptr(), _stream_handle(dev_idx),
     )
     _host_status(status, "paged decode")
@@ -532,7 +539,7 @@ class AttentionBackendB200(AttentionBackend):
     """
 
     def __init__(self, config: Any, *, strict: bool = True, decode_variant: str = "auto",
-                 partition_tokens: Optional[int] = None) -> None:
+                 partition_tokens: Optional[int] = None, overlap_after_write: bool = False) -> None:
         hd = getattr(config, "head_dim", 0)
         if hd not in (64, 128):
             raise RuntimeError(
@@ -549,6 +556,13 @@ class AttentionBackendB200(AttentionBackend):
         self.strict = strict
         self.decode_variant = decode_variant
         self.partition_tokens = partition_tokens
+        # With overlap_after_write, a decode that directly follows this
+        # backend's KV write of the same layer on the same stream starts its
+        # set-up while the write runs (``after_write``).  The caller promises
+        # that nothing launched between the two calls signals its dependents
+        # early and writes the decode's inputs (plain torch kernels do not).
+        self.overlap_after_write = overlap_after_write
+        self._last_write: Optional[Tuple[int, int]] = None
 
     def allocate_pool(self, num_layers: int, num_blocks: int, block_size: int, num_kv_heads: int,
                       head_dim: int, dtype: torch.dtype, device: torch.device) -> KVCachePool:
@@ -563,21 +577,26 @@ class AttentionBackendB200(AttentionBackend):
                        slot_mapping: torch.Tensor) -> None:
         pool = self._pool
         assert pool is not None, "allocate_pool must be called first"
+        self._last_write = None
         paged_cache_write(key, value, pool.key_caches[layer_idx], pool.value_caches[layer_idx],
                           slot_mapping, pool.block_size, strict=self.strict)
+        if self.overlap_after_write and key.shape[0] > 0:
+            self._last_write = (layer_idx, _stream_handle(key.get_device()))
 
     def decode_attention(self, layer_idx: int, query: torch.Tensor, attn_metadata: Any,
                          pool: Any) -> torch.Tensor:
+        last, self._last_write = self._last_write, None  # only the very next decode may overlap
         if query.shape[0] == 0:
             return query
         group = next((g for g in attn_metadata.groups if g.attention_type == "decode_gpu"), None)
         if group is None:
             return query
+        after = last is not None and query.is_cuda and last == (layer_idx, _stream_handle(query.get_device()))
         return paged_decode_attention(
             query, pool.key_caches[layer_idx], pool.value_caches[layer_idx],
             attn_metadata.decode_block_tables, group.kv_len_after, pool.block_size,
             variant=self.decode_variant, partition_tokens=self.partition_tokens,
-            strict=self.strict,
+            strict=self.strict, after_write=after,
         )
 
     def prefill_attention(self, layer_idx: int, query: torch.Tensor, key: torch.Tensor,

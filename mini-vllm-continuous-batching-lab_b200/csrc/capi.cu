@@ -303,6 +303,7 @@ int mvb_paged_decode_plan(int32_t num_seqs, int32_t num_heads, int32_t num_kv_he
                           int32_t* partition_tokens_out, int32_t* num_partitions_out,
                           int64_t* workspace_bytes_out) {
   Plan pl;
+  variant &= ~MVB_DECODE_AFTER_WRITE;  // a launch-ordering hint: no effect on the plan
   const int st = make_plan(num_seqs, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
                            max_blocks_per_seq, dtype, variant, partition_tokens, cache_ptr, &pl);
   if (st != MVB_OK) return st;
@@ -323,6 +324,8 @@ int mvb_paged_decode(const void* query, int64_t q_stride_seq, int64_t q_stride_h
                      int32_t partition_tokens, void* workspace, int64_t workspace_bytes,
                      int32_t* error_flags, void* stream) {
   Plan pl;
+  const bool after_write = (variant & MVB_DECODE_AFTER_WRITE) != 0;
+  variant &= ~MVB_DECODE_AFTER_WRITE;
   const int st = make_plan(num_seqs, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
                            max_blocks_per_seq, dtype, variant, partition_tokens, key_cache, &pl);
   if (st != MVB_OK) return st;
@@ -373,6 +376,7 @@ int mvb_paged_decode(const void* query, int64_t q_stride_seq, int64_t q_stride_h
   a.part_m = pl.num_parts > 1 ? reinterpret_cast<float*>(ws + pl.off_m) : nullptr;
   a.part_l = pl.num_parts > 1 ? reinterpret_cast<float*>(ws + pl.off_l) : nullptr;
   a.err = error_flags;
+  a.early_inputs = after_write ? 1 : 0;  // honoured by the stream kernel
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e;

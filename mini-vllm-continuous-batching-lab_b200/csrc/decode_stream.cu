@@ -69,7 +69,11 @@ decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
   const int Nd = a.num_seqs;
   const int KHG = a.num_kv_heads * a.head_groups;
 
-  grid_dependency_wait();      // inputs of the previous kernel in the stream are visible
+  // Without early_inputs any input may come from the previous kernel in the
+  // stream: wait for it first.  With it (the previous kernel is the KV write,
+  // which writes only the cache) the set-up below reads query, block table and
+  // kv_len at once, and only the first cache load waits.
+  if (!a.early_inputs) grid_dependency_wait();
   grid_launch_dependents();    // the fixup kernel may be scheduled as CTAs retire
 
   // ---- prologue: tiles per sequence (all its units) and their exclusive prefix ----
@@ -197,10 +201,6 @@ decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
   };
 
   fill_rows(0);
-  if (lane == 0) {
-    const int n0 = n < STAGES ? n : STAGES;
-    for (int j = 0; j < n0; ++j) issue(j);
-  }
 
   const int g0 = lane >> 2, qd = lane & 3;
   uint32_t qa[KC][4], qa_next[KC][4];
@@ -264,6 +264,11 @@ decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
   };
 
   prefetch_next(r0);  // the range's first unit (it may start before r0: locate handles it)
+  if (a.early_inputs) grid_dependency_wait();  // the cache is complete from here on
+  if (lane == 0) {
+    const int n0 = n < STAGES ? n : STAGES;
+    for (int j = 0; j < n0; ++j) issue(j);
+  }
   bool failed = false;
   int j = 0;
   for (; j < n; ++j) {

@@ -46,6 +46,7 @@ struct DecodeArgs {
   float* part_m;     // [num_seqs][num_heads][num_parts] running max (log2 units)
   float* part_l;     // [num_seqs][num_heads][num_parts] sum of exp2(x - m)
   int* err;
+  int early_inputs;  // read query / block table / kv_len before the grid-dependency wait
 };
 
 // ---------------------------------------------------------------------------

@@ -376,3 +376,66 @@ def test_direct_binding_and_ctypes_route_agree(monkeypatch):
     b = M.paged_decode_attention(t["query"], kc_b, vc_b, t["block_tables"], t["kv_len"], 16)
     assert torch.equal(kc_a, kc_b) and torch.equal(vc_a, vc_b)
     assert torch.equal(a, b)
+
+
+def _write_then_decode_case(seed: int, num_seqs: int):
+    """Config-2 shapes whose new tokens dominate attention: K = 4, V = 3 at
+    every new slot, so a decode that read the cache before the write landed
+    would be far outside tolerance, not just a few ulps off."""
+    spec = W.make_spec(2, seed=seed, num_seqs=num_seqs)
+    t = W.torch_tensors(spec, torch.bfloat16, DEV)
+    t["new_key"].fill_(4.0)
+    t["new_value"].fill_(3.0)
+    kc, vc = torch_to_np(t["key_caches"][0], "bf16"), torch_to_np(t["value_caches"][0], "bf16")
+    oracle.cache_write(torch_to_np(t["new_key"], "bf16"), torch_to_np(t["new_value"], "bf16"), kc, vc,
+                       spec.slot_mapping, 16, "bf16")
+    ref, st = oracle.decode(torch_to_np(t["query"], "bf16"), kc, vc, spec.block_tables, spec.context_lens, 16,
+                            "bf16")
+    assert (st == 0).all()
+    return spec, t, ref
+
+
+@pytest.mark.parametrize("num_seqs", [256, 7])
+def test_decode_after_write_overlap_sees_the_write(num_seqs):
+    """after_write=True (set-up overlapped with the preceding KV write, no host
+    sync in between) gives the oracle's write-then-decode result, bit-identical
+    to the ordered launch."""
+    spec, t, ref = _write_then_decode_case(31, num_seqs)
+    outs = {}
+    for flag in (False, True, True):
+        kc, vc = t["key_caches"][0].clone(), t["value_caches"][0].clone()
+        torch.cuda.synchronize()
+        M.paged_cache_write(t["new_key"], t["new_value"], kc, vc, t["slot_mapping"], 16, strict=False)
+        o = M.paged_decode_attention(t["query"], kc, vc, t["block_tables"], t["kv_len"], 16, strict=False,
+                                     after_write=flag)
+        M.check_device_errors()
+        assert_close(o, ref, "bf16", f"after_write={flag}")
+        if flag in outs:
+            assert torch.equal(o, outs[flag])
+        outs[flag] = o
+    assert torch.equal(outs[False], outs[True])
+
+
+def test_backend_overlap_after_write_only_for_the_adjacent_decode():
+    """The backend passes after_write only to the decode that directly follows
+    its own write of the same layer; results match the oracle either way."""
+    spec, t, ref = _write_then_decode_case(32, 64)
+    backend = M.AttentionBackendB200(M.ModelConfig(num_heads=14, num_kv_heads=2, head_dim=64), strict=False,
+                                     overlap_after_write=True)
+    kcs = [t["key_caches"][0].clone(), t["key_caches"][0].clone()]
+    vcs = [t["value_caches"][0].clone(), t["value_caches"][0].clone()]
+    pool = M.KVCachePool(kcs, vcs, spec.num_blocks, 16, 2, 2, 64, torch.device(DEV), torch.bfloat16)
+    backend._pool = pool
+    group = M.AttentionGroup(seq_indices=list(range(spec.num_seqs)), attention_type="decode_gpu",
+                             cached_len_before=None, query_len=None, kv_len_after=t["kv_len"])
+    meta = M.AttentionMetadata(groups=[group], decode_block_tables=t["block_tables"], block_size=16,
+                               num_kv_heads=2, head_dim=64)
+    backend.write_kv_cache(0, t["new_key"], t["new_value"], t["slot_mapping"])
+    assert backend._last_write is not None
+    a = backend.decode_attention(0, t["query"], meta, pool)
+    assert backend._last_write is None
+    backend.write_kv_cache(1, t["new_key"], t["new_value"], t["slot_mapping"])
+    b = backend.decode_attention(0, t["query"], meta, pool)  # another layer's write: no overlap
+    M.check_device_errors()
+    assert_close(a, ref, "bf16", "adjacent")
+    assert torch.equal(a, b)

@@ -50,7 +50,7 @@ def test_abi_version_and_status_strings():
 
 def test_header_constants_match_binding():
     text = open(HEADER).read()
-    consts = dict((k, int(v)) for k, v in re.findall(r"#define\s+(MVB_\w+)\s+(-?\d+)", text))
+    consts = dict((k, int(v, 0)) for k, v in re.findall(r"#define\s+(MVB_\w+)\s+(-?(?:0x[0-9a-fA-F]+|\d+))", text))
     assert consts["MVB_DTYPE_BF16"] == _native.DTYPE_BF16
     assert consts["MVB_DTYPE_F16"] == _native.DTYPE_F16
     assert consts["MVB_DEV_DUP_SLOT"] == _native.DEV_DUP_SLOT
@@ -58,6 +58,7 @@ def test_header_constants_match_binding():
     assert consts["MVB_ERR_VARIANT"] == _native.ERR_VARIANT
     assert consts["MVB_DECODE_MMA"] == _native.DECODE_MMA
     assert consts["MVB_DECODE_STREAM"] == _native.DECODE_STREAM
+    assert consts["MVB_DECODE_AFTER_WRITE"] == _native.DECODE_AFTER_WRITE
 
 
 def _plan(**kw):
