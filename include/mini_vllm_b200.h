@@ -67,6 +67,29 @@ extern "C" {
                               ranges per warp + a fixup kernel merging cut units
                               (num_seqs <= 4096) */
 
+/* Logical -> physical gather of cached K/V for a batch of sequences (the
+ * prefill path's prefix read) into contiguous [total_tokens, KH, D] outputs:
+ *   key_out[out_offsets[i] + p] = key_cache[block_table[seq_rows[i]][p / BS], :, p % BS, :]
+ * for p < out_offsets[i + 1] - out_offsets[i] (same for value_out).
+ * Replaces gather_prefix_kv / _gather_prefix_kv_kernel
+ * (mini_vllm/attention/paged_attention_gpu.py:329-433) and batches
+ * gather_paged_kv (mini_vllm/cache/cache_read.py:19-84).
+ * block_table: int64 [block_table_rows, >= max_blocks_per_seq], row stride
+ * block_table_stride; seq_rows: int64 [num_seqs] rows of it; out_offsets:
+ * int64 [num_seqs + 1], an exclusive prefix of the token counts
+ * (out_offsets[num_seqs] == total_tokens), all device memory.  Rows must be
+ * 16-byte multiples (head_dim * element size) and every pointer 16-byte aligned.
+ * Device errors (the row is zero-filled): a logical block past
+ * max_blocks_per_seq -> MVB_DEV_TABLE_SHORT; a block id outside
+ * [0, num_blocks) or a sequence row outside the table -> MVB_DEV_BLOCK_ID;
+ * offsets that are not an increasing prefix from 0 -> MVB_DEV_KV_LEN. */
+int mvb_paged_gather(const void* key_cache, const void* value_cache, const int64_t* block_table,
+                     int64_t block_table_rows, int64_t block_table_stride, int32_t max_blocks_per_seq,
+                     const int64_t* seq_rows, const int64_t* out_offsets, void* key_out, void* value_out,
+                     int32_t num_seqs, int64_t total_tokens, int32_t num_kv_heads, int32_t head_dim,
+                     int32_t block_size, int32_t num_blocks, int32_t dtype, int32_t* error_flags,
+                     void* stream);
+
 /* Flag ORed into `variant` of mvb_paged_decode (ignored by the plan): the
  * kernel launched immediately before this call on `stream` is
  * mvb_kv_cache_write (or a kernel that signals its dependents only when it

@@ -13,8 +13,11 @@ from .attention import (
     AttentionBackendB200,
     check_device_errors,
     decode_plan,
+    gather_paged_kv,
+    gather_prefix_kv,
     paged_cache_write,
     paged_decode_attention,
+    paged_gather,
     triton_cache_write,
     triton_decode_attention,
 )
@@ -34,8 +37,11 @@ __all__ = [
     "check_device_errors",
     "compute_num_gpu_blocks",
     "decode_plan",
+    "gather_paged_kv",
+    "gather_prefix_kv",
     "paged_cache_write",
     "paged_decode_attention",
+    "paged_gather",
     "triton_cache_write",
     "triton_decode_attention",
 ]

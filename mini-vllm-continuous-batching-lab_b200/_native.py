@@ -70,6 +70,11 @@ SIGNATURES = {
         [_vp, _i64, _i64, _vp, _vp, _vp, _i64, _i32, _vp, _vp, _i64, _i64,
          _i32, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _i32, _i32, _vp, _i64, _vp, _vp],
     ),
+    "mvb_paged_gather": (
+        _i32,
+        [_vp, _vp, _vp, _i64, _i64, _i32, _vp, _vp, _vp, _vp, _i32, _i64, _i32, _i32, _i32, _i32, _i32,
+         _vp, _vp],
+    ),
     "mvb_paged_decode_noalloc": (
         _i32,
         [_vp, _i64, _i64, _vp, _vp, _vp, _i64, _i32, _vp, _vp, _i64, _i64,

@@ -4,8 +4,11 @@ from .paged_attention_b200 import (
     AttentionBackendB200,
     check_device_errors,
     decode_plan,
+    gather_paged_kv,
+    gather_prefix_kv,
     paged_cache_write,
     paged_decode_attention,
+    paged_gather,
     triton_cache_write,
     triton_decode_attention,
     validate_block_size,
@@ -17,8 +20,11 @@ __all__ = [
     "AttentionBackendB200",
     "check_device_errors",
     "decode_plan",
+    "gather_paged_kv",
+    "gather_prefix_kv",
     "paged_cache_write",
     "paged_decode_attention",
+    "paged_gather",
     "triton_cache_write",
     "triton_decode_attention",
     "validate_block_size",

@@ -38,7 +38,7 @@ raises; with ``strict=False`` the word accumulates until
 from __future__ import annotations
 
 import threading
-from typing import Any, Dict, Optional, Tuple
+from typing import Any, Dict, List, Optional, Tuple
 
 import torch
 
@@ -519,6 +519,127 @@ def paged_decode_attention(
     return out
 
 
+# ---------------------------------------------------------------------------
+# gather (prefill prefix read)
+# ---------------------------------------------------------------------------
+def _host_ints(values) -> List[int]:
+    if isinstance(values, torch.Tensor):
+        return [int(v) for v in values.reshape(-1).tolist()]
+    return [int(v) for v in values]
+
+
+def paged_gather(
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    block_table: torch.Tensor,
+    seq_rows,
+    num_tokens,
+    block_size: int,
+    *,
+    strict: bool = True,
+) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Logical -> physical gather of the first ``num_tokens[i]`` cached tokens
+    of each sequence ``block_table[seq_rows[i]]`` into contiguous
+    ``[sum(num_tokens), num_kv_heads, head_dim]`` K and V, sequences one after
+    another (``mvb_paged_gather``, one launch for the batch).
+
+    The batched form of ``gather_paged_kv`` (mini_vllm/cache/cache_read.py:19-84).
+    A table too short for a sequence's tokens raises ``IndexError`` as there;
+    a ``-1`` or out-of-range block id inside them raises ``IndexError`` too.
+    """
+    _require(key_cache.dim() == 4 and key_cache.shape == value_cache.shape,
+             lambda: f"key_cache {tuple(key_cache.shape)} / value_cache {tuple(value_cache.shape)} mismatch")
+    _require(key_cache.dtype == value_cache.dtype and key_cache.dtype in _DTYPE_CODES,
+             lambda: f"cache dtypes {key_cache.dtype} / {value_cache.dtype} must match and be bf16, f16 or f32")
+    _require(key_cache.is_contiguous() and value_cache.is_contiguous(), "caches must be contiguous")
+    _require(key_cache.is_cuda and value_cache.get_device() == key_cache.get_device(),
+             "key_cache and value_cache must be on one CUDA device")
+    num_blocks, num_kv_heads, bs, head_dim = key_cache.shape
+    _require(block_size == bs, lambda: f"block_size {block_size} != cache dim2 {bs}")
+    _require((head_dim * key_cache.element_size()) % 16 == 0,
+             lambda: f"head_dim {head_dim} rows must be a multiple of 16 bytes")
+    rows, counts = _host_ints(seq_rows), _host_ints(num_tokens)
+    _require(len(rows) == len(counts), lambda: f"{len(rows)} sequences but {len(counts)} token counts")
+    if any(n < 0 for n in counts):
+        raise ValueError(f"token counts must be >= 0, got {counts}")
+    _require(block_table.dim() == 2, lambda: f"block_table must be 2-D, got {tuple(block_table.shape)}")
+    n_rows, max_blocks = block_table.shape
+    for r in rows:
+        if not 0 <= r < n_rows:
+            raise IndexError(f"sequence index {r} out of range for a block table of {n_rows} rows")
+    total = sum(counts)
+    dev = key_cache.device
+    out_k = torch.empty((total, num_kv_heads, head_dim), dtype=key_cache.dtype, device=dev)
+    out_v = torch.empty((total, num_kv_heads, head_dim), dtype=key_cache.dtype, device=dev)
+    if total == 0:
+        return out_k, out_v
+    for n in counts:
+        if n > max_blocks * block_size:
+            raise IndexError(
+                f"block_table length {max_blocks} insufficient to cover {n} tokens (block_size={block_size})"
+            )
+    if block_table.dtype != torch.int64 or block_table.get_device() != key_cache.get_device() \
+            or block_table.stride(1) != 1:
+        block_table = block_table.to(device=dev, dtype=torch.int64).contiguous()
+    offsets = [0]
+    for n in counts:
+        offsets.append(offsets[-1] + n)
+    meta = torch.tensor(rows + offsets, dtype=torch.int64).to(dev)  # one small copy: rows, then offsets
+    dev_idx = key_cache.get_device()
+    state = _state(dev_idx)
+    status = _native.lib().mvb_paged_gather(
+        key_cache.data_ptr(), value_cache.data_ptr(), block_table.data_ptr(), n_rows, block_table.stride(0),
+        max_blocks, meta.data_ptr(), meta.data_ptr() + 8 * len(rows), out_k.data_ptr(), out_v.data_ptr(),
+        len(rows), total, num_kv_heads, head_dim, block_size, num_blocks, _DTYPE_CODES[key_cache.dtype],
+        state.err_ptr, _stream_handle(dev_idx),
+    )
+    _host_status(status, "paged gather")
+    if strict:
+        flags = _take_flags(state)
+        if flags:
+            _raise_flags(flags, {"max_blocks": max_blocks, "block_size": block_size, "num_blocks": num_blocks})
+    return out_k, out_v
+
+
+def gather_prefix_kv(
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    block_table: torch.Tensor,
+    cached_len_before,
+    seq_indices,
+    block_size: int,
+    *,
+    strict: bool = True,
+) -> Tuple[torch.Tensor, torch.Tensor]:
+    """The cached prefixes of the prefill sequences, concatenated:
+    ``[sum(cached_len_before), num_kv_heads, head_dim]`` K and V.
+
+    Same signature and result as the Triton ``gather_prefix_kv``
+    (paged_attention_gpu.py:391-433), with no host loop over tokens; rows of
+    ``block_table`` are the global sequence indices ``seq_indices``."""
+    return paged_gather(key_cache, value_cache, block_table, seq_indices, cached_len_before, block_size,
+                        strict=strict)
+
+
+def gather_paged_kv(
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    block_table,
+    num_tokens: int,
+    block_size: int,
+) -> Tuple[torch.Tensor, torch.Tensor]:
+    """``gather_paged_kv`` (mini_vllm/cache/cache_read.py:19-84) on the GPU: the
+    first ``num_tokens`` tokens of one sequence whose physical blocks are
+    ``block_table`` (a list of ids in logical order)."""
+    ids = _host_ints(block_table)
+    if num_tokens > len(ids) * block_size:
+        raise IndexError(
+            f"block_table length {len(ids)} insufficient to cover {num_tokens} tokens (block_size={block_size})"
+        )
+    table = torch.tensor([ids or [0]], dtype=torch.int64)
+    return paged_gather(key_cache, value_cache, table, [0], [int(num_tokens)], block_size)
+
+
 # Reference names, for code that imports them from the Triton module.
 triton_cache_write = paged_cache_write
 triton_decode_attention = paged_decode_attention
@@ -599,35 +720,49 @@ class AttentionBackendB200(AttentionBackend):
             strict=self.strict, after_write=after,
         )
 
-    def prefill_attention(self, layer_idx: int, query: torch.Tensor, key: torch.Tensor,
-                          value: torch.Tensor, attn_metadata: Any, pool: Any) -> torch.Tensor:
+    def prefill_attention(self, layer_idx: int, query: torch.Tensor, key: Optional[torch.Tensor],
+                          value: Optional[torch.Tensor], attn_metadata: Any, pool: Any) -> torch.Tensor:
+        """Causal prefill attention over each sequence's cached prefix and its new
+        chunk (mirror of AttentionBackendGPU.prefill_attention,
+        paged_attention_gpu.py:577-661).
+
+        The cache is read by one ``paged_gather`` launch per group.  With the
+        chunk's ``key`` / ``value`` given, the gather reads the cached prefix and
+        the chunk is appended, as the Triton backend does; with ``None``, the
+        whole context is read from the cache (the new tokens are written before
+        attention), as AttentionBackendRef does (paged_attention_ref.py:166-240).
+        The attention itself is torch SDPA with the offset causal mask.
+        """
         if query.shape[0] == 0:
             return query
         num_heads, head_dim = query.shape[1], query.shape[2]
         reps = num_heads // pool.num_kv_heads
         scale = head_dim ** -0.5
         kc, vc = pool.key_caches[layer_idx], pool.value_caches[layer_idx]
-        bs = pool.block_size
+        with_chunk = key is not None and value is not None
         parts = []
         offset = 0
         for group in attn_metadata.groups:
             if group.attention_type not in ("prefill_gpu", "prefill_ref"):
                 continue
-            for i, seq_idx in enumerate(group.seq_indices):
-                cached = int(group.cached_len_before[i])
-                q_len = int(group.query_len[i])
-                kv_len = cached + q_len
-                row = attn_metadata.prefill_block_tables[int(seq_idx)].to(kc.device)
-                pos = torch.arange(kv_len, device=kc.device)
-                blk = row[pos // bs]
-                if bool((blk < 0).any()):
-                    raise IndexError(
-                        f"prefill block table insufficient to cover {kv_len} tokens (-1 entry reached)"
-                    )
-                k = kc[blk, :, pos % bs, :].repeat_interleave(reps, dim=1)  # [kv_len, H, D]
-                v = vc[blk, :, pos % bs, :].repeat_interleave(reps, dim=1)
-                qpos = torch.arange(cached, kv_len, device=kc.device)
-                mask = pos.unsqueeze(0) <= qpos.unsqueeze(1)
+            seqs = _host_ints(group.seq_indices)
+            cached = _host_ints(group.cached_len_before)
+            qlens = _host_ints(group.query_len)
+            counts = cached if with_chunk else [c + n for c, n in zip(cached, qlens)]
+            ks, vs = paged_gather(kc, vc, attn_metadata.prefill_block_tables, seqs, counts, pool.block_size,
+                                  strict=self.strict)
+            src = 0
+            for c, q_len, n in zip(cached, qlens, counts):
+                kv_len = c + q_len
+                k, v = ks[src:src + n], vs[src:src + n]
+                if with_chunk:
+                    k = torch.cat([k, key[offset:offset + q_len]], dim=0)
+                    v = torch.cat([v, value[offset:offset + q_len]], dim=0)
+                k = k.repeat_interleave(reps, dim=1)
+                v = v.repeat_interleave(reps, dim=1)
+                qpos = torch.arange(c, kv_len, device=query.device)
+                kpos = torch.arange(kv_len, device=query.device)
+                mask = kpos.unsqueeze(0) <= qpos.unsqueeze(1)
                 q = query[offset:offset + q_len]
                 o = torch.nn.functional.scaled_dot_product_attention(
                     q.permute(1, 0, 2).unsqueeze(0), k.permute(1, 0, 2).unsqueeze(0),
@@ -635,6 +770,7 @@ class AttentionBackendB200(AttentionBackend):
                 )
                 parts.append(o.squeeze(0).permute(1, 0, 2))
                 offset += q_len
+                src += n
         if not parts:
             return query
         return torch.cat(parts, dim=0)

@@ -1,0 +1,266 @@
+"""Paged gather (prefill prefix read) and prefill attention on the GPU.
+
+The gather is a copy, so it must be bit-exact: against the reference's own
+gather_paged_kv outputs (golden vectors), against the oracle's gather for
+batched, ragged and shuffled tables, and for every dtype.  Ports the
+reference's TestGatherPrefix (test_paged_attention_gpu.py:695-790), its
+TestPrefillAttention / TestFutureTokenLeakage (test_paged_attention_ref.py:
+342-533), and adds the error contract.
+
+Prefill attention compares with a float32 SDPA of the oracle-gathered K/V
+within 2e-3 + 1e-2 * |ref| (bf16 / f16 inputs; the attention itself is torch
+SDPA on the GPU in the input dtype).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import make_golden as MG
+import mini_vllm_b200 as M
+import oracle
+from conftest import np_to_torch, torch_to_np
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+TDT = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}
+
+
+def _pool(nb, kh, bs, d, dtype, seed):
+    g = torch.Generator().manual_seed(seed)
+    kc = torch.randn(nb, kh, bs, d, generator=g).to(dtype).to(DEV)
+    vc = torch.randn(nb, kh, bs, d, generator=g).to(dtype).to(DEV)
+    return kc, vc
+
+
+def _oracle_gather(kc, vc, ids, n, bs, dt):
+    return oracle.gather(torch_to_np(kc, dt), torch_to_np(vc, dt), np.asarray(ids, np.int64), n, bs, dt)
+
+
+def test_golden_gathers_bit_exact(golden):
+    """Every gather case of the reference's own gather_paged_kv, bit for bit."""
+    cases, arrays = golden
+    ran = 0
+    for c in [c for c in cases if c["kind"] == "gather"]:
+        x = MG.gather_inputs(c)
+        kc, vc = np_to_torch(x["kc"], c["dtype"], DEV), np_to_torch(x["vc"], c["dtype"], DEV)
+        if c["expect_error"]:
+            with pytest.raises(IndexError, match="insufficient"):
+                M.gather_paged_kv(kc, vc, x["table"].tolist(), c["num_tokens"], c["block_size"])
+            continue
+        k, v = M.gather_paged_kv(kc, vc, x["table"].tolist(), c["num_tokens"], c["block_size"])
+        assert k.shape == (c["num_tokens"], c["num_kv_heads"], c["head_dim"]) and k.dtype == TDT[c["dtype"]]
+        assert np.array_equal(torch_to_np(k, c["dtype"]), arrays[f"{c['name']}/k"])
+        assert np.array_equal(torch_to_np(v, c["dtype"]), arrays[f"{c['name']}/v"])
+        ran += 1
+    assert ran >= 6
+
+
+# ---- TestGatherPrefix (test_paged_attention_gpu.py:695-790) ----
+def _written_pool(nb, seq_len, slots, seed):
+    kc = torch.zeros(nb, 2, 16, 64, dtype=torch.float16, device=DEV)
+    vc = torch.zeros_like(kc)
+    g = torch.Generator().manual_seed(seed)
+    k = (torch.randn(seq_len, 2, 64, generator=g) + 10.0).to(torch.float16).to(DEV)
+    v = (torch.randn(seq_len, 2, 64, generator=g) + 1000.0).to(torch.float16).to(DEV)
+    M.paged_cache_write(k, v, kc, vc, torch.as_tensor(slots, dtype=torch.int64, device=DEV), 16)
+    return kc, vc, k, v
+
+
+@pytest.mark.parametrize("seq_len,nb,table", [(10, 32, [0]), (25, 32, [0, 1])])
+def test_gather_prefix_full_and_multi_block(seq_len, nb, table):
+    kc, vc, k, v = _written_pool(nb, seq_len, list(range(seq_len)), seed=seq_len)
+    bt = torch.tensor([table], dtype=torch.int64, device=DEV)
+    gk, gv = M.gather_prefix_kv(kc, vc, bt, [seq_len], [0], 16)
+    assert torch.equal(gk, k) and torch.equal(gv, v)
+    rk, rv = _oracle_gather(kc, vc, table, seq_len, 16, "f16")
+    assert np.array_equal(torch_to_np(gk, "f16"), rk) and np.array_equal(torch_to_np(gv, "f16"), rv)
+
+
+def test_gather_prefix_noncontiguous_blocks():
+    slots = list(range(160, 176)) + list(range(800, 804))
+    kc, vc, k, v = _written_pool(64, 20, slots, seed=3)
+    bt = torch.tensor([[10, 50]], dtype=torch.int64, device=DEV)
+    gk, gv = M.gather_prefix_kv(kc, vc, bt, [20], [0], 16)
+    assert torch.equal(gk, k) and torch.equal(gv, v)
+
+
+def test_gather_prefix_zero_returns_empty():
+    kc, vc = _pool(32, 2, 16, 64, torch.float16, 1)
+    gk, gv = M.gather_prefix_kv(kc, vc, torch.zeros(1, 1, dtype=torch.int64, device=DEV), [0], [0], 16)
+    assert gk.shape == (0, 2, 64) and gv.shape == (0, 2, 64)
+
+
+# ---- batched, ragged, every dtype ----
+@pytest.mark.parametrize("dt,bs,d,kh", [("bf16", 16, 64, 2), ("f16", 32, 128, 8), ("f32", 1, 64, 1),
+                                        ("bf16", 8, 128, 4)])
+def test_batched_gather_matches_oracle(dt, bs, d, kh):
+    rng = np.random.default_rng(bs * 1000 + d)
+    nseq_table = 12
+    counts = rng.integers(0, 300, size=nseq_table)
+    counts[3] = 0
+    need = [(int(n) + bs - 1) // bs for n in counts]
+    maxb = max(need) + 2
+    nb = sum(need) + 5
+    perm = rng.permutation(nb)
+    table = np.full((nseq_table, maxb), -1, np.int64)
+    pos = 0
+    for i, k in enumerate(need):
+        table[i, :k] = perm[pos:pos + k]
+        pos += k
+    kc, vc = _pool(nb, kh, bs, d, TDT[dt], seed=bs + d)
+    seqs = [7, 0, 3, 11, 5, 5]  # repeats and a zero-length sequence are allowed
+    gk, gv = M.gather_prefix_kv(kc, vc, torch.from_numpy(table).to(DEV), [int(counts[s]) for s in seqs], seqs, bs)
+    off = 0
+    for s in seqs:
+        n = int(counts[s])
+        rk, rv = _oracle_gather(kc, vc, table[s, :need[s]], n, bs, dt)
+        assert np.array_equal(torch_to_np(gk[off:off + n], dt), rk), f"seq {s}"
+        assert np.array_equal(torch_to_np(gv[off:off + n], dt), rv), f"seq {s}"
+        off += n
+    assert off == gk.shape[0]
+
+
+def test_large_batched_gather_checksum():
+    """64 sequences of up to 4096 tokens (one launch, ~70 MB moved), against a
+    torch index-gather of the same rows."""
+    rng = np.random.default_rng(5)
+    counts = rng.integers(1, 4096, size=64)
+    need = (counts + 15) // 16
+    nb = int(need.sum()) + 8
+    perm = rng.permutation(nb)
+    maxb = int(need.max())
+    table = np.full((64, maxb), -1, np.int64)
+    pos = 0
+    for i, k in enumerate(need):
+        table[i, :k] = perm[pos:pos + k]
+        pos += k
+    kc, vc = _pool(nb, 2, 16, 64, torch.bfloat16, seed=9)
+    bt = torch.from_numpy(table).to(DEV)
+    gk, gv = M.paged_gather(kc, vc, bt, list(range(64)), counts.tolist(), 16)
+    rows, toks = [], []
+    for i, n in enumerate(counts.tolist()):
+        p = torch.arange(n, device=DEV)
+        rows.append(bt[i][p // 16])
+        toks.append(p % 16)
+    blk, tok = torch.cat(rows), torch.cat(toks)
+    assert torch.equal(gk, kc[blk, :, tok, :]) and torch.equal(gv, vc[blk, :, tok, :])
+
+
+# ---- errors ----
+def test_gather_errors():
+    kc, vc = _pool(8, 2, 16, 64, torch.bfloat16, 2)
+    bt = torch.tensor([[0, -1], [1, 2]], dtype=torch.int64, device=DEV)
+    with pytest.raises(IndexError, match="out of range"):  # -1 inside the prefix
+        M.gather_prefix_kv(kc, vc, bt, [20], [0], 16)
+    with pytest.raises(IndexError, match="insufficient"):  # table too short
+        M.gather_prefix_kv(kc, vc, bt, [40], [1], 16)
+    with pytest.raises(IndexError, match="sequence index"):
+        M.gather_prefix_kv(kc, vc, bt, [4], [2], 16)
+    bad = torch.tensor([[0, 99]], dtype=torch.int64, device=DEV)  # block id past the pool
+    with pytest.raises(IndexError, match="out of range"):
+        M.gather_prefix_kv(kc, vc, bad, [30], [0], 16)
+    with pytest.raises(ValueError):
+        M.gather_prefix_kv(kc, vc, bt, [-1], [0], 16)
+    # the error word is left clear after a raised error
+    gk, _ = M.gather_prefix_kv(kc, vc, bt, [16], [0], 16)
+    assert torch.equal(gk, kc[0].permute(1, 0, 2))
+
+
+# ---- prefill attention ----
+def _sdpa_ref(q, k, v, cached, reps):
+    """float32 SDPA with the offset causal mask (the reference's math)."""
+    qf, kf, vf = q.float(), k.float().repeat_interleave(reps, 1), v.float().repeat_interleave(reps, 1)
+    kv_len, q_len = kf.shape[0], qf.shape[0]
+    mask = torch.arange(kv_len, device=q.device)[None, :] <= torch.arange(cached, cached + q_len,
+                                                                          device=q.device)[:, None]
+    o = torch.nn.functional.scaled_dot_product_attention(
+        qf.permute(1, 0, 2)[None], kf.permute(1, 0, 2)[None], vf.permute(1, 0, 2)[None], attn_mask=mask,
+        scale=q.shape[-1] ** -0.5)
+    return o[0].permute(1, 0, 2)
+
+
+def _close(a, b):
+    assert ((a.float() - b).abs() <= 2e-3 + 1e-2 * b.abs()).all()
+
+
+def _prefill_setup(dtype, seqs, bs=16, kh=2, h=14, d=64, seed=0):
+    """Write each sequence's whole context (cached + new) into a shuffled pool."""
+    g = torch.Generator().manual_seed(seed)
+    need = [(c + n + bs - 1) // bs for c, n in seqs]
+    nb = sum(need) + 4
+    perm = torch.randperm(nb, generator=g)
+    maxb = max(need)
+    table = torch.full((len(seqs), maxb), -1, dtype=torch.int64)
+    pos = 0
+    for i, k in enumerate(need):
+        table[i, :k] = perm[pos:pos + k]
+        pos += k
+    kc = torch.randn(nb, kh, bs, d, generator=g).to(dtype).to(DEV)
+    vc = torch.randn(nb, kh, bs, d, generator=g).to(dtype).to(DEV)
+    ks, vs, qs, new_k, new_v = [], [], [], [], []
+    for i, (c, n) in enumerate(seqs):
+        k = torch.randn(c + n, kh, d, generator=g).to(dtype).to(DEV)
+        v = torch.randn(c + n, kh, d, generator=g).to(dtype).to(DEV)
+        p = torch.arange(c + n)
+        slots = (table[i][p // bs] * bs + p % bs).to(DEV)
+        M.paged_cache_write(k, v, kc, vc, slots, bs)
+        ks.append(k)
+        vs.append(v)
+        new_k.append(k[c:])
+        new_v.append(v[c:])
+        qs.append(torch.randn(n, h, d, generator=g).to(dtype).to(DEV))
+    backend = M.AttentionBackendB200(M.ModelConfig(num_heads=h, num_kv_heads=kh, head_dim=d))
+    pool = M.KVCachePool([kc], [vc], nb, bs, 1, kh, d, DEV, dtype)
+    backend._pool = pool
+    group = M.AttentionGroup(seq_indices=list(range(len(seqs))), attention_type="prefill_gpu",
+                             cached_len_before=torch.tensor([c for c, _ in seqs]),
+                             query_len=torch.tensor([n for _, n in seqs]),
+                             kv_len_after=torch.tensor([c + n for c, n in seqs]))
+    meta = M.AttentionMetadata(groups=[group], prefill_block_tables=table.to(DEV), block_size=bs,
+                               num_kv_heads=kh, head_dim=d)
+    return backend, pool, meta, ks, vs, qs, torch.cat(new_k), torch.cat(new_v)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("with_chunk", [True, False])
+def test_prefill_attention_matches_sdpa(dtype, with_chunk):
+    """Full prefill, prefix 8 + 1..3 new tokens, several sequences (the
+    reference's TestPrefillAttention cases) and a long chunked prefill."""
+    seqs = [(0, 12), (8, 2), (8, 3), (8, 1), (37, 5), (300, 64)]
+    backend, pool, meta, ks, vs, qs, nk, nv = _prefill_setup(dtype, seqs)
+    q = torch.cat(qs)
+    out = backend.prefill_attention(0, q, nk if with_chunk else None, nv if with_chunk else None, meta, pool)
+    assert out.shape == q.shape and out.dtype == dtype
+    off = 0
+    for i, (c, n) in enumerate(seqs):
+        _close(out[off:off + n], _sdpa_ref(qs[i], ks[i], vs[i], c, 7))
+        off += n
+
+
+def test_prefill_future_tokens_blocked():
+    """TestFutureTokenLeakage (test_paged_attention_ref.py:485-533): a query at
+    position P+i never sees positions > P+i, even when they hold extreme V."""
+    kc = torch.zeros(4, 1, 4, 8, dtype=torch.float16, device=DEV)  # head_dim 8: 16-byte rows
+    vc = torch.zeros_like(kc)
+    k_all = torch.zeros(7, 1, 8, dtype=torch.float16)
+    v_all = torch.zeros(7, 1, 8, dtype=torch.float16)
+    for pos in range(7):
+        k_all[pos] = pos + 1
+        v_all[pos] = pos + 1
+    v_all[5:] = 1e4
+    M.paged_cache_write(k_all.to(DEV), v_all.to(DEV), kc, vc, torch.arange(7, device=DEV), 4)
+    q = torch.randn(3, 2, 8, generator=torch.Generator().manual_seed(0)).to(torch.float16).to(DEV)
+    backend = M.AttentionBackendB200.__new__(M.AttentionBackendB200)  # head_dim 8 is below the decode set
+    backend.strict = True
+    pool = M.KVCachePool([kc], [vc], 4, 4, 1, 1, 8, DEV, torch.float16)
+    group = M.AttentionGroup(seq_indices=[0], attention_type="prefill_gpu", cached_len_before=torch.tensor([4]),
+                             query_len=torch.tensor([3]), kv_len_after=torch.tensor([7]))
+    meta = M.AttentionMetadata(groups=[group], prefill_block_tables=torch.tensor([[0, 1]], device=DEV),
+                               block_size=4, num_kv_heads=1, head_dim=8)
+    out = M.AttentionBackendB200.prefill_attention(backend, 0, q, None, None, meta, pool)
+    ref = _sdpa_ref(q, k_all.to(DEV), v_all.to(DEV), 4, 2)
+    _close(out, ref)
+    assert out[0].float().abs().max() < 100  # q0 (position 4) does not see the 1e4 values at 5, 6

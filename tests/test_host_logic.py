@@ -220,3 +220,16 @@ def test_snake_assignment_uneven_batch():
     owned = sharding.snake_assignment(np.array([5, 1, 9, 3, 7]), 2)
     assert sorted(np.concatenate(owned).tolist()) == [0, 1, 2, 3, 4]
     assert sorted(o.size for o in owned) == [2, 3]
+
+
+def test_gather_host_checks_without_gpu():
+    """The gather's host-side contract: a table too short for the requested
+    tokens raises IndexError (gather_paged_kv, cache_read.py:62-67) and host
+    caches are rejected before any device work."""
+    kc = torch.zeros(4, 2, 16, 64, dtype=torch.bfloat16)
+    with pytest.raises(IndexError, match="insufficient to cover 40 tokens"):
+        M.gather_paged_kv(kc, kc, [0, 1], 40, 16)
+    with pytest.raises(M.ArgumentError, match="one CUDA device"):
+        M.paged_gather(kc, kc, torch.zeros(1, 2, dtype=torch.int64), [0], [4], 16)
+    with pytest.raises(M.ArgumentError, match="mismatch"):
+        M.paged_gather(kc, kc[:2], torch.zeros(1, 2, dtype=torch.int64), [0], [4], 16)
