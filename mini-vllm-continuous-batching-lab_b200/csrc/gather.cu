@@ -8,9 +8,9 @@
 // sequences: out[off_i + p] = cache[block_table[row_i][p / BS], :, p % BS, :]
 // for p < n_i, where n_i = out_offsets[i + 1] - out_offsets[i].
 //
-// It is an HBM copy (2 x read + 2 x write of T * KH * D elements), so the
-// kernel moves 16-byte vectors, one per thread and step of a grid-stride loop
-// sized to a few waves of resident threads.  A token whose logical block lies
+// It is an HBM copy (2 x read + 2 x write of T * KH * D elements): 16-byte
+// vectors, four per lane in flight, over a grid-stride loop of one wave of
+// resident CTAs.  A token whose logical block lies
 // past the table (IndexError in gather_paged_kv) or whose block id is outside
 // [0, num_blocks) (-1 padding, where the Triton kernel left the output
 // unwritten) gets zero rows and an error bit.
@@ -39,48 +39,109 @@ struct GatherArgs {
   int* err;
 };
 
-__global__ void __launch_bounds__(256) paged_gather_kernel(const GatherArgs a) {
+// Chunk c of the output is (token t, KV head, 16-byte chunk) with
+// c = (t * KH + kvh) * CH + chunk.  A warp moves U * 32 consecutive chunks per
+// step: it finds the sequence of its first token once (32-ary ballot search
+// over the offsets), each lane steps forward only across sequence boundaries,
+// and all U loads of K and V are in flight before the stores.  POW2: KH, CH and
+// the block size are powers of two, so the index math is shifts and masks.
+constexpr int kGatherUnroll = 4;
+
+__device__ __forceinline__ int gather_find_sequence(const GatherArgs& a, int64_t t, int lane) {
+  int lo = 0, hi = a.num_seqs;  // the last i with offsets[i] <= t (offsets[0] <= t assumed; checked later)
+  while (hi - lo > 1) {
+    const int step = (hi - lo + 31) >> 5;
+    const int probe = lo + lane * step;
+    const bool le = probe < hi && __ldg(a.offsets + probe) <= t;
+    const unsigned m = __ballot_sync(0xffffffffu, le) | 1u;
+    lo += (31 - __clz(m)) * step;
+    hi = min(hi, lo + step);
+  }
+  return lo;
+}
+
+constexpr int kGatherCtasPerSm = 4;  // 256 threads x <= 64 registers
+
+template <bool POW2>
+__global__ void __launch_bounds__(256, kGatherCtasPerSm) paged_gather_kernel(const GatherArgs a) {
   grid_dependency_wait();  // the cache may have been written by the previous kernel
   grid_launch_dependents();
-  const int64_t per_token = (int64_t)a.kh * a.ch;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  constexpr int U = kGatherUnroll;
+  const int lane = threadIdx.x & 31;
+  const int per_token = a.kh * a.ch;
+  const int sh_tok = POW2 ? __ffs(per_token) - 1 : 0, sh_ch = POW2 ? __ffs(a.ch) - 1 : 0;
+  const int sh_bs = POW2 ? __ffs(a.block_size) - 1 : 0;
+  const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t step = (((int64_t)gridDim.x * blockDim.x) >> 5) * (U * 32);
   int bad = 0;
-  for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < a.total_chunks; c += stride) {
-    const int64_t t = c / per_token;
-    const int r = (int)(c - t * per_token);
-    const int kvh = r / a.ch, chunk = r - kvh * a.ch;
-    // sequence of output token t: the last i with offsets[i] <= t
-    int lo = 0, hi = a.num_seqs;
-    while (hi - lo > 1) {
-      const int mid = (lo + hi) >> 1;
-      if (__ldg(a.offsets + mid) <= t)
-        lo = mid;
-      else
-        hi = mid;
-    }
-    const int64_t o0 = __ldg(a.offsets + lo);
-    const int64_t p = t - o0;
-    const int64_t blk = p / a.block_size;
-    const int64_t row = __ldg(a.rows + lo);
-    uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-    if (p < 0 || t >= __ldg(a.offsets + lo + 1)) {
-      bad |= MVB_DEV_KV_LEN;  // offsets are not an increasing prefix starting at 0
-    } else if (row < 0 || row >= a.bt_rows) {
-      bad |= MVB_DEV_BLOCK_ID;
-    } else if (blk >= a.max_blocks) {
-      bad |= MVB_DEV_TABLE_SHORT;
-    } else {
+  // Source chunk of each of this lane's U output chunks in the step at `base`
+  // (-1: a zero row).  Warp-uniform `base`: the search is warp-collective.
+  auto resolve = [&](int64_t base, int64_t (&src)[U]) {
+    const int64_t t0 = POW2 ? (base >> sh_tok) : base / per_token;
+    const int s0 = gather_find_sequence(a, t0, lane);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      src[u] = -1;
+      const int64_t c = base + u * 32 + lane;
+      if (c >= a.total_chunks) continue;
+      const int r = (int)(c - t0 * per_token);  // < U * 32 + per_token
+      const int dt = POW2 ? (r >> sh_tok) : r / per_token;
+      const int rem = r - dt * per_token;
+      const int kvh = POW2 ? (rem >> sh_ch) : rem / a.ch;
+      const int chunk = rem - kvh * a.ch;
+      const int64_t t = t0 + dt;
+      int s = s0;
+      while (s + 1 < a.num_seqs && t >= __ldg(a.offsets + s + 1)) ++s;
+      const int64_t o0 = __ldg(a.offsets + s);
+      const int64_t row = __ldg(a.rows + s);
+      if (t < o0 || t >= __ldg(a.offsets + s + 1)) {
+        bad |= MVB_DEV_KV_LEN;  // offsets are not an increasing prefix starting at 0
+        continue;
+      }
+      if (row < 0 || row >= a.bt_rows) {
+        bad |= MVB_DEV_BLOCK_ID;
+        continue;
+      }
+      const int p = (int)(t - o0);  // a position inside one sequence
+      const int blk = POW2 ? (p >> sh_bs) : p / a.block_size;
+      if (blk >= a.max_blocks) {
+        bad |= MVB_DEV_TABLE_SHORT;
+        continue;
+      }
       const int64_t bid = __ldg(a.bt + row * a.bt_s0 + blk);
       if (bid < 0 || bid >= a.num_blocks) {
         bad |= MVB_DEV_BLOCK_ID;
-      } else {
-        const int64_t src = ((bid * a.kh + kvh) * a.block_size + (p - blk * a.block_size)) * a.ch + chunk;
-        kv = __ldg(a.kc + src);
-        vv = __ldg(a.vc + src);
+        continue;
+      }
+      src[u] = ((bid * a.kh + kvh) * a.block_size + (p - blk * a.block_size)) * a.ch + chunk;
+    }
+  };
+  // Software pipeline: the next step's addresses are resolved (its metadata
+  // loads in flight) while this step's K/V loads are in flight.
+  int64_t base = warp0 * (U * 32);
+  int64_t cur[U];
+  if (base < a.total_chunks) resolve(base, cur);
+  for (; base < a.total_chunks; base += step) {
+    uint4 kv[U], vv[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      kv[u] = make_uint4(0, 0, 0, 0);
+      vv[u] = make_uint4(0, 0, 0, 0);
+      if (cur[u] >= 0) {  // read once: streaming (evict-first) loads
+        kv[u] = __ldcs(a.kc + cur[u]);
+        vv[u] = __ldcs(a.vc + cur[u]);
       }
     }
-    a.ko[c] = kv;
-    a.vo[c] = vv;
+    const int64_t next = base + step;
+    if (next < a.total_chunks) resolve(next, cur);  // cur is free once the loads are issued
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t c = base + u * 32 + lane;
+      if (c < a.total_chunks) {  // streaming stores: the outputs are consumed by the next kernel
+        __stcs(a.ko + c, kv[u]);
+        __stcs(a.vo + c, vv[u]);
+      }
+    }
   }
   if (bad) atomicOr(a.err, bad);
 }
@@ -132,13 +193,17 @@ extern "C" int mvb_paged_gather(const void* key_cache, const void* value_cache, 
   a.num_blocks = num_blocks;
   a.err = error_flags;
 
-  cudaError_t e = ensure_kernel_attrs(paged_gather_kernel, 0);
+  auto pow2 = [](int64_t v) { return v > 0 && (v & (v - 1)) == 0; };
+  const bool p2 = pow2(a.kh) && pow2(a.ch) && pow2(a.block_size);
+  auto kern = p2 ? paged_gather_kernel<true> : paged_gather_kernel<false>;
+  cudaError_t e = ensure_kernel_attrs(kern, 0);
   if (e != cudaSuccess) return MVB_ERR_CUDA;
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t want = (a.total_chunks + 255) / 256;
-  const int64_t cap = (int64_t)sms * 8;  // 8 resident 256-thread CTAs per SM, one wave
+  const int64_t per_cta = 256 * kGatherUnroll;
+  const int64_t want = (a.total_chunks + per_cta - 1) / per_cta;
+  const int64_t cap = (int64_t)sms * kGatherCtasPerSm;  // one wave of resident CTAs
   const unsigned grid = (unsigned)(want < cap ? want : cap);
-  e = launch_pdl(paged_gather_kernel, dim3(grid), dim3(256), 0, static_cast<cudaStream_t>(stream), a);
+  e = launch_pdl(kern, dim3(grid), dim3(256), 0, static_cast<cudaStream_t>(stream), a);
   return e == cudaSuccess ? MVB_OK : MVB_ERR_CUDA;
 }
