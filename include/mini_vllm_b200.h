@@ -57,6 +57,7 @@ extern "C" {
 #define MVB_DEV_SLOT_RANGE    8   /* slot not -1 and outside [0, NB*BS)         */
 #define MVB_DEV_DUP_SLOT     16   /* two tokens of one write target one slot    */
 #define MVB_DEV_TIMEOUT      32   /* a bounded pipeline wait ran out            */
+#define MVB_DEV_POSITION     64   /* a rope position outside the cos/sin table  */
 
 /* ---- decode kernel variants --------------------------------------------- */
 #define MVB_DECODE_AUTO 0  /* STREAM when eligible, else MMA, else FMA           */
@@ -89,6 +90,32 @@ int mvb_paged_gather(const void* key_cache, const void* value_cache, const int64
                      int32_t num_seqs, int64_t total_tokens, int32_t num_kv_heads, int32_t head_dim,
                      int32_t block_size, int32_t num_blocks, int32_t dtype, int32_t* error_flags,
                      void* stream);
+
+/* Rotary position embedding of the step's query and key rows fused with the
+ * paged KV-cache write of the rotated keys and the values: bit for bit the
+ * reference's  q = rope(q, pos); k = rope(k, pos); write_kv_cache(k, v, slots)
+ * (mini_vllm/model_runner/qwen_runner.py:163-170, mini_vllm/model/rotary.py:47-85:
+ * out = x * cos[pos] + rotate_half(x) * sin[pos], each operation rounded to the
+ * dtype).  query / key / value: [T, H|KH|KH, D] with element strides (value may
+ * be a view of the fused QKV output); query_out: [T, H, D] with strides (may
+ * equal query); key_out: optional contiguous [T, KH, D] receiving the rotated
+ * keys (NULL: cache only); positions: int64 [T]; cos_table / sin_table:
+ * contiguous [table_rows, D] of the same dtype (the RotaryEmbedding cache).
+ * Slots follow mvb_kv_cache_write (-1 skipped, range and duplicate checks);
+ * a position outside [0, table_rows) sets MVB_DEV_POSITION and leaves that
+ * token's query/key rows unwritten.  Replaces, as one launch, RotaryEmbedding.__call__
+ * for q and k and triton_cache_write (paged_attention_gpu.py:90-154). */
+int mvb_rope_kv_cache_write(const void* query, int64_t q_stride_token, int64_t q_stride_head,
+                            void* query_out, int64_t qo_stride_token, int64_t qo_stride_head,
+                            const void* key, int64_t k_stride_token, int64_t k_stride_head,
+                            const void* value, int64_t v_stride_token, int64_t v_stride_head,
+                            const int64_t* positions, const void* cos_table, const void* sin_table,
+                            int64_t table_rows, void* key_cache, void* value_cache,
+                            const int64_t* slot_mapping, void* key_out, int32_t num_tokens,
+                            int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+                            int32_t block_size, int32_t num_blocks, int32_t dtype,
+                            uint32_t* slot_claims, uint32_t epoch, int32_t* error_flags,
+                            void* stream);
 
 /* Flag ORed into `variant` of mvb_paged_decode (ignored by the plan): the
  * kernel launched immediately before this call on `stream` is

@@ -18,6 +18,8 @@ from .attention import (
     paged_cache_write,
     paged_decode_attention,
     paged_gather,
+    rope_cache_write,
+    rope_tables,
     triton_cache_write,
     triton_decode_attention,
 )
@@ -42,6 +44,8 @@ __all__ = [
     "paged_cache_write",
     "paged_decode_attention",
     "paged_gather",
+    "rope_cache_write",
+    "rope_tables",
     "triton_cache_write",
     "triton_decode_attention",
 ]

@@ -38,6 +38,7 @@ DEV_TABLE_SHORT = 4
 DEV_SLOT_RANGE = 8
 DEV_DUP_SLOT = 16
 DEV_TIMEOUT = 32
+DEV_POSITION = 64
 
 # decode variants (MVB_DECODE_*)
 DECODE_AUTO = 0
@@ -74,6 +75,11 @@ SIGNATURES = {
         _i32,
         [_vp, _vp, _vp, _i64, _i64, _i32, _vp, _vp, _vp, _vp, _i32, _i64, _i32, _i32, _i32, _i32, _i32,
          _vp, _vp],
+    ),
+    "mvb_rope_kv_cache_write": (
+        _i32,
+        [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64,
+         _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _u32, _vp, _vp],
     ),
     "mvb_paged_decode_noalloc": (
         _i32,

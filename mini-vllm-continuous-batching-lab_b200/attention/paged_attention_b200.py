@@ -199,6 +199,9 @@ def _raise_flags(flags: int, detail: Optional[Dict[str, Any]]) -> None:
             "Duplicate slots in slot_mapping: parallel writes to one slot race, "
             "so duplicate slots are forbidden."
         )
+    if flags & _native.DEV_POSITION:
+        rows = d.get("table_rows")
+        raise IndexError(f"rope position out of range of the cos/sin table ({rows} rows)")
     if flags & _native.DEV_TIMEOUT:
         raise RuntimeError("paged decode: a bounded pipeline wait timed out on the device")
     raise RuntimeError(f"unknown device error flags 0x{flags:x}")
@@ -638,6 +641,124 @@ def gather_paged_kv(
         )
     table = torch.tensor([ids or [0]], dtype=torch.int64)
     return paged_gather(key_cache, value_cache, table, [0], [int(num_tokens)], block_size)
+
+
+# ---------------------------------------------------------------------------
+# rotary embedding fused with the KV write
+# ---------------------------------------------------------------------------
+def rope_tables(head_dim: int, theta: float = 1000000.0, max_seq_len: int = 32768,
+                dtype: torch.dtype = torch.float32, device=None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """The cos / sin cache ``[max_seq_len, head_dim]`` of the reference's
+    RotaryEmbedding (mini_vllm/model/rotary.py:15-33): inverse frequencies
+    theta^(-2i/D), outer product with the positions, duplicated halves, cos/sin
+    in float32, then cast to ``dtype``.  The same torch operations in the same
+    order, so the tables are bit-identical to the reference's on the same
+    device."""
+    inv_freq = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float32, device=device) / head_dim))
+    pos = torch.arange(max_seq_len, dtype=torch.float32, device=device)
+    freqs = torch.einsum("i,j->ij", pos, inv_freq)
+    emb = torch.cat((freqs, freqs), dim=-1)
+    return emb.cos().to(dtype), emb.sin().to(dtype)
+
+
+def rope_cache_write(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    positions: torch.Tensor,
+    cos: torch.Tensor,
+    sin: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    slot_mapping: torch.Tensor,
+    block_size: int,
+    *,
+    query_out: Optional[torch.Tensor] = None,
+    return_key: bool = False,
+    strict: bool = True,
+    check_duplicates: bool = True,
+) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """RoPE of the step's query and key rows fused with the paged KV write, in one launch.
+
+    Bit for bit the reference's ``q = rope(q, positions); k = rope(k, positions);
+    write_kv_cache(k, v, slot_mapping)`` (mini_vllm/model_runner/qwen_runner.py:
+    163-170) with ``rope`` = ``RotaryEmbedding.__call__`` (rotary.py:47-85) over
+    the tables ``cos`` / ``sin`` (see ``rope_tables``).  Returns the rotated
+    query (into ``query_out`` when given, which may be ``query`` itself) and,
+    with ``return_key``, the rotated keys (which the prefill path appends after
+    the cached prefix).  Slots follow ``paged_cache_write``; a position outside
+    the tables raises ``IndexError``.
+    """
+    _require(query.dim() == 3 and key.dim() == 3 and key.shape == value.shape,
+             lambda: f"query {tuple(query.shape)} / key {tuple(key.shape)} / value {tuple(value.shape)}")
+    num_tokens, num_heads, head_dim = query.shape
+    _require(key.shape[0] == num_tokens and key.shape[2] == head_dim,
+             lambda: f"key {tuple(key.shape)} does not match query {tuple(query.shape)}")
+    num_kv_heads = key.shape[1]
+    _require(key_cache.dim() == 4 and key_cache.shape == value_cache.shape
+             and key_cache.shape[1] == num_kv_heads and key_cache.shape[3] == head_dim,
+             lambda: f"caches {tuple(key_cache.shape)} / {tuple(value_cache.shape)} do not match key "
+                     f"{tuple(key.shape)}")
+    _require(block_size > 0 and key_cache.shape[2] == block_size,
+             lambda: f"block_size {block_size} != cache dim2 {key_cache.shape[2]}")
+    _require(head_dim % 2 == 0, lambda: f"head_dim {head_dim} must be even")
+    dt = query.dtype
+    _require(dt in _DTYPE_CODES and key.dtype == dt and value.dtype == dt and key_cache.dtype == dt
+             and value_cache.dtype == dt and cos.dtype == dt and sin.dtype == dt,
+             "query, key, value, caches and cos/sin tables must share one dtype (bf16, f16 or f32)")
+    _require(cos.dim() == 2 and cos.shape == sin.shape and cos.shape[1] == head_dim,
+             lambda: f"cos/sin tables {tuple(cos.shape)} / {tuple(sin.shape)} must be [rows, {head_dim}]")
+    _require(positions.dim() == 1 and positions.shape[0] == num_tokens,
+             lambda: f"positions {tuple(positions.shape)} != ({num_tokens},)")
+    _require(slot_mapping.dim() == 1 and slot_mapping.shape[0] == num_tokens,
+             lambda: f"slot_mapping {tuple(slot_mapping.shape)} != ({num_tokens},)")
+    _require(query.is_cuda, lambda: f"query.device must be cuda, got {query.device}")
+    dev_idx = query.get_device()
+    _require(all(t.get_device() == dev_idx for t in (key, value, key_cache, value_cache, cos, sin)),
+             "query, key, value, caches and tables must be on one CUDA device")
+    _require(key_cache.is_contiguous() and value_cache.is_contiguous(), "caches must be contiguous")
+    if query_out is None:
+        query_out = torch.empty((num_tokens, num_heads, head_dim), dtype=dt, device=query.device)
+    else:
+        _require(query_out.shape == query.shape and query_out.dtype == dt and query_out.get_device() == dev_idx
+                 and query_out.stride(2) == 1, "query_out must match query and have a contiguous last dim")
+    key_out = torch.empty((num_tokens, num_kv_heads, head_dim), dtype=dt, device=query.device) if return_key \
+        else None
+    if num_tokens == 0:
+        return query_out, key_out
+    if query.stride(2) != 1:
+        query = query.contiguous()
+    if key.stride(2) != 1:
+        key = key.contiguous()
+    if value.stride(2) != 1:
+        value = value.contiguous()
+    cos, sin = cos.contiguous(), sin.contiguous()
+    if positions.dtype != torch.int64 or positions.get_device() != dev_idx or not positions.is_contiguous():
+        positions = positions.to(device=query.device, dtype=torch.int64).contiguous()
+    if slot_mapping.dtype != torch.int64 or slot_mapping.get_device() != dev_idx or not slot_mapping.is_contiguous():
+        slot_mapping = slot_mapping.to(device=query.device, dtype=torch.int64).contiguous()
+    state = _state(dev_idx)
+    num_blocks = key_cache.shape[0]
+    if check_duplicates:
+        claims, epoch = state.next_claims(num_blocks * block_size)
+        claims_ptr = claims.data_ptr()
+    else:
+        claims_ptr, epoch = None, 0
+    status = _native.lib().mvb_rope_kv_cache_write(
+        query.data_ptr(), query.stride(0), query.stride(1), query_out.data_ptr(), query_out.stride(0),
+        query_out.stride(1), key.data_ptr(), key.stride(0), key.stride(1), value.data_ptr(), value.stride(0),
+        value.stride(1), positions.data_ptr(), cos.data_ptr(), sin.data_ptr(), cos.shape[0],
+        key_cache.data_ptr(), value_cache.data_ptr(), slot_mapping.data_ptr(),
+        key_out.data_ptr() if key_out is not None else None, num_tokens, num_heads, num_kv_heads, head_dim,
+        block_size, num_blocks, _DTYPE_CODES[dt], claims_ptr, epoch, state.err_ptr, _stream_handle(dev_idx),
+    )
+    _host_status(status, "rope + kv cache write")
+    if strict:
+        flags = _take_flags(state)
+        if flags:
+            _raise_flags(flags, {"slot_mapping": slot_mapping, "total_slots": num_blocks * block_size,
+                                 "block_size": block_size, "num_blocks": num_blocks, "table_rows": cos.shape[0]})
+    return query_out, key_out
 
 
 # Reference names, for code that imports them from the Triton module.

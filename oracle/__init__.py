@@ -1,4 +1,4 @@
-"""CPU oracle of mini-vLLM's paged KV write and paged decode — test infrastructure.
+"""CPU oracle of mini-vLLM's paged KV write, gather, decode and RoPE — test infrastructure.
 
 Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline /
 reference arm may use this package, and only as the checker or the timed CPU
@@ -17,6 +17,9 @@ from .oracle import (  # noqa: F401
     decode,
     decode_numpy,
     gather,
+    from_float32,
     max_threads,
+    rope_numpy,
+    round_to_dtype,
     to_float32,
 )

@@ -19,6 +19,8 @@ Reference lines restated:
   gather       <- mini_vllm/cache/cache_read.py:19-84     (gather_paged_kv)
   decode       <- mini_vllm/attention/paged_attention_ref.py:102-161
                   (AttentionBackendRef.decode_attention; torch SDPA math)
+  rope_numpy   <- mini_vllm/model/rotary.py:47-85 (RotaryEmbedding.__call__,
+                  _rotate_half), with the rounding of each torch operation
 """
 
 from __future__ import annotations
@@ -202,3 +204,45 @@ def decode_numpy(query, key_cache, value_cache, block_table, kv_len, block_size:
         p /= p.sum(axis=1, keepdims=True)
         out[s] = np.einsum("hn,nhd->hd", p, v).astype(np.float32)
     return out
+
+
+# ---------------------------------------------------------------------------
+# rotary embedding (numpy restatement)
+# ---------------------------------------------------------------------------
+def round_to_dtype(x32: np.ndarray, dtype: str) -> np.ndarray:
+    """float32 values rounded to `dtype` (round to nearest even), as float32."""
+    x32 = np.asarray(x32, dtype=np.float32)
+    if dtype == "f32":
+        return x32
+    if dtype == "f16":
+        return x32.astype(np.float16).astype(np.float32)
+    bits = x32.view(np.uint32).astype(np.uint64)
+    rounded = (bits + 0x7FFF + ((bits >> 16) & 1)) >> 16
+    nan = np.isnan(x32)
+    out = (rounded.astype(np.uint32) << 16).view(np.float32).copy()
+    out[nan] = x32[nan]
+    return out
+
+
+def from_float32(x32: np.ndarray, dtype: str) -> np.ndarray:
+    """float32 values already representable in `dtype` to the storage form."""
+    if dtype == "bf16":
+        return (np.asarray(x32, np.float32).view(np.uint32) >> 16).astype(np.uint16)
+    return np.asarray(x32).astype(np.float16 if dtype == "f16" else np.float32)
+
+
+def rope_numpy(x, positions, cos, sin, dtype: str) -> np.ndarray:
+    """x * cos[pos] + rotate_half(x) * sin[pos] over [T, heads, D] (rotary.py:47-85).
+
+    Each of the three torch operations rounds to the dtype: the products are
+    formed in float32 (exact for 16-bit inputs) and rounded, their sum is a
+    float32 add of the rounded products, rounded again."""
+    xf = to_float32(np.asarray(x), dtype)
+    pos = np.asarray(positions, dtype=np.int64)
+    c = to_float32(np.asarray(cos), dtype)[pos][:, None, :]
+    sn = to_float32(np.asarray(sin), dtype)[pos][:, None, :]
+    half = xf.shape[-1] // 2
+    rot = np.concatenate([-xf[..., half:], xf[..., :half]], axis=-1)
+    a = round_to_dtype(xf * c, dtype)
+    b = round_to_dtype(rot * sn, dtype)
+    return from_float32(round_to_dtype(a + b, dtype), dtype)

@@ -117,6 +117,24 @@ def write_spec_inputs(c: Dict) -> Dict[str, np.ndarray]:
             "value": t["new_value"], "slots": spec.slot_mapping, "block_size": spec.block_size}
 
 
+def rope_inputs(c: Dict) -> Dict[str, np.ndarray]:
+    """Inputs of a fused RoPE + write case (query, key, value, positions, pools, slots)."""
+    rng = np.random.default_rng(c["seed"])
+    t, h, kh, d = c["num_tokens"], c["num_heads"], c["num_kv_heads"], c["head_dim"]
+    nb, bs, dt = c["num_blocks"], c["block_size"], c["dtype"]
+    slots = rng.permutation(nb * bs)[:t].astype(np.int64)
+    for i in c.get("skip", []):
+        slots[i] = -1
+    lo = c.get("pos_min", 0)
+    return {"q": _conv(rng.standard_normal((t, h, d), dtype=np.float32), dt),
+            "k": _conv(rng.standard_normal((t, kh, d), dtype=np.float32), dt),
+            "v": _conv(rng.standard_normal((t, kh, d), dtype=np.float32), dt),
+            "kc0": _conv(rng.standard_normal((nb, kh, bs, d), dtype=np.float32), dt),
+            "vc0": _conv(rng.standard_normal((nb, kh, bs, d), dtype=np.float32), dt),
+            "positions": rng.integers(lo, c["max_seq"], size=t).astype(np.int64),
+            "slots": slots}
+
+
 # ---------------------------------------------------------------------------
 # case list
 # ---------------------------------------------------------------------------
@@ -192,6 +210,18 @@ def case_list() -> List[Dict]:
     dt_("d_gqa4_d128_bf16", "bf16", 12, 32, 8, 16, 128, [[5, 9, 1, -1], [11, 2, 3, 4]], [33, 49], 37)
     dt_("d_bs32_f16", "f16", 12, 4, 2, 32, 64, [[3, 9, -1], [1, 2, 0]], [40, 96], 38)
     dt_("d_gqa7_d64_f32", "f32", 16, 14, 2, 16, 64, [[4, 8, 0], [14, 1, 2]], [48, 33], 39)
+
+    def r(name, dtype, t, h, kh, d, theta, max_seq, nb, bs, seed, **kw):
+        cases.append(dict(kind="rope", name=name, dtype=dtype, num_tokens=t, num_heads=h, num_kv_heads=kh,
+                          head_dim=d, theta=theta, max_seq=max_seq, num_blocks=nb, block_size=bs, seed=seed,
+                          **kw))
+
+    # RotaryEmbedding + write_to_paged_cache, as the runner applies them (qwen_runner.py:163-170)
+    r("r_qwen_bf16", "bf16", 16, 14, 2, 64, 1e6, 4096, 16, 16, 40, skip=[3])
+    r("r_d128_f16", "f16", 7, 8, 4, 128, 1e4, 512, 8, 16, 41)
+    r("r_small_f32", "f32", 5, 4, 2, 64, 1e6, 64, 4, 4, 42, skip=[0])
+    r("r_far_pos_bf16", "bf16", 9, 4, 1, 64, 1e6, 32768, 4, 16, 43, pos_min=30000)
+    r("r_d32_bf16", "bf16", 3, 2, 1, 32, 1e4, 128, 2, 4, 44)
     return cases
 
 
@@ -206,6 +236,7 @@ def main(ref_root: str) -> None:
     from mini_vllm.cache.cache_read import gather_paged_kv
     from mini_vllm.cache.cache_write import write_to_paged_cache
     from mini_vllm.cache.pool import KVCachePool
+    from mini_vllm.model.rotary import RotaryEmbedding
     from mini_vllm.model_runner.base import AttentionGroup, AttentionMetadata, ModelConfig
 
     def to_torch(a: np.ndarray, dtype: str) -> torch.Tensor:
@@ -251,6 +282,20 @@ def main(ref_root: str) -> None:
             if rows_k:
                 arrays[f"{name}/rows_k"] = np.stack(rows_k)
                 arrays[f"{name}/rows_v"] = np.stack(rows_v)
+        elif c["kind"] == "rope":
+            x = rope_inputs(c)
+            c["inputs_sha256"] = sha(x["q"], x["k"], x["v"], x["kc0"], x["vc0"], x["positions"], x["slots"])
+            tdt = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[dt]
+            rope = RotaryEmbedding(head_dim=c["head_dim"], theta=c["theta"], max_seq_len=c["max_seq"], dtype=tdt)
+            c["tables_sha256"] = sha(to_numpy(rope.cos, dt), to_numpy(rope.sin, dt))
+            pos = torch.from_numpy(x["positions"])
+            q_rot = rope(to_torch(x["q"], dt), pos)
+            k_rot = rope(to_torch(x["k"], dt), pos)
+            kc, vc = to_torch(x["kc0"], dt), to_torch(x["vc0"], dt)
+            write_to_paged_cache(k_rot, to_torch(x["v"], dt), kc, vc, torch.from_numpy(x["slots"]),
+                                 c["block_size"])
+            arrays[f"{name}/q_rot"], arrays[f"{name}/k_rot"] = to_numpy(q_rot, dt), to_numpy(k_rot, dt)
+            c["result_sha256"] = sha(to_numpy(kc, dt), to_numpy(vc, dt))
         elif c["kind"] == "gather":
             x = gather_inputs(c)
             c["inputs_sha256"] = sha(x["kc"], x["vc"], x["table"])
@@ -296,4 +341,6 @@ def load_golden():
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py <path of the reference checkout>")
+    main(sys.argv[1])

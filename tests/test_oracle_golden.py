@@ -1,8 +1,8 @@
 """Pin the CPU oracle to the reference (CPU only).
 
 The golden vectors in tests/golden were produced by the reference's own
-write_to_paged_cache, gather_paged_kv and AttentionBackendRef.decode_attention
-(tests/golden/make_golden.py).  The C oracle must reproduce the writes and
+write_to_paged_cache, gather_paged_kv, AttentionBackendRef.decode_attention and
+RotaryEmbedding (tests/golden/make_golden.py).  The C oracle must reproduce the writes and
 gathers bit for bit and the decodes to float32 round-off; the numpy
 restatement must agree with the C one.
 """
@@ -24,7 +24,7 @@ def _cases(golden, kind):
 def test_golden_fixture_covers_all_kinds(golden):
     cases, _ = golden
     kinds = {c["kind"] for c in cases}
-    assert kinds == {"write", "write_spec", "gather", "decode", "decode_spec"}
+    assert kinds == {"write", "write_spec", "gather", "decode", "decode_spec", "rope"}
     assert len(cases) >= 60
 
 
@@ -114,3 +114,39 @@ def test_oracle_threads_do_not_change_results():
     a, _ = oracle.decode(t["query"], t["key_cache"], t["value_cache"], spec.block_tables, spec.context_lens, 16, "bf16", threads=1)
     b, _ = oracle.decode(t["query"], t["key_cache"], t["value_cache"], spec.block_tables, spec.context_lens, 16, "bf16", threads=0)
     assert np.array_equal(a, b)
+
+
+def _storage(t, dtype):
+    import torch
+
+    if dtype == "bf16":
+        return t.contiguous().view(torch.int16).numpy().view(np.uint16).copy()
+    return t.contiguous().numpy().copy()
+
+
+def test_rope_tables_and_oracle_rope_write_bit_exact(golden):
+    """rope_tables reproduces the reference's RotaryEmbedding cos/sin caches bit
+    for bit (CPU), and the numpy restatement of rope followed by the oracle's
+    write reproduces the reference's rotated q / k and the whole pool."""
+    import mini_vllm_b200 as M
+
+    cases, arrays = _cases(golden, "rope")
+    assert len(cases) >= 5
+    tdt = {"bf16": "bfloat16", "f16": "float16", "f32": "float32"}
+    for c in cases:
+        import torch
+
+        dt = c["dtype"]
+        x = MG.rope_inputs(c)
+        assert MG.sha(x["q"], x["k"], x["v"], x["kc0"], x["vc0"], x["positions"], x["slots"]) == \
+            c["inputs_sha256"], c["name"]
+        cos, sin = M.rope_tables(c["head_dim"], c["theta"], c["max_seq"], getattr(torch, tdt[dt]))
+        cos_np, sin_np = _storage(cos, dt), _storage(sin, dt)
+        assert MG.sha(cos_np, sin_np) == c["tables_sha256"], c["name"]
+        q_rot = oracle.rope_numpy(x["q"], x["positions"], cos_np, sin_np, dt)
+        k_rot = oracle.rope_numpy(x["k"], x["positions"], cos_np, sin_np, dt)
+        assert np.array_equal(q_rot, arrays[f"{c['name']}/q_rot"]), c["name"]
+        assert np.array_equal(k_rot, arrays[f"{c['name']}/k_rot"]), c["name"]
+        kc, vc = x["kc0"].copy(), x["vc0"].copy()
+        oracle.cache_write(k_rot, x["v"], kc, vc, x["slots"], c["block_size"], dt)
+        assert MG.sha(kc, vc) == c["result_sha256"], c["name"]
