@@ -16,14 +16,15 @@
 //   * a unit cut by a range boundary is written as a partial state
 //     (m, l, O per head row) to the warp's first or last slot.
 // decode_stream_fixup_kernel then merges the partials of every cut unit (one
-// warp per unit, contributors in warp order, so the result is deterministic).
+// CTA per unit, contributors in warp order, so the result is deterministic).
 // It is launched as a programmatic dependent of the streaming kernel, so its
-// launch overlaps the streaming kernel's tail; merging inside the streaming
-// kernel instead put 10-20 us of dependent L2 round trips on the critical path
-// of whichever warp finished a unit last.
+// CTAs are scheduled during the streaming kernel's tail.  Merging inside the
+// streaming kernel (per warp or per CTA, by the last arriver) was measured and
+// was slower: the arrivals and merges land on the critical path of the warps
+// that finish last.
 // The only CTA-wide synchronisation is the prologue, where the CTA scans
-// kv_len into the per-sequence tile prefix it locates tiles with; CTA 0 also
-// stores that prefix for the fixup kernel.
+// kv_len into the per-sequence tile prefix it locates tiles with; the warp that
+// begins a cut unit leaves a descriptor of it for the fixup kernel.
 #include "mma_tile.cuh"
 
 namespace mvb {
@@ -335,7 +336,8 @@ decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
 }
 
 // ---------------------------------------------------------------------------
-// fixup: merge the partial states of every unit cut by a warp-range boundary
+// fixup, one warp per unit: merge the partial states of every unit cut by a
+// warp-range boundary (units cut into few pieces)
 // ---------------------------------------------------------------------------
 // One warp per warp w of the stream grid: when w begins a cut unit (its
 // descriptor says which), the warp merges every head row of that unit, RP rows
@@ -461,6 +463,184 @@ __global__ void __launch_bounds__(128) decode_stream_fixup_kernel(const DecodeAr
 }
 
 // ---------------------------------------------------------------------------
+// fixup, one CTA per unit: the same merge for units cut into many pieces
+// ---------------------------------------------------------------------------
+// One CTA of kFixupWarps warps per kFixupWarps warps of the stream grid: for
+// each of them that begins a cut unit (its descriptor says which), the whole
+// CTA merges every head row of that unit, RP rows per pass:
+//   out[r][d] = sum_c O_c[r][d] 2^(m_c - M_r) / L_r,
+//   M_r = max_c m_c,  L_r = sum_c l_c 2^(m_c - M_r).
+// The contributors are split into kFixupWarps contiguous shares.  Each warp
+// loads its share's (m, l) (lane c: contributor c of the share) together with
+// the O columns of its first CB contributors, reduces its share's max and sum,
+// and the CTA combines the shares' (max, sum) pairs in shared memory; each warp
+// then accumulates its share's columns with coefficients broadcast from the
+// owning lanes, and the shares' sums are added in shared memory.  A unit cut
+// into at most kFixupWarps * CB pieces costs one L2 round trip after the
+// descriptor's; a long unit cut into ~30 pieces (32 K-token contexts) two.
+// Contributors are the warps holding tiles of the unit, in warp order (w..w_last
+// when every warp has tiles, T_all >= warps; else, with one tile per non-empty
+// warp, the warps holding tiles us, us + 1, ...), and the summation order is
+// fixed, so the result does not depend on timing.
+constexpr int kFixupWarps = 4;
+// Average pieces per unit above which the CTA fixup is used (the warp fixup
+// merges CB = 4 pieces per L2 round trip).
+constexpr int kFixupCtaPiecesPerUnit = 8;
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kFixupWarps * 32) decode_stream_fixup_cta_kernel(const DecodeArgs a,
+                                                                                  const StreamArgs sa) {
+  constexpr int ROW = D + 2, DPL = D / 32, FW = kFixupWarps;
+  constexpr int RP = D == 64 ? 8 : 4;  // head rows per pass
+  constexpr int CB = 4;                // contributors per batch of O loads (divides 32)
+  __shared__ float s_m[FW][RP], s_l[FW][RP];
+  __shared__ float s_acc[FW][RP][D];
+  __shared__ int4 s_desc[FW][2];
+  grid_dependency_wait();  // the streaming kernel's partials and descriptors are visible
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int Wtot = sa.num_warps;
+  if (threadIdx.x < 2 * FW) {  // the FW descriptors of this CTA's stream warps, in one round trip
+    const int w = blockIdx.x * FW + (threadIdx.x >> 1);
+    s_desc[threadIdx.x >> 1][threadIdx.x & 1] = w < Wtot ? __ldcg(sa.desc + 2 * w + (threadIdx.x & 1))
+                                                         : make_int4(-1, 0, 0, 0);
+  }
+  __syncthreads();
+  for (int q = 0; q < FW; ++q) {
+    const int4 d0 = s_desc[q][0];
+    if (d0.x < 0) continue;  // CTA-uniform
+    const int4 d1 = s_desc[q][1];
+    const int w_first = blockIdx.x * FW + q;
+    const int us = d0.x, ue = d0.y, seq = d0.z, T_all = d0.w, h0 = d1.x, nrows = d1.y;
+    const bool dense = T_all >= Wtot;
+    const int nct = dense ? stream_warp_of(ue - 1, T_all, Wtot) - w_first + 1 : ue - us;
+    auto contributor = [&](int c) { return dense ? w_first + c : stream_warp_of(us + c, T_all, Wtot); };
+    // w_first keeps the unit in its "last" slot (1), later contributors in slot 0
+    auto row_ptr = [&](int w, int r) -> const float* {
+      return sa.part + ((int64_t)w * 2 + (w == w_first ? 1 : 0)) * 16 * ROW + r * ROW;
+    };
+    // this warp's share of the contributors: [c_lo, c_hi)
+    const int share = (nct + FW - 1) / FW;
+    const int c_lo = min(nct, warp * share), c_hi = min(nct, c_lo + share);
+    T* out = static_cast<T*>(a.out) + (int64_t)seq * a.o_s0;
+
+    for (int rb = 0; rb < nrows; rb += RP) {
+      float x[CB][RP][DPL];  // O columns of contributors c0 .. c0 + CB - 1 of the share (0 past its end)
+      auto load_batch = [&](int c0) {
+  #pragma unroll
+        for (int c = 0; c < CB; ++c) {
+          const int w = c0 + c < c_hi ? contributor(c0 + c) : -1;
+  #pragma unroll
+          for (int r = 0; r < RP; ++r)
+  #pragma unroll
+            for (int i = 0; i < DPL; ++i)
+              x[c][r][i] = w >= 0 && rb + r < nrows ? __ldcg(row_ptr(w, rb + r) + 2 + lane + 32 * i) : 0.f;
+        }
+      };
+      float2 ml[RP];  // (m, l) of contributor c32 + lane
+      bool ok;        // ... which exists
+      auto load_ml = [&](int c32) {
+        const int w = c32 + lane < c_hi ? contributor(c32 + lane) : -1;
+        ok = w >= 0;
+  #pragma unroll
+        for (int r = 0; r < RP; ++r)
+          ml[r] = ok && rb + r < nrows ? __ldcg(reinterpret_cast<const float2*>(row_ptr(w, rb + r)))
+                                       : make_float2(-INFINITY, 0.f);
+      };
+      load_batch(c_lo);  // in flight during the (m, l) pass
+      load_ml(c_lo);
+      // the share's max and sum per row, 32 contributors per step
+      float M[RP], L[RP];
+  #pragma unroll
+      for (int r = 0; r < RP; ++r) M[r] = -INFINITY, L[r] = 0.f;
+      for (int c32 = c_lo; c32 < c_hi;) {
+  #pragma unroll
+        for (int r = 0; r < RP; ++r) {
+          float bm = ml[r].x;
+  #pragma unroll
+          for (int sh = 16; sh > 0; sh >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, sh));
+          const float nm = fmaxf(M[r], bm);
+          float sum = ok && nm > -INFINITY ? ml[r].y * fast_exp2(ml[r].x - nm) : 0.f;
+  #pragma unroll
+          for (int sh = 16; sh > 0; sh >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, sh);
+          L[r] = (M[r] > -INFINITY ? L[r] * fast_exp2(M[r] - nm) : 0.f) + sum;
+          M[r] = nm;
+        }
+        c32 += 32;
+        if (c32 >= c_hi) break;
+        load_ml(c32);
+      }
+      if (lane == 0) {
+  #pragma unroll
+        for (int r = 0; r < RP; ++r) s_m[warp][r] = M[r], s_l[warp][r] = L[r];
+      }
+      __syncthreads();
+      // the unit's max and sum per row, shares in a fixed order
+      float inv[RP];
+  #pragma unroll
+      for (int r = 0; r < RP; ++r) {
+        float gm = -INFINITY;
+  #pragma unroll
+        for (int q = 0; q < FW; ++q) gm = fmaxf(gm, s_m[q][r]);
+        float gl = 0.f;
+  #pragma unroll
+        for (int q = 0; q < FW; ++q)
+          if (s_m[q][r] > -INFINITY) gl += s_l[q][r] * fast_exp2(s_m[q][r] - gm);
+        M[r] = gm;
+        inv[r] = 1.f / gl;
+      }
+      float acc[RP][DPL];
+  #pragma unroll
+      for (int r = 0; r < RP; ++r)
+  #pragma unroll
+        for (int i = 0; i < DPL; ++i) acc[r][i] = 0.f;
+      if (c_lo < c_hi) {
+        // coefficient 2^(m_c - M) / L of contributor cf_base + lane
+        float cf[RP];
+        int cf_base = c_lo;
+        auto coeffs = [&]() {
+  #pragma unroll
+          for (int r = 0; r < RP; ++r) cf[r] = ok ? fast_exp2(ml[r].x - M[r]) * inv[r] : 0.f;
+        };
+        if (c_hi - c_lo > 32) load_ml(c_lo);  // the pass above left a later group in ml
+        coeffs();
+        for (int c0 = c_lo;; c0 += CB) {
+          if (c0 - cf_base >= 32) {  // next group of 32 contributors
+            cf_base += 32;
+            load_ml(cf_base);
+            coeffs();
+          }
+  #pragma unroll
+          for (int c = 0; c < CB; ++c)
+  #pragma unroll
+            for (int r = 0; r < RP; ++r) {
+              const float wt = __shfl_sync(0xffffffffu, cf[r], c0 - cf_base + c);
+  #pragma unroll
+              for (int i = 0; i < DPL; ++i) acc[r][i] = fmaf(x[c][r][i], wt, acc[r][i]);
+            }
+          if (c0 + CB >= c_hi) break;
+          load_batch(c0 + CB);
+        }
+      }
+  #pragma unroll
+      for (int r = 0; r < RP; ++r)
+  #pragma unroll
+        for (int i = 0; i < DPL; ++i) s_acc[warp][r][lane + 32 * i] = acc[r][i];
+      __syncthreads();
+      for (int e = threadIdx.x; e < RP * D; e += FW * 32) {
+        const int r = e / D, col = e - r * D;
+        if (rb + r < nrows) {
+          float v = 0.f;
+  #pragma unroll
+          for (int q = 0; q < FW; ++q) v += s_acc[q][r][col];
+          out[(int64_t)(h0 + rb + r) * a.o_s1 + col] = from_f32<T>(v);
+        }
+      }
+      __syncthreads();  // s_m / s_acc are reused by the next pass
+    }
+  }  // q
+}
+
+// ---------------------------------------------------------------------------
 // host launch
 // ---------------------------------------------------------------------------
 // Warps per CTA and pipeline stages per warp (overridable at build time for tuning sweeps).
@@ -507,6 +687,8 @@ cudaError_t launch_stream_t(const CUtensorMap& tmk, const CUtensorMap& tmv, cons
   if (e != cudaSuccess) return e;
   e = ensure_kernel_attrs(decode_stream_fixup_kernel<T, D>, 0);
   if (e != cudaSuccess) return e;
+  e = ensure_kernel_attrs(decode_stream_fixup_cta_kernel<T, D>, 0);
+  if (e != cudaSuccess) return e;
   // Resident CTAs per SM, queried once per (device, shared-memory size): the
   // query costs microseconds of host time, and this runs once per layer-step.
   static std::mutex occ_mu;
@@ -538,8 +720,15 @@ cudaError_t launch_stream_t(const CUtensorMap& tmk, const CUtensorMap& tmv, cons
   sa.num_warps = ctas * NW;
   e = launch_pdl(kern, dim3(ctas), dim3(NW * 32), smem, stream, tmk, tmv, a, sa);
   if (e != cudaSuccess) return e;
-  return launch_pdl(decode_stream_fixup_kernel<T, D>, dim3((unsigned)((sa.num_warps + 3) / 4)), dim3(128), 0,
-                    stream, a, sa);
+  // Stream warps per unit = the pieces an average unit is cut into: few (many
+  // short sequences) -> one warp per unit; many (a few long sequences) -> the
+  // warps of a CTA share a unit's pieces.
+  const int64_t units = (int64_t)a.num_seqs * a.num_kv_heads * a.head_groups;
+  const unsigned fixup_ctas = (unsigned)((sa.num_warps + 3) / 4);
+  if ((int64_t)sa.num_warps > kFixupCtaPiecesPerUnit * units)
+    return launch_pdl(decode_stream_fixup_cta_kernel<T, D>, dim3(fixup_ctas), dim3(kFixupWarps * 32), 0, stream, a,
+                      sa);
+  return launch_pdl(decode_stream_fixup_kernel<T, D>, dim3(fixup_ctas), dim3(128), 0, stream, a, sa);
 }
 
 cudaError_t launch_decode_stream(const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a,
