@@ -161,8 +161,8 @@ decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
     t = off - k * ut;
   };
   // All lanes: resolve the pool rows of tiles [j0, j0 + kStreamRowBatch) of this range.
-  auto fill_rows = [&](int j0) {
-    for (int i = lane; i < kStreamRowBatch; i += 32) {
+  auto fill_rows = [&](int j0, int i0 = 0) {
+    for (int i = i0 + lane; i < kStreamRowBatch; i += 32) {
       const int j = j0 + i;
       int row = -1;
       if (j < n) {
@@ -201,7 +201,25 @@ decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
     }
   };
 
-  fill_rows(0);
+  // The first 32 block ids only: the first loads are issued before the rest of
+  // the batch is resolved (below).
+  for (int j = lane; j < 32; j += 32) {
+    int row = -1;
+    if (j < n) {
+      int s, k, t;
+      locate(r0 + j, s, k, t);
+      const int kvh = k / a.head_groups;
+      const int tok = t * kTile;
+      const int bi = tok / a.block_size;
+      const int64_t b = __ldg(a.bt + (int64_t)s * a.bt_s0 + bi);
+      if (b >= 0 && b < a.num_blocks)
+        row = ((int)b * a.num_kv_heads + kvh) * a.block_size + (tok - bi * a.block_size);
+      else
+        atomicOr(a.err, MVB_DEV_BLOCK_ID);
+    }
+    myrows[j] = row;
+  }
+  __syncwarp();
 
   const int g0 = lane >> 2, qd = lane & 3;
   uint32_t qa[KC][4], qa_next[KC][4];
@@ -270,6 +288,7 @@ decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
     const int n0 = n < STAGES ? n : STAGES;
     for (int j = 0; j < n0; ++j) issue(j);
   }
+  fill_rows(0, 32);  // the rest of the first batch, while the first loads are in flight
   bool failed = false;
   int j = 0;
   for (; j < n; ++j) {
