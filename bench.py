@@ -68,10 +68,11 @@ def parse_args():
     p.add_argument("--e2e-steps", type=int, default=2000)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--seed", type=int, default=0)
-    p.add_argument("--op", choices=["step", "gather", "rope_write"], default="step",
+    p.add_argument("--op", choices=["step", "gather", "rope_write", "metadata"], default="step",
                    help="step: the decode step (the headline); gather: the prefill prefix gather "
                         "(mvb_paged_gather) of every config-2 context; rope_write: the fused RoPE + "
-                        "KV write (mvb_rope_kv_cache_write) of an 8192-token prefill chunk")
+                        "KV write (mvb_rope_kv_cache_write) of an 8192-token prefill chunk; metadata: "
+                        "the per-step attention metadata of a config-2 decode step (StepMetadataBuilder)")
     return p.parse_args()
 
 
@@ -749,8 +750,73 @@ def rope_write_op(args):
     }), flush=True)
 
 
+def metadata_op(args):
+    """Secondary measurement: StepMetadataBuilder.build for one config-2 decode
+    step (256 sequences, ctx U[128,2048], block 16: positions, slot mapping,
+    padded block tables, kv_len_after, sample indices) — host time per step
+    including the upload and the launch, the device work drained at the end.
+    The CPU line is the oracle's restatement of ModelInputBuilder's per-token
+    loops on the same step."""
+    import torch
+
+    import mini_vllm_b200 as M
+    from mini_vllm_b200 import workloads as W
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    spec = W.make_spec(2, seed=args.seed)
+    decode = [([int(b) for b in row if b >= 0], int(c) - 1) for row, c in zip(spec.block_tables, spec.context_lens)]
+    builder = M.StepMetadataBuilder(spec.block_size, dev)
+    md = builder.build([], decode)  # correctness gate: slots equal the workload's
+    assert np.array_equal(md.slot_mapping.cpu().numpy(), spec.slot_mapping)
+    for _ in range(max(3, args.warmup)):
+        builder.build([], decode, strict=False)
+    torch.cuda.synchronize()
+    n = max(10, min(args.steps, 2000))
+    t0 = time.perf_counter()
+    for _ in range(n):
+        builder.build([], decode, strict=False)
+    torch.cuda.synchronize()
+    sec = (time.perf_counter() - t0) / n
+    import oracle
+
+    lists = [d[0] for d in decode]
+    t0 = time.perf_counter()
+    reps = 0
+    while reps < 3 or time.perf_counter() - t0 < 2.0:
+        oracle.step_metadata_numpy(lists, [d[1] for d in decode], [1] * len(decode), [], 0, spec.block_size)
+        reps += 1
+    cpu_sec = (time.perf_counter() - t0) / reps
+    # the padded-table entry point (an engine that keeps its tables as arrays)
+    tables = spec.block_tables
+    counts = (tables >= 0).sum(axis=1)
+    cached = spec.context_lens.astype(np.int64) - 1
+    ones = np.ones(len(decode), dtype=np.int64)
+    for _ in range(max(3, args.warmup)):
+        builder.build_from_arrays(tables, counts, cached, ones, [], 0, strict=False)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(n):
+        builder.build_from_arrays(tables, counts, cached, ones, [], 0, strict=False)
+    torch.cuda.synchronize()
+    sec_arrays = (time.perf_counter() - t0) / n
+    print(json.dumps({
+        "metric": "per-step attention metadata build, us/step (config-2 decode step)", "value": round(sec * 1e6, 2),
+        "from_arrays_us": round(sec_arrays * 1e6, 2),
+        "unit": "us", "n_gpus": 1, "steps": n, "warmup": max(3, args.warmup), "higher_is_better": False,
+        "vs_baseline": None, "data": "synthetic",
+        "config": {"workload": "metadata: 256 decode sequences, ctx U[128,2048], block 16",
+                   "blocks": int(sum(len(x) for x in lists)), "timing": "host perf_counter over K builds, one sync"},
+        "cpu_baseline": {"value": round(cpu_sec * 1e6, 1), "unit": "us", "cores": 1, "kind": "port",
+                         "sample": "oracle restatement of ModelInputBuilder's per-token loops, same step"},
+    }), flush=True)
+
+
 def main():
     args = parse_args()
+    if args.op == "metadata":
+        metadata_op(args)
+        return
     if args.op == "gather":
         gather_op(args)
         return

@@ -117,6 +117,24 @@ int mvb_rope_kv_cache_write(const void* query, int64_t q_stride_token, int64_t q
                             uint32_t* slot_claims, uint32_t epoch, int32_t* error_flags,
                             void* stream);
 
+/* The per-step attention metadata on the device, for a step of num_seqs
+ * sequences (prefill chunks first, then decodes): replaces the per-token host
+ * loops of ModelInputBuilder.build (mini_vllm/engine/input_builder.py:48-196).
+ * Inputs (device, int64): sequence s's block table B_s is
+ * blocks[block_starts[s] .. block_starts[s] + block_counts[s]) (the lists
+ * concatenated, or the rows of a padded table); cached_len [S] =
+ * cached_len_before; token_offsets [S + 1] the exclusive prefix of the query
+ * lengths q_s.  Outputs (device): positions [T] = c_s + i; slot_mapping [T] =
+ * B_s[p / BS] * BS + p % BS (input_builder.py:202-221); block_tables
+ * [S, max_blocks] int64, B_s then -1 padding (input_builder.py:238-256);
+ * kv_len_after [S] int32 = c_s + q_s.  A position past B_s sets
+ * MVB_DEV_TABLE_SHORT (the reference's "Block not allocated") and gets slot -1. */
+int mvb_build_step_metadata(const int64_t* blocks, const int64_t* block_starts, const int64_t* block_counts,
+                            const int64_t* cached_len, const int64_t* token_offsets, int32_t num_seqs,
+                            int64_t num_tokens, int32_t max_blocks, int32_t block_size, int64_t* positions,
+                            int64_t* slot_mapping, int64_t* block_tables, int32_t* kv_len_after,
+                            int32_t* error_flags, void* stream);
+
 /* Flag ORed into `variant` of mvb_paged_decode (ignored by the plan): the
  * kernel launched immediately before this call on `stream` is
  * mvb_kv_cache_write (or a kernel that signals its dependents only when it

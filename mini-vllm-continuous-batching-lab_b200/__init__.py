@@ -24,6 +24,7 @@ from .attention import (
     triton_decode_attention,
 )
 from .cache import KVCachePool, compute_num_gpu_blocks
+from .engine import StepMetadata, StepMetadataBuilder
 from .model_runner import AttentionGroup, AttentionMetadata, ModelConfig
 
 __version__ = "0.1.0"
@@ -36,6 +37,8 @@ __all__ = [
     "AttentionMetadata",
     "KVCachePool",
     "ModelConfig",
+    "StepMetadata",
+    "StepMetadataBuilder",
     "check_device_errors",
     "compute_num_gpu_blocks",
     "decode_plan",

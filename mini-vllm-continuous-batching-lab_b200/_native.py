@@ -81,6 +81,10 @@ SIGNATURES = {
         [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64,
          _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _u32, _vp, _vp],
     ),
+    "mvb_build_step_metadata": (
+        _i32,
+        [_vp, _vp, _vp, _vp, _vp, _i32, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp],
+    ),
     "mvb_paged_decode_noalloc": (
         _i32,
         [_vp, _i64, _i64, _vp, _vp, _vp, _i64, _i32, _vp, _vp, _i64, _i64,

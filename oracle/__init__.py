@@ -21,5 +21,6 @@ from .oracle import (  # noqa: F401
     max_threads,
     rope_numpy,
     round_to_dtype,
+    step_metadata_numpy,
     to_float32,
 )

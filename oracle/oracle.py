@@ -21,6 +21,8 @@ Reference lines restated:
                   (AttentionBackendRef.decode_attention; torch SDPA math)
   rope_numpy   <- mini_vllm/model/rotary.py:47-85 (RotaryEmbedding.__call__,
                   _rotate_half), with the rounding of each torch operation
+  step_metadata_numpy <- mini_vllm/engine/input_builder.py:48-256
+                  (positions, _compute_slot, _build_block_table_tensor, sample indices)
 """
 
 from __future__ import annotations
@@ -246,3 +248,44 @@ def rope_numpy(x, positions, cos, sin, dtype: str) -> np.ndarray:
     a = round_to_dtype(xf * c, dtype)
     b = round_to_dtype(rot * sn, dtype)
     return from_float32(round_to_dtype(a + b, dtype), dtype)
+
+
+# ---------------------------------------------------------------------------
+# step metadata (numpy restatement)
+# ---------------------------------------------------------------------------
+def step_metadata_numpy(block_lists, cached, query_len, completes, num_prefill: int, block_size: int):
+    """positions, slot_mapping, prefill / decode block tables (-1 padded to the
+    step's longest table, at least 1; (0, 0) for an empty phase), sample token
+    indices and kv_len_after of one step, sequences prefill first
+    (input_builder.py:48-256).  Raises RuntimeError("Block not allocated ...")
+    for a position past a sequence's blocks, as _compute_slot does."""
+    S = len(block_lists)
+    positions, slots, sample = [], [], []
+    tok = 0
+    for s in range(S):
+        blocks = list(block_lists[s])
+        for i in range(int(query_len[s])):
+            pos = int(cached[s]) + i
+            lb = pos // block_size
+            if lb >= len(blocks):
+                raise RuntimeError(f"Block not allocated for position={pos} (logical_idx={lb}, "
+                                   f"num_blocks={len(blocks)})")
+            positions.append(pos)
+            slots.append(blocks[lb] * block_size + pos % block_size)
+        if s < num_prefill:
+            if completes[s]:
+                sample.append(tok + int(query_len[s]) - 1)
+        else:
+            sample.append(tok)
+        tok += int(query_len[s])
+    max_blocks = max(1, max((len(b) for b in block_lists), default=0))
+
+    def table(rows):
+        if not rows:
+            return np.zeros((0, 0), dtype=np.int64)
+        return np.array([list(b) + [-1] * (max_blocks - len(b)) for b in rows], dtype=np.int64)
+
+    kv_len = np.array([int(c) + int(q) for c, q in zip(cached, query_len)], dtype=np.int64)
+    return (np.array(positions, dtype=np.int64), np.array(slots, dtype=np.int64),
+            table(block_lists[:num_prefill]), table(block_lists[num_prefill:]),
+            np.array(sample, dtype=np.int64), kv_len)

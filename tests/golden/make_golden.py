@@ -222,6 +222,18 @@ def case_list() -> List[Dict]:
     r("r_small_f32", "f32", 5, 4, 2, 64, 1e6, 64, 4, 4, 42, skip=[0])
     r("r_far_pos_bf16", "bf16", 9, 4, 1, 64, 1e6, 32768, 4, 16, 43, pos_min=30000)
     r("r_d32_bf16", "bf16", 3, 2, 1, 32, 1e4, 128, 2, 4, 44)
+
+    def m(name, bs, nblocks, chunk, prefill, decode, seed):
+        cases.append(dict(kind="metadata", name=name, dtype="i64", block_size=bs, num_gpu_blocks=nblocks,
+                          chunk=chunk, prefill=prefill, decode=decode, seed=seed))
+
+    # ModelInputBuilder.build steps: (prompt_len, prefill_cursor) / (prompt_len, generated)
+    m("m_mixed_bs4", 4, 64, 4, [[10, 0], [10, 4], [9, 8]], [[6, 1], [7, 2], [9, 3], [5, 1]], 50)
+    m("m_chunked_bs16", 16, 256, 128, [[300, 64], [40, 0]], [[100, 5], [16, 1]], 51)
+    m("m_decode32_bs16", 16, 2048, 64, [], [[int(x), int(g)] for x, g in
+                                              zip(np.random.default_rng(52).integers(100, 900, 32),
+                                                  np.random.default_rng(53).integers(1, 40, 32))], 52)
+    m("m_prefill_only_bs8", 8, 128, 32, [[70, 0], [70, 32]], [], 53)
     return cases
 
 
@@ -236,7 +248,14 @@ def main(ref_root: str) -> None:
     from mini_vllm.cache.cache_read import gather_paged_kv
     from mini_vllm.cache.cache_write import write_to_paged_cache
     from mini_vllm.cache.pool import KVCachePool
+    from mini_vllm.cache.allocator import BlockAllocator
+    from mini_vllm.cache.manager import BlockManager
+    from mini_vllm.config import Config
+    from mini_vllm.engine.input_builder import ModelInputBuilder
     from mini_vllm.model.rotary import RotaryEmbedding
+    from mini_vllm.sequence.sampling_params import SamplingParams
+    from mini_vllm.sequence.sequence import Sequence
+    from mini_vllm.sequence.status import Status
     from mini_vllm.model_runner.base import AttentionGroup, AttentionMetadata, ModelConfig
 
     def to_torch(a: np.ndarray, dtype: str) -> torch.Tensor:
@@ -282,6 +301,54 @@ def main(ref_root: str) -> None:
             if rows_k:
                 arrays[f"{name}/rows_k"] = np.stack(rows_k)
                 arrays[f"{name}/rows_v"] = np.stack(rows_v)
+        elif c["kind"] == "metadata":
+            rng = np.random.default_rng(c["seed"])
+            cfg = Config(block_size=c["block_size"], num_gpu_blocks=c["num_gpu_blocks"],
+                         max_prefill_chunk_size=c["chunk"], max_num_seqs=1024, max_num_batched_tokens=1 << 20,
+                         vocab_size=1 << 16, device="cpu")
+            mgr = BlockManager(c["block_size"], BlockAllocator(num_blocks=c["num_gpu_blocks"]))
+            seqs_p, seqs_d = [], []
+            for i, (plen, cursor) in enumerate(c["prefill"]):
+                sq = Sequence(f"p{i}", f"gp{i}", rng.integers(0, 1 << 16, plen).tolist(),
+                              SamplingParams(max_tokens=1 << 12), 0.0)
+                sq.prefill_cursor = cursor
+                sq.status = Status.PREFILL
+                seqs_p.append(sq)
+            for i, (plen, gen) in enumerate(c["decode"]):
+                sq = Sequence(f"d{i}", f"gd{i}", rng.integers(0, 1 << 16, plen).tolist(),
+                              SamplingParams(max_tokens=1 << 12), 0.0)
+                sq.prefill_cursor = plen
+                sq.status = Status.RUNNING
+                sq.output_token_ids = [7] * gen
+                sq.num_generated_tokens = gen
+                seqs_d.append(sq)
+            # positions each sequence needs blocks for, allocated position-major so that
+            # the sequences' blocks interleave in the pool
+            need = [min(len(sq.prompt_token_ids), sq.prefill_cursor + c["chunk"]) for sq in seqs_p] + \
+                   [len(sq.prompt_token_ids) + sq.num_generated_tokens for sq in seqs_d]
+            for sq in seqs_p + seqs_d:
+                mgr.allocate_for_seq(sq)
+            for pos in range(max(need, default=0)):
+                for sq, n in zip(seqs_p + seqs_d, need):
+                    if pos < n:
+                        mgr.ensure_block(sq, pos)
+            mi = ModelInputBuilder(mgr, cfg).build(seqs_p, seqs_d)
+            c["block_lists"] = [mgr.get_block_table(sq.seq_id) for sq in seqs_p + seqs_d]
+            groups = {g.attention_type: g for g in mi.attn_metadata.groups}
+            c["cached"] = [int(x) for g in mi.attn_metadata.groups for x in g.cached_len_before.tolist()]
+            c["query_len"] = [int(x) for g in mi.attn_metadata.groups for x in g.query_len.tolist()]
+            c["completes"] = [sq.prefill_cursor + min(c["chunk"], len(sq.prompt_token_ids) - sq.prefill_cursor)
+                              >= len(sq.prompt_token_ids) for sq in seqs_p]
+            assert [g.attention_type for g in mi.attn_metadata.groups] == \
+                (["prefill_gpu"] if seqs_p else []) + (["decode_gpu"] if seqs_d else []), groups.keys()
+            arrays[f"{name}/positions"] = mi.positions.numpy()
+            arrays[f"{name}/slot_mapping"] = mi.slot_mapping.numpy()
+            arrays[f"{name}/prefill_block_tables"] = mi.attn_metadata.prefill_block_tables.numpy()
+            arrays[f"{name}/decode_block_tables"] = mi.attn_metadata.decode_block_tables.numpy()
+            arrays[f"{name}/sample_token_indices"] = mi.sample_token_indices.numpy()
+            arrays[f"{name}/kv_len_after"] = np.concatenate(
+                [g.kv_len_after.numpy() for g in mi.attn_metadata.groups]) if mi.attn_metadata.groups \
+                else np.zeros(0, np.int64)
         elif c["kind"] == "rope":
             x = rope_inputs(c)
             c["inputs_sha256"] = sha(x["q"], x["k"], x["v"], x["kc0"], x["vc0"], x["positions"], x["slots"])

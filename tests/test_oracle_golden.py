@@ -24,7 +24,7 @@ def _cases(golden, kind):
 def test_golden_fixture_covers_all_kinds(golden):
     cases, _ = golden
     kinds = {c["kind"] for c in cases}
-    assert kinds == {"write", "write_spec", "gather", "decode", "decode_spec", "rope"}
+    assert kinds == {"write", "write_spec", "gather", "decode", "decode_spec", "rope", "metadata"}
     assert len(cases) >= 60
 
 
@@ -150,3 +150,19 @@ def test_rope_tables_and_oracle_rope_write_bit_exact(golden):
         kc, vc = x["kc0"].copy(), x["vc0"].copy()
         oracle.cache_write(k_rot, x["v"], kc, vc, x["slots"], c["block_size"], dt)
         assert MG.sha(kc, vc) == c["result_sha256"], c["name"]
+
+
+def test_oracle_step_metadata_matches_reference_builder(golden):
+    """The numpy restatement of ModelInputBuilder.build reproduces the
+    reference's positions, slot mapping, padded tables, sample indices and
+    kv_len_after for every golden step."""
+    cases, arrays = _cases(golden, "metadata")
+    assert len(cases) >= 4
+    for c in cases:
+        P = len(c["prefill"])
+        out = oracle.step_metadata_numpy(c["block_lists"], c["cached"], c["query_len"], c["completes"], P,
+                                         c["block_size"])
+        for got, key in zip(out, ["positions", "slot_mapping", "prefill_block_tables", "decode_block_tables",
+                                  "sample_token_indices", "kv_len_after"]):
+            ref = arrays[f"{c['name']}/{key}"]
+            assert got.shape == ref.shape and np.array_equal(got, ref), (c["name"], key)
