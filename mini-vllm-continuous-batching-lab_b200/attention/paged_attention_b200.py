@@ -826,7 +826,10 @@ class AttentionBackendB200(AttentionBackend):
             self._last_write = (layer_idx, _stream_handle(key.get_device()))
 
     def decode_attention(self, layer_idx: int, query: torch.Tensor, attn_metadata: Any,
-                         pool: Any) -> torch.Tensor:
+                         pool: Any, *, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """The reference method (backend.py:63-77); ``out=`` (an extension) lets
+        a runner decode straight into its ``attn_out[num_prefill:]`` slice
+        instead of allocating and copying (qwen_runner.py:173-190)."""
         last, self._last_write = self._last_write, None  # only the very next decode may overlap
         if query.shape[0] == 0:
             return query
@@ -837,7 +840,7 @@ class AttentionBackendB200(AttentionBackend):
         return paged_decode_attention(
             query, pool.key_caches[layer_idx], pool.value_caches[layer_idx],
             attn_metadata.decode_block_tables, group.kv_len_after, pool.block_size,
-            variant=self.decode_variant, partition_tokens=self.partition_tokens,
+            out=out, variant=self.decode_variant, partition_tokens=self.partition_tokens,
             strict=self.strict, after_write=after,
         )
 

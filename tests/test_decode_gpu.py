@@ -439,3 +439,24 @@ def test_backend_overlap_after_write_only_for_the_adjacent_decode():
     M.check_device_errors()
     assert_close(a, ref, "bf16", "adjacent")
     assert torch.equal(a, b)
+
+
+def test_backend_decode_into_runner_slice():
+    """decode_attention(out=attn_out[num_prefill:]) writes the decode rows in
+    place (no allocation, no slice copy) with the same bits as the returning
+    form."""
+    spec = W.make_spec(2, seed=12, num_seqs=48)
+    t = W.torch_tensors(spec, torch.bfloat16, DEV)
+    backend = M.AttentionBackendB200(M.ModelConfig(num_heads=14, num_kv_heads=2, head_dim=64))
+    pool = M.KVCachePool([t["key_caches"][0]], [t["value_caches"][0]], spec.num_blocks, 16, 1, 2, 64,
+                         torch.device(DEV), torch.bfloat16)
+    backend._pool = pool
+    group = M.AttentionGroup(seq_indices=list(range(spec.num_seqs)), attention_type="decode_gpu",
+                             cached_len_before=None, query_len=None, kv_len_after=t["kv_len"])
+    meta = M.AttentionMetadata(groups=[group], decode_block_tables=t["block_tables"], block_size=16,
+                               num_kv_heads=2, head_dim=64)
+    ref = backend.decode_attention(0, t["query"], meta, pool)
+    attn_out = torch.full((5 + spec.num_seqs, 14, 64), 7.0, dtype=torch.bfloat16, device=DEV)
+    res = backend.decode_attention(0, t["query"], meta, pool, out=attn_out[5:])
+    assert res.data_ptr() == attn_out[5:].data_ptr()
+    assert torch.equal(attn_out[5:], ref) and (attn_out[:5] == 7.0).all()
