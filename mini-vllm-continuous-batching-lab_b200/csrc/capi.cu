@@ -275,6 +275,7 @@ int mvb_kv_cache_write(const void* key, int64_t key_stride_token, int64_t key_st
                        int32_t num_tokens, int32_t num_kv_heads, int32_t head_dim,
                        int32_t block_size, int32_t num_blocks, int32_t dtype,
                        uint32_t* slot_claims, uint32_t epoch, int32_t* error_flags, void* stream) {
+  mvb::NvtxRange nvtx_range("mvb_kv_cache_write");
   if (dtype != MVB_DTYPE_F32 && dtype != MVB_DTYPE_F16 && dtype != MVB_DTYPE_BF16)
     return MVB_ERR_DTYPE;
   if (block_size <= 0) return MVB_ERR_BLOCK_SIZE;
@@ -323,6 +324,7 @@ int mvb_paged_decode(const void* query, int64_t q_stride_seq, int64_t q_stride_h
                      int32_t num_blocks, float scale, int32_t dtype, int32_t variant,
                      int32_t partition_tokens, void* workspace, int64_t workspace_bytes,
                      int32_t* error_flags, void* stream) {
+  mvb::NvtxRange nvtx_range("mvb_paged_decode");
   Plan pl;
   const bool after_write = (variant & MVB_DECODE_AFTER_WRITE) != 0;
   variant &= ~MVB_DECODE_AFTER_WRITE;

@@ -53,6 +53,7 @@ extern "C" int mvb_paged_decode_noalloc(
     int64_t out_stride_head, int32_t num_seqs, int32_t num_heads, int32_t num_kv_heads,
     int32_t head_dim, int32_t block_size, int32_t num_blocks, float scale, int32_t dtype,
     int32_t variant, int32_t partition_tokens, int32_t* error_flags, void* stream) {
+  mvb::NvtxRange nvtx_range("mvb_paged_decode_noalloc");
   // The split-K family only: tensor-core kernel when eligible, else CUDA cores.
   variant &= ~MVB_DECODE_AFTER_WRITE;  // the split-K kernels read every input after the wait
   if (variant == MVB_DECODE_STREAM) return MVB_ERR_VARIANT;

@@ -157,6 +157,7 @@ extern "C" int mvb_paged_gather(const void* key_cache, const void* value_cache, 
                                 const int64_t* out_offsets, void* key_out, void* value_out, int32_t num_seqs,
                                 int64_t total_tokens, int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
                                 int32_t num_blocks, int32_t dtype, int32_t* error_flags, void* stream) {
+  mvb::NvtxRange nvtx_range("mvb_paged_gather");
   if (dtype != MVB_DTYPE_F32 && dtype != MVB_DTYPE_F16 && dtype != MVB_DTYPE_BF16) return MVB_ERR_DTYPE;
   if (head_dim <= 0) return MVB_ERR_HEAD_DIM;
   if (block_size <= 0) return MVB_ERR_BLOCK_SIZE;

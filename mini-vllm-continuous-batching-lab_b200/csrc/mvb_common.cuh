@@ -14,7 +14,9 @@
 #include <mutex>
 #include <utility>
 
-#include "mini_vllm_b200.h"  // include/ (the build passes -I include)
+#include "mini_vllm_b200.h"
+
+#include <nvtx3/nvToolsExt.h>  // include/ (the build passes -I include)
 
 namespace mvb {
 
@@ -99,6 +101,15 @@ __device__ __forceinline__ void fence_mbar_init() {
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+
+// NVTX range over one C-ABI call (its launches and host work), visible in a
+// profiler's timeline; without a profiler attached a push / pop costs a few ns.
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
 
 // Programmatic dependent launch.  A kernel launched with the programmatic
 // stream-serialization attribute may start while the previous kernel in the

@@ -190,6 +190,7 @@ extern "C" int mvb_rope_kv_cache_write(
     void* key_cache, void* value_cache, const int64_t* slot_mapping, void* key_out, int32_t num_tokens,
     int32_t num_heads, int32_t num_kv_heads, int32_t head_dim, int32_t block_size, int32_t num_blocks,
     int32_t dtype, uint32_t* slot_claims, uint32_t epoch, int32_t* error_flags, void* stream) {
+  mvb::NvtxRange nvtx_range("mvb_rope_kv_cache_write");
   if (dtype != MVB_DTYPE_F32 && dtype != MVB_DTYPE_F16 && dtype != MVB_DTYPE_BF16) return MVB_ERR_DTYPE;
   if (head_dim <= 0 || head_dim % 2 != 0) return MVB_ERR_HEAD_DIM;
   if (block_size <= 0) return MVB_ERR_BLOCK_SIZE;

@@ -86,6 +86,7 @@ extern "C" int mvb_build_step_metadata(const int64_t* blocks, const int64_t* blo
                                        int32_t block_size, int64_t* positions, int64_t* slot_mapping,
                                        int64_t* block_tables, int32_t* kv_len_after, int32_t* error_flags,
                                        void* stream) {
+  mvb::NvtxRange nvtx_range("mvb_build_step_metadata");
   if (block_size <= 0) return MVB_ERR_BLOCK_SIZE;
   if (num_seqs < 0 || num_tokens < 0 || max_blocks < 0) return MVB_ERR_INVALID_ARG;
   if (num_seqs == 0) return MVB_OK;
