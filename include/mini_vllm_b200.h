@@ -135,6 +135,23 @@ int mvb_build_step_metadata(const int64_t* blocks, const int64_t* block_starts, 
                             int64_t* slot_mapping, int64_t* block_tables, int32_t* kv_len_after,
                             int32_t* error_flags, void* stream);
 
+/* Test hook of the bounded waits — no reference counterpart.  Runs
+ * mvb_paged_decode with MVB_DECODE_STREAM, except that the load of local tile
+ * `hold_tile` of stream warp `hold_warp` is never issued and every pipeline
+ * wait gives up after `wait_limit` (1 .. 2^22) try-waits: that warp's wait
+ * runs out, it reports MVB_DEV_TIMEOUT, waits (bounded) for its own loads in
+ * flight and leaves; every other warp finishes normally and the context stays
+ * usable.  Used by the failure-detection test; never needed in production. */
+int mvb_test_decode_wait_timeout(const void* query, int64_t q_stride_seq, int64_t q_stride_head,
+                                 const void* key_cache, const void* value_cache,
+                                 const int64_t* block_table, int64_t block_table_stride,
+                                 int32_t max_blocks_per_seq, const int32_t* kv_len, void* out,
+                                 int64_t out_stride_seq, int64_t out_stride_head, int32_t num_seqs,
+                                 int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+                                 int32_t block_size, int32_t num_blocks, float scale, int32_t dtype,
+                                 void* workspace, int64_t workspace_bytes, int32_t* error_flags,
+                                 void* stream, int32_t hold_warp, int32_t hold_tile, int32_t wait_limit);
+
 /* Flag ORed into `variant` of mvb_paged_decode (ignored by the plan): the
  * kernel launched immediately before this call on `stream` is
  * mvb_kv_cache_write (or a kernel that signals its dependents only when it

@@ -85,6 +85,11 @@ SIGNATURES = {
         _i32,
         [_vp, _vp, _vp, _vp, _vp, _i32, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp],
     ),
+    "mvb_test_decode_wait_timeout": (
+        _i32,
+        [_vp, _i64, _i64, _vp, _vp, _vp, _i64, _i32, _vp, _vp, _i64, _i64,
+         _i32, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _vp, _i64, _vp, _vp, _i32, _i32, _i32],
+    ),
     "mvb_paged_decode_noalloc": (
         _i32,
         [_vp, _i64, _i64, _vp, _vp, _vp, _i64, _i32, _vp, _vp, _i64, _i64,

@@ -243,6 +243,10 @@ bool pool_tensor_map(const void* base, int64_t rows, int head_dim, int dtype, CU
 
 bool aligned_to(const void* p, int64_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// Bounded-wait test hook (mvb_test_decode_wait_timeout); thread-local so a
+// test call on one thread never reaches another thread's launches.
+thread_local int g_hold_warp = -1, g_hold_tile = -1, g_wait_limit = kWaitSpinLimit;
+
 }  // namespace
 }  // namespace mvb
 
@@ -379,6 +383,9 @@ int mvb_paged_decode(const void* query, int64_t q_stride_seq, int64_t q_stride_h
   a.part_l = pl.num_parts > 1 ? reinterpret_cast<float*>(ws + pl.off_l) : nullptr;
   a.err = error_flags;
   a.early_inputs = after_write ? 1 : 0;  // honoured by the stream kernel
+  a.hold_warp = g_hold_warp;
+  a.hold_tile = g_hold_tile;
+  a.wait_limit = g_wait_limit;
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e;
@@ -412,3 +419,25 @@ int mvb_paged_decode(const void* query, int64_t q_stride_seq, int64_t q_stride_h
 }
 
 }  // extern "C"
+
+extern "C" int mvb_test_decode_wait_timeout(
+    const void* query, int64_t q_stride_seq, int64_t q_stride_head, const void* key_cache,
+    const void* value_cache, const int64_t* block_table, int64_t block_table_stride, int32_t max_blocks_per_seq,
+    const int32_t* kv_len, void* out, int64_t out_stride_seq, int64_t out_stride_head, int32_t num_seqs,
+    int32_t num_heads, int32_t num_kv_heads, int32_t head_dim, int32_t block_size, int32_t num_blocks,
+    float scale, int32_t dtype, void* workspace, int64_t workspace_bytes, int32_t* error_flags, void* stream,
+    int32_t hold_warp, int32_t hold_tile, int32_t wait_limit) {
+  if (hold_warp < 0 || hold_tile < 0 || wait_limit <= 0 || wait_limit > kWaitSpinLimit) return MVB_ERR_INVALID_ARG;
+  g_hold_warp = hold_warp;
+  g_hold_tile = hold_tile;
+  g_wait_limit = wait_limit;
+  const int st = mvb_paged_decode(query, q_stride_seq, q_stride_head, key_cache, value_cache, block_table,
+                                  block_table_stride, max_blocks_per_seq, kv_len, out, out_stride_seq,
+                                  out_stride_head, num_seqs, num_heads, num_kv_heads, head_dim, block_size,
+                                  num_blocks, scale, dtype, MVB_DECODE_STREAM, 0, workspace, workspace_bytes,
+                                  error_flags, stream);
+  g_hold_warp = -1;
+  g_hold_tile = -1;
+  g_wait_limit = kWaitSpinLimit;
+  return st;
+}

@@ -188,6 +188,7 @@ decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
     const uint32_t bar = smem_u32(mybars + st);
     const int row = myrows[j % kStreamRowBatch];
     myok[st] = row >= 0;
+    if (W == a.hold_warp && j == a.hold_tile) return;  // test hook: the stage never completes
     if (row < 0) {
       mbar_arrive(bar);
       return;
@@ -317,7 +318,7 @@ decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
       lrow[0] = lrow[1] = 0.f;
     }
     const int st = j % STAGES;
-    const bool got = mbar_wait_bounded(smem_u32(mybars + st), (uint32_t)((j / STAGES) & 1));
+    const bool got = mbar_wait_bounded(smem_u32(mybars + st), (uint32_t)((j / STAGES) & 1), a.wait_limit);
     if (__any_sync(0xffffffffu, !got)) {
       failed = true;
       break;
@@ -340,7 +341,7 @@ decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
     if (lane == 0) atomicOr(a.err, MVB_DEV_TIMEOUT);
     const int issued = min(n, j + STAGES);
     for (int jj = j; jj < issued; ++jj)
-      mbar_wait_bounded(smem_u32(mybars + jj % STAGES), (uint32_t)((jj / STAGES) & 1));
+      mbar_wait_bounded(smem_u32(mybars + jj % STAGES), (uint32_t)((jj / STAGES) & 1), a.wait_limit);
     if (lane == 0) sa.desc[2 * W] = make_int4(-1, 0, 0, 0);
     return;  // the unit's output stays unwritten; the error flag reports it
   }

@@ -49,6 +49,12 @@ struct DecodeArgs {
   float* part_l;     // [num_seqs][num_heads][num_parts] sum of exp2(x - m)
   int* err;
   int early_inputs;  // read query / block table / kv_len before the grid-dependency wait
+  // Test hook of the bounded waits (stream kernel): the load of local tile
+  // `hold_tile` of warp `hold_warp` is never issued, so that warp's wait on it
+  // runs out after `wait_limit` try-waits and reports MVB_DEV_TIMEOUT.
+  // Production calls: hold_warp = -1, wait_limit = kWaitSpinLimit.
+  int hold_warp, hold_tile;
+  int wait_limit;
 };
 
 // ---------------------------------------------------------------------------
@@ -145,8 +151,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Bounded wait on one phase of an mbarrier; false when the bound ran out.
-__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
-  for (int i = 0; i < kWaitSpinLimit; ++i)
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, int limit = kWaitSpinLimit) {
+  for (int i = 0; i < limit; ++i)
     if (mbar_try_wait(bar, parity)) return true;
   return false;
 }
