@@ -256,9 +256,10 @@ int mvb_paged_decode(const void* query, int64_t q_stride_seq, int64_t q_stride_h
  * or allocating library routine.  Every GPU that loads the library holds the
  * array until exit; the first call on a device looks up its address
  * (cudaGetSymbolAddress), so make that first call before any stream capture.
- * All calls share the one array: calls that overlap on the GPU (different
- * streams, or devices sharing nothing else) race on it and must be ordered
- * by the caller.
+ * All calls on one device share that device's copy of the array and find the
+ * previous call's contents there: calls that overlap on the same GPU (for
+ * example on two streams) race on it and must be ordered by the caller.
+ * Each device has its own copy, so calls on different devices do not race.
  */
 int mvb_paged_decode_noalloc(const void* query, int64_t q_stride_seq, int64_t q_stride_head,
                              const void* key_cache, const void* value_cache,
