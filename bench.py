@@ -626,16 +626,20 @@ def gather_op(args):
     # CPU baseline: the oracle's gather (the reference's gather_paged_kv restated), one sequence at a time
     import oracle
 
-    kc_np, vc_np = to_np_bf16(kcs[0]), to_np_bf16(vcs[0])
-    t0 = time.perf_counter()
-    n_cpu = 0
-    for i in range(spec.num_seqs):
-        oracle.gather(kc_np, vc_np, spec.block_tables[i], ctx[i], spec.block_size, "bf16")
-        n_cpu += ctx[i]
-        if time.perf_counter() - t0 > 10:
-            break
-    cpu_sec = time.perf_counter() - t0
-    cpu_gbs = 4 * n_cpu * spec.num_kv_heads * spec.head_dim * 2 / cpu_sec / 1e9
+    cpu_baseline = None
+    if not args.no_cpu_baseline:
+        kc_np, vc_np = to_np_bf16(kcs[0]), to_np_bf16(vcs[0])
+        t0 = time.perf_counter()
+        n_cpu = 0
+        for i in range(spec.num_seqs):
+            oracle.gather(kc_np, vc_np, spec.block_tables[i], ctx[i], spec.block_size, "bf16")
+            n_cpu += ctx[i]
+            if time.perf_counter() - t0 > 10:
+                break
+        cpu_sec = time.perf_counter() - t0
+        cpu_gbs = 4 * n_cpu * spec.num_kv_heads * spec.head_dim * 2 / cpu_sec / 1e9
+        cpu_baseline = {"value": round(cpu_gbs, 3), "unit": "GB/s", "cores": 1, "kind": "port",
+                        "sample": f"oracle gather of {n_cpu} tokens, one sequence at a time"}
     print(json.dumps({
         "metric": "paged gather GB/s (prefill prefix read of every config-2 context)", "value": round(nbytes / sec / 1e9, 2),
         "unit": "GB/s", "n_gpus": 1, "steps": replays * L, "warmup": warm * L, "ms_per_step": round(sec * 1e3, 5),
@@ -645,10 +649,8 @@ def gather_op(args):
                    "timing": "CUDA graph of L launches, CUDA events"},
         "roofline": {"bound": "hbm", "achieved": round(nbytes / mean / 1e9, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(nbytes / mean / 1e9 / peak, 4), "traffic": None, "peak_kind": peak_kind,
-                     "kernel": "paged_gather_kernel", "bytes_per_launch": int(nbytes), "mean_launch_us": round(mean * 1e6, 2)},
-        "cpu_baseline": {"value": round(cpu_gbs, 3), "unit": "GB/s", "cores": 1, "kind": "port",
-                         "sample": f"oracle gather of {n_cpu} tokens, one sequence at a time"},
-        "gpu_launches": replays * L, "clocks": clocks.summary(),
+                     "kernel": "paged_gather_tma_kernel", "bytes_per_launch": int(nbytes), "mean_launch_us": round(mean * 1e6, 2)},
+        "cpu_baseline": cpu_baseline, "gpu_launches": replays * L, "clocks": clocks.summary(),
     }), flush=True)
 
 

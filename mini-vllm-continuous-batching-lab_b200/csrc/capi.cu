@@ -25,6 +25,22 @@ cudaError_t launch_decode_stream(const CUtensorMap& tmk, const CUtensorMap& tmv,
 int stream_warps_per_cta(int head_dim);
 int stream_smem_bytes(int head_dim, int num_seqs);
 
+// cuTensorMapEncodeTiled from the driver (nullptr when the driver lacks it);
+// shared by the decode (pool maps) and the gather (output maps).
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
 namespace {
 
 constexpr int kAbiVersion = 1;
@@ -182,20 +198,6 @@ int make_plan(int num_seqs, int num_heads, int num_kv_heads, int head_dim, int b
 }
 
 // ---- TMA tensor maps over a pool tensor viewed as [rows, head_dim] ---------
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
-                                         &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
 struct MapEntry {
   const void* ptr;
   int64_t rows;

@@ -95,7 +95,8 @@ def test_gather_prefix_zero_returns_empty():
 
 # ---- batched, ragged, every dtype ----
 @pytest.mark.parametrize("dt,bs,d,kh", [("bf16", 16, 64, 2), ("f16", 32, 128, 8), ("f32", 1, 64, 1),
-                                        ("bf16", 8, 128, 4)])
+                                        ("bf16", 8, 128, 4), ("f32", 16, 64, 2), ("f32", 64, 128, 1),
+                                        ("bf16", 64, 256, 3), ("f16", 16, 8, 2), ("bf16", 16, 64, 6)])
 def test_batched_gather_matches_oracle(dt, bs, d, kh):
     rng = np.random.default_rng(bs * 1000 + d)
     nseq_table = 12
@@ -147,6 +148,78 @@ def test_large_batched_gather_checksum():
         toks.append(p % 16)
     blk, tok = torch.cat(rows), torch.cat(toks)
     assert torch.equal(gk, kc[blk, :, tok, :]) and torch.equal(gv, vc[blk, :, tok, :])
+
+
+# ---- the C ABI: zero rows and error bits ----
+def _abi_gather(kc, vc, bt, rows, offsets, total):
+    """mvb_paged_gather with explicit (possibly inconsistent) offsets; returns
+    (status, K, V, error word).  The outputs start filled with 7.0."""
+    from mini_vllm_b200 import _native
+
+    nb, kh, bs, d = kc.shape
+    meta = torch.tensor(list(rows) + list(offsets), dtype=torch.int64, device=DEV)
+    ko = torch.full((total, kh, d), 7.0, dtype=kc.dtype, device=DEV)
+    vo = torch.full_like(ko, 7.0)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    st = _native.lib().mvb_paged_gather(
+        kc.data_ptr(), vc.data_ptr(), bt.data_ptr(), bt.shape[0], bt.stride(0), bt.shape[1], meta.data_ptr(),
+        meta.data_ptr() + 8 * len(rows), ko.data_ptr(), vo.data_ptr(), len(rows), total, kh, d, bs, nb,
+        {torch.bfloat16: _native.DTYPE_BF16, torch.float16: _native.DTYPE_F16,
+         torch.float32: _native.DTYPE_F32}[kc.dtype], err.data_ptr(), torch.cuda.current_stream(DEV).cuda_stream)
+    torch.cuda.synchronize()
+    return st, ko, vo, int(err.item())
+
+
+def _expected(kc, vc, bt, rows, offsets, total):
+    """Token t of sequence i (offsets[i] <= t < offsets[i + 1]) is
+    cache[bt[rows[i]][p // BS], :, p % BS]; a token without a sequence, or
+    whose block is -1 / past the pool / past the table, is a zero row."""
+    nb, kh, bs, d = kc.shape
+    ek = torch.zeros(total, kh, d, dtype=kc.dtype, device=DEV)
+    ev = torch.zeros_like(ek)
+    for i, r in enumerate(rows):
+        for t in range(max(offsets[i], 0), min(offsets[i + 1], total)):
+            p = t - offsets[i]
+            if not 0 <= r < bt.shape[0] or p // bs >= bt.shape[1]:
+                continue
+            b = int(bt[r, p // bs])
+            if 0 <= b < nb:
+                ek[t], ev[t] = kc[b, :, p % bs], vc[b, :, p % bs]
+    return ek, ev
+
+
+@pytest.mark.parametrize("dt,bs,d,kh", [("bf16", 16, 64, 2), ("f32", 8, 64, 2)])  # tile form, vector form
+def test_abi_bad_blocks_give_zero_rows(dt, bs, d, kh):
+    kc, vc = _pool(12, kh, bs, d, TDT[dt], 4)
+    bt = torch.tensor([[3, -1, 5, 1], [2, 99, 7, 0], [4, 6, 8, 9]], dtype=torch.int64, device=DEV)
+    rows, counts = [0, 1, 2, 5], [3 * bs + 5, 2 * bs + 1, 4 * bs, 7]  # row 5 is outside the table
+    offsets = [0]
+    for n in counts:
+        offsets.append(offsets[-1] + n)
+    st, ko, vo, err = _abi_gather(kc, vc, bt, rows, offsets, offsets[-1])
+    assert st == 0
+    ek, ev = _expected(kc, vc, bt, rows, offsets, offsets[-1])
+    assert torch.equal(ko, ek) and torch.equal(vo, ev)
+    assert err & 2  # MVB_DEV_BLOCK_ID
+
+
+@pytest.mark.parametrize("offsets,total", [([0, 20, 50], 64), ([5, 30, 50], 50), ([0, 40, 30, 70], 70)])
+def test_abi_offsets_that_are_not_a_prefix_sum(offsets, total):
+    """Offsets that end short of total_tokens, start past 0, or fall: the tile
+    form hands over to the per-token loop.  With rising offsets a token
+    without a sequence is a zero row with MVB_DEV_KV_LEN; with falling ones
+    the token-to-sequence search is not defined, but every row is written."""
+    kc, vc = _pool(24, 2, 16, 64, torch.bfloat16, 5)
+    bt = torch.arange(24, dtype=torch.int64, device=DEV).flip(0).reshape(3, 8).contiguous()
+    rows = list(range(len(offsets) - 1))
+    st, ko, vo, err = _abi_gather(kc, vc, bt, rows, offsets, total)
+    assert st == 0
+    if all(a <= b for a, b in zip(offsets, offsets[1:])):
+        ek, ev = _expected(kc, vc, bt, rows, offsets, total)
+        assert torch.equal(ko, ek) and torch.equal(vo, ev)
+        assert err & 1  # MVB_DEV_KV_LEN
+    else:
+        assert not (ko == 7.0).all(dim=-1).any() and not (vo == 7.0).all(dim=-1).any()
 
 
 # ---- errors ----
