@@ -568,6 +568,7 @@ def gather_op(args):
     offsets = np.concatenate([[0], np.cumsum(ctx)]).astype(np.int64)
     meta = torch.from_numpy(np.concatenate([np.arange(spec.num_seqs), offsets]).astype(np.int64)).to(dev)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
+    counter = torch.zeros(2, dtype=torch.int32, device=dev)  # the work counter; each launch leaves it zero
     lib = _native.lib()
 
     def launch(layer):
@@ -575,7 +576,7 @@ def gather_op(args):
                                   bt.stride(0), bt.shape[1], meta.data_ptr(), meta.data_ptr() + 8 * spec.num_seqs,
                                   gk.data_ptr(), gv.data_ptr(), spec.num_seqs, total, spec.num_kv_heads,
                                   spec.head_dim, spec.block_size, spec.num_blocks, _native.DTYPE_BF16,
-                                  err.data_ptr(), torch.cuda.current_stream(dev).cuda_stream)
+                                  counter.data_ptr(), err.data_ptr(), torch.cuda.current_stream(dev).cuda_stream)
         assert st == _native.OK, _native.status_string(st)
 
     s = torch.cuda.Stream(device=dev)
@@ -600,7 +601,7 @@ def gather_op(args):
         ev1.record()
         torch.cuda.synchronize()
     sec = ev0.elapsed_time(ev1) / 1e3 / (replays * L)
-    assert int(err.item()) == 0
+    assert int(err.item()) == 0 and counter.tolist() == [0, 0]
     blocks_read = int(((spec.context_lens + spec.block_size - 1) // spec.block_size).sum())
     nbytes = 4 * total * spec.num_kv_heads * spec.head_dim * 2 + 8 * blocks_read + 16 * spec.num_seqs
     # roofline: single launches behind a sleep

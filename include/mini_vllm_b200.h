@@ -83,13 +83,20 @@ extern "C" {
  * Device errors (the row is zero-filled): a logical block past
  * max_blocks_per_seq -> MVB_DEV_TABLE_SHORT; a block id outside
  * [0, num_blocks) or a sequence row outside the table -> MVB_DEV_BLOCK_ID;
- * offsets that are not an increasing prefix from 0 -> MVB_DEV_KV_LEN. */
+ * offsets that are not an increasing prefix from 0 -> MVB_DEV_KV_LEN.
+ * work_counter: optional, two 4-byte-aligned uint32 device words that are zero
+ * before the call (zero them once when allocating them); every call leaves
+ * them zero again.  With them the tile-copy kernel hands the last half of the
+ * work out in small pieces, so that SMs with more memory bandwidth take more
+ * of it; NULL splits the work evenly in advance (same result, slower tail).
+ * Calls that share the words must not overlap on the GPU: give each stream
+ * its own pair. */
 int mvb_paged_gather(const void* key_cache, const void* value_cache, const int64_t* block_table,
                      int64_t block_table_rows, int64_t block_table_stride, int32_t max_blocks_per_seq,
                      const int64_t* seq_rows, const int64_t* out_offsets, void* key_out, void* value_out,
                      int32_t num_seqs, int64_t total_tokens, int32_t num_kv_heads, int32_t head_dim,
-                     int32_t block_size, int32_t num_blocks, int32_t dtype, int32_t* error_flags,
-                     void* stream);
+                     int32_t block_size, int32_t num_blocks, int32_t dtype, uint32_t* work_counter,
+                     int32_t* error_flags, void* stream);
 
 /* Rotary position embedding of the step's query and key rows fused with the
  * paged KV-cache write of the rotated keys and the values: bit for bit the

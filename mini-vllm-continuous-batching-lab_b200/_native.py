@@ -48,7 +48,7 @@ DECODE_STREAM = 3
 # flag ORed into the decode variant (MVB_DECODE_AFTER_WRITE)
 DECODE_AFTER_WRITE = 0x100
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 # Every symbol include/mini_vllm_b200.h declares, with (restype, argtypes).
 _i32, _i64, _u32, _f32, _vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_uint32, ctypes.c_float, ctypes.c_void_p
@@ -74,7 +74,7 @@ SIGNATURES = {
     "mvb_paged_gather": (
         _i32,
         [_vp, _vp, _vp, _i64, _i64, _i32, _vp, _vp, _vp, _vp, _i32, _i64, _i32, _i32, _i32, _i32, _i32,
-         _vp, _vp],
+         _vp, _vp, _vp],
     ),
     "mvb_rope_kv_cache_write": (
         _i32,

@@ -78,6 +78,7 @@ class _DeviceState:
         self.err_ptr = self.err.data_ptr()
         self._claims: Dict[int, Tuple[torch.Tensor, int]] = {}
         self._workspaces: Dict[str, torch.Tensor] = {}
+        self._counters: Dict[int, torch.Tensor] = {}
 
     def next_claims(self, total_slots: int) -> Tuple[torch.Tensor, int]:
         """Claim array for a pool of ``total_slots`` and a fresh epoch (never 0)."""
@@ -93,6 +94,15 @@ class _DeviceState:
                 epoch = 1
         self._claims[total_slots] = (arr, epoch)
         return arr, epoch
+
+    def gather_counter(self, stream: int) -> int:
+        """Device address of the gather's two work-counter words for one stream
+        (zero when allocated; every gather leaves them zero)."""
+        buf = self._counters.get(stream)
+        if buf is None:
+            buf = torch.zeros(2, dtype=torch.int32, device=self.device)
+            self._counters[stream] = buf
+        return buf.data_ptr()
 
     def workspace(self, nbytes: int, variant: str) -> torch.Tensor:
         """Decode workspace of one kernel variant (the stream kernel and the
@@ -590,11 +600,12 @@ def paged_gather(
     meta = torch.tensor(rows + offsets, dtype=torch.int64).to(dev)  # one small copy: rows, then offsets
     dev_idx = key_cache.get_device()
     state = _state(dev_idx)
+    stream = _stream_handle(dev_idx)
     status = _native.lib().mvb_paged_gather(
         key_cache.data_ptr(), value_cache.data_ptr(), block_table.data_ptr(), n_rows, block_table.stride(0),
         max_blocks, meta.data_ptr(), meta.data_ptr() + 8 * len(rows), out_k.data_ptr(), out_v.data_ptr(),
         len(rows), total, num_kv_heads, head_dim, block_size, num_blocks, _DTYPE_CODES[key_cache.dtype],
-        state.err_ptr, _stream_handle(dev_idx),
+        state.gather_counter(stream or 0), state.err_ptr, stream,
     )
     _host_status(status, "paged gather")
     if strict:

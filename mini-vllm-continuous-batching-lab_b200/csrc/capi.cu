@@ -43,7 +43,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 namespace {
 
-constexpr int kAbiVersion = 1;
+constexpr int kAbiVersion = 2;
 // Longest context the auto plan serves with one CTA per (sequence, KV head);
 // beyond it the flash-decoding split is used.
 constexpr int64_t kUnsplitMaxTokens = 8192;

@@ -190,6 +190,14 @@ __global__ void __launch_bounds__(256, kGatherCtasPerSm) paged_gather_kernel(con
 #ifndef MVB_GATHER_TMA_STAGE_MAX
 #define MVB_GATHER_TMA_STAGE_MAX (16 * 1024)
 #endif
+#ifndef MVB_GATHER_STATIC_PCT
+#define MVB_GATHER_STATIC_PCT 50
+#endif
+#ifndef MVB_GATHER_CHUNK
+#define MVB_GATHER_CHUNK 2
+#endif
+constexpr int kStaticPct = MVB_GATHER_STATIC_PCT;  // share of the items split statically when balancing
+constexpr int kDynChunk = MVB_GATHER_CHUNK;        // items per counter ticket
 constexpr int kTmaStages = MVB_GATHER_TMA_STAGES;         // per warp; kTmaStages - 1 items in flight
 constexpr int kTmaRingBytes = MVB_GATHER_TMA_RING_BYTES;  // stage bytes of one CTA (all its warps)
 constexpr int kTmaStageMax = MVB_GATHER_TMA_STAGE_MAX;    // K + V bytes of one item, at most
@@ -201,7 +209,9 @@ struct GatherTmaArgs {
   GatherArgs g;
   int64_t total_tokens;
   int64_t total_items;    // V * groups
-  int64_t items_per_warp;
+  int64_t items_per_warp; // static items of each warp
+  int64_t dyn_start;      // first item handed out by the counter (total_items: no counter)
+  uint32_t* counter;      // [next ticket, finished warps], zero on entry and on exit; or nullptr
   int row_bytes;          // R = head_dim * element size
   int khb;                // KV heads per item
   int groups;             // KH / khb
@@ -238,9 +248,6 @@ template <int N> __device__ __forceinline__ void bulk_wait_read() {
   asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
 }
 
-__device__ __forceinline__ int64_t tile_vstart(const GatherArgs& a, int s) {
-  return (__ldg(a.offsets + s) >> 4) + s;
-}
 
 __global__ void __launch_bounds__(kTmaMaxWarps * 32)
     paged_gather_tma_kernel(const __grid_constant__ CUtensorMap kpool, const __grid_constant__ CUtensorMap vpool,
@@ -249,23 +256,39 @@ __global__ void __launch_bounds__(kTmaMaxWarps * 32)
   grid_dependency_wait();  // the cache (and the offsets) may come from the previous kernel
   grid_launch_dependents();
   const GatherArgs& a = t.g;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // The item map needs offsets that rise from 0 to total_tokens; other offsets
   // take the vector form's per-token loop (zero rows and MVB_DEV_KV_LEN for
-  // tokens without a sequence).
-  bool bad_offsets = false;
-  for (int i = threadIdx.x; i <= a.num_seqs; i += blockDim.x) {
-    const int64_t o = __ldg(a.offsets + i);
-    if (i == 0 ? o != 0 : o < __ldg(a.offsets + i - 1)) bad_offsets = true;
-    if (i == a.num_seqs && o != t.total_tokens) bad_offsets = true;
+  // tokens without a sequence).  Every warp checks all offsets itself, 256 per
+  // round of independent loads, so all warps of the grid take the same path.
+  {
+    bool bad_offsets = false;
+    int64_t carry = 0;  // offsets[base - 1]
+    for (int base = 0; base <= a.num_seqs; base += 256) {
+      int64_t o[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int i = base + k * 32 + lane;
+        o[k] = i <= a.num_seqs ? __ldg(a.offsets + i) : 0;
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int i = base + k * 32 + lane;
+        const int64_t up = __shfl_up_sync(0xffffffffu, o[k], 1);
+        const int64_t prev = lane > 0 ? up : carry;
+        carry = __shfl_sync(0xffffffffu, o[k], 31);
+        if (i <= a.num_seqs && (i == 0 ? o[k] != 0 : o[k] < prev)) bad_offsets = true;
+        if (i == a.num_seqs && o[k] != t.total_tokens) bad_offsets = true;
+      }
+    }
+    if (__any_sync(0xffffffffu, bad_offsets)) {
+      gather_vector_loop<false>(a);
+      return;
+    }
   }
-  if (__syncthreads_or(bad_offsets)) {
-    gather_vector_loop<false>(a);
-    return;
-  }
-
   extern __shared__ __align__(128) unsigned char smem[];
+  auto vstart = [&](int i) -> int64_t { return (__ldg(a.offsets + i) >> 4) + i; };
   constexpr int S = kTmaStages;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int R = t.row_bytes, khb = t.khb;
   const uint32_t tile_bytes = (uint32_t)kTmaTile * R * khb, stage_bytes = 2 * tile_bytes;  // K tile, V tile
   const uint32_t bar0 = smem_u32(smem) + warp * S * 8;
@@ -279,7 +302,7 @@ __global__ void __launch_bounds__(kTmaMaxWarps * 32)
 
   const int64_t gw = (int64_t)blockIdx.x * t.warps + warp;
   const int64_t i0 = gw * t.items_per_warp;
-  const int64_t i1 = min(i0 + t.items_per_warp, t.total_items);
+  const int64_t i1 = min(i0 + t.items_per_warp, min(t.dyn_start, t.total_items));
   const uint64_t policy = l2_policy_evict_first();
   const int ch = R >> 4;  // 16-byte chunks per row
   int issued = 0, consumed = 0, groups = 0, bad = 0;
@@ -362,18 +385,42 @@ __global__ void __launch_bounds__(kTmaMaxWarps * 32)
     ++issued;
   };
 
-  for (int64_t base = i0; base < i1 && ok; base += 32) {
+  // Batches: the warp's static range, 32 items at a time, then (with a
+  // counter) kDynChunk items per ticket until the tickets run past the items,
+  // so SMs that get more bandwidth take more of the tail.  Lane 0 asks for
+  // the next ticket one batch ahead.
+  uint32_t ticket = 0;
+  auto grab = [&]() {
+    if (lane == 0) ticket = atomicAdd(t.counter, 1u);
+  };
+  int64_t cursor = i0;
+  if (t.counter != nullptr && cursor >= i1) grab();
+  while (ok) {
+    int64_t base, end;
+    if (cursor < i1) {
+      base = cursor;
+      end = min(cursor + 32, i1);
+      cursor = end;
+      if (t.counter != nullptr && cursor >= i1) grab();
+    } else if (t.counter != nullptr) {
+      base = t.dyn_start + (int64_t)__shfl_sync(0xffffffffu, ticket, 0) * kDynChunk;
+      if (base >= t.total_items) break;
+      end = min(base + kDynChunk, t.total_items);
+      grab();
+    } else {
+      break;
+    }
     // Resolve item base + lane.  s0: the sequence of the batch's first tile
     // (32-ary ballot search over vstart); lane L's tile lies at most 31
     // sequences further, counted against vstart(s0 + 1 .. s0 + 32).
     const int64_t w = base + lane;
-    const bool in = w < i1;
+    const bool in = w < end;
     const int64_t vfirst = base / t.groups;
     int lo = 0, hi = a.num_seqs;
     while (hi - lo > 1) {
       const int step = (hi - lo + 31) >> 5;
       const int probe = lo + lane * step;
-      const bool le = probe < hi && tile_vstart(a, probe) <= vfirst;
+      const bool le = probe < hi && vstart(probe) <= vfirst;
       const unsigned msk = __ballot_sync(0xffffffffu, le) | 1u;
       lo += (31 - __clz(msk)) * step;
       hi = min(hi, lo + step);
@@ -381,7 +428,7 @@ __global__ void __launch_bounds__(kTmaMaxWarps * 32)
     const int64_t v = (in ? w : base) / t.groups;
     const int hg = (int)((in ? w : base) - v * t.groups);
     const int sn = lo + 1 + lane;
-    const int64_t next_start = sn < a.num_seqs ? tile_vstart(a, sn) : INT64_MAX;
+    const int64_t next_start = sn < a.num_seqs ? vstart(sn) : INT64_MAX;
     int s = lo;
 #pragma unroll
     for (int i = 0; i < 32; ++i) s += __shfl_sync(0xffffffffu, next_start, i) <= v ? 1 : 0;
@@ -435,6 +482,16 @@ __global__ void __launch_bounds__(kTmaMaxWarps * 32)
   }
   if (lane == 0) bulk_wait_read<0>();
   if (bad) atomicOr(a.err, bad);
+  if (t.counter != nullptr && lane == 0) {
+    // The last warp to finish puts both words back to zero for the next call;
+    // every warp's last ticket request is ordered before its count.
+    __threadfence();
+    const uint32_t done = atomicAdd(t.counter + 1, 1u);
+    if (done == (uint32_t)gridDim.x * t.warps - 1) {
+      atomicExch(t.counter, 0u);
+      atomicExch(t.counter + 1, 0u);
+    }
+  }
 }
 
 int64_t round_up_128(int64_t v) { return (v + 127) / 128 * 128; }
@@ -511,7 +568,8 @@ extern "C" int mvb_paged_gather(const void* key_cache, const void* value_cache, 
                                 const int64_t* seq_rows,
                                 const int64_t* out_offsets, void* key_out, void* value_out, int32_t num_seqs,
                                 int64_t total_tokens, int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
-                                int32_t num_blocks, int32_t dtype, int32_t* error_flags, void* stream) {
+                                int32_t num_blocks, int32_t dtype, uint32_t* work_counter, int32_t* error_flags,
+                                void* stream) {
   mvb::NvtxRange nvtx_range("mvb_paged_gather");
   if (dtype != MVB_DTYPE_F32 && dtype != MVB_DTYPE_F16 && dtype != MVB_DTYPE_BF16) return MVB_ERR_DTYPE;
   if (head_dim <= 0) return MVB_ERR_HEAD_DIM;
@@ -527,7 +585,8 @@ extern "C" int mvb_paged_gather(const void* key_cache, const void* value_cache, 
   const int64_t row_bytes = (int64_t)head_dim * (dtype == MVB_DTYPE_F32 ? 4 : 2);
   if (row_bytes % 16 != 0) return MVB_ERR_HEAD_DIM;  // rows move as 16-byte vectors
   auto aligned = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
-  if (!aligned(key_cache) || !aligned(value_cache) || !aligned(key_out) || !aligned(value_out))
+  if (!aligned(key_cache) || !aligned(value_cache) || !aligned(key_out) || !aligned(value_out) ||
+      (reinterpret_cast<uintptr_t>(work_counter) & 3) != 0)
     return MVB_ERR_ALIGNMENT;
 
   GatherArgs a;
@@ -587,7 +646,15 @@ extern "C" int mvb_paged_gather(const void* key_cache, const void* value_cache, 
       t.total_items = (total_tokens / kTmaTile + num_seqs) * (int64_t)t.groups;
       const int64_t want = (t.total_items + warps - 1) / warps, cap = (int64_t)sms * per_sm;
       const int64_t grid = want < cap ? want : cap;
-      t.items_per_warp = (t.total_items + grid * warps - 1) / (grid * warps);
+      const int64_t all_warps = grid * warps;
+      t.counter = work_counter;
+      if (work_counter != nullptr) {  // a static share, then tickets
+        t.items_per_warp = t.total_items * kStaticPct / 100 / all_warps;
+        t.dyn_start = t.items_per_warp * all_warps;
+      } else {
+        t.items_per_warp = (t.total_items + all_warps - 1) / all_warps;
+        t.dyn_start = t.total_items;
+      }
       const cudaError_t e = launch_pdl(paged_gather_tma_kernel, dim3((unsigned)grid), dim3(warps * 32), smem, st,
                                        maps[0], maps[1], maps[2], maps[3], t);
       return e == cudaSuccess ? MVB_OK : MVB_ERR_CUDA;

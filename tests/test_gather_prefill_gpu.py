@@ -151,9 +151,10 @@ def test_large_batched_gather_checksum():
 
 
 # ---- the C ABI: zero rows and error bits ----
-def _abi_gather(kc, vc, bt, rows, offsets, total):
-    """mvb_paged_gather with explicit (possibly inconsistent) offsets; returns
-    (status, K, V, error word).  The outputs start filled with 7.0."""
+def _abi_gather(kc, vc, bt, rows, offsets, total, counter=None):
+    """mvb_paged_gather with explicit (possibly inconsistent) offsets and an
+    optional work counter; returns (status, K, V, error word).  The outputs
+    start filled with 7.0."""
     from mini_vllm_b200 import _native
 
     nb, kh, bs, d = kc.shape
@@ -165,7 +166,8 @@ def _abi_gather(kc, vc, bt, rows, offsets, total):
         kc.data_ptr(), vc.data_ptr(), bt.data_ptr(), bt.shape[0], bt.stride(0), bt.shape[1], meta.data_ptr(),
         meta.data_ptr() + 8 * len(rows), ko.data_ptr(), vo.data_ptr(), len(rows), total, kh, d, bs, nb,
         {torch.bfloat16: _native.DTYPE_BF16, torch.float16: _native.DTYPE_F16,
-         torch.float32: _native.DTYPE_F32}[kc.dtype], err.data_ptr(), torch.cuda.current_stream(DEV).cuda_stream)
+         torch.float32: _native.DTYPE_F32}[kc.dtype], None if counter is None else counter.data_ptr(),
+        err.data_ptr(), torch.cuda.current_stream(DEV).cuda_stream)
     torch.cuda.synchronize()
     return st, ko, vo, int(err.item())
 
@@ -188,19 +190,82 @@ def _expected(kc, vc, bt, rows, offsets, total):
     return ek, ev
 
 
+@pytest.mark.parametrize("with_counter", [False, True])
 @pytest.mark.parametrize("dt,bs,d,kh", [("bf16", 16, 64, 2), ("f32", 8, 64, 2)])  # tile form, vector form
-def test_abi_bad_blocks_give_zero_rows(dt, bs, d, kh):
+def test_abi_bad_blocks_give_zero_rows(dt, bs, d, kh, with_counter):
     kc, vc = _pool(12, kh, bs, d, TDT[dt], 4)
     bt = torch.tensor([[3, -1, 5, 1], [2, 99, 7, 0], [4, 6, 8, 9]], dtype=torch.int64, device=DEV)
     rows, counts = [0, 1, 2, 5], [3 * bs + 5, 2 * bs + 1, 4 * bs, 7]  # row 5 is outside the table
     offsets = [0]
     for n in counts:
         offsets.append(offsets[-1] + n)
-    st, ko, vo, err = _abi_gather(kc, vc, bt, rows, offsets, offsets[-1])
+    counter = torch.zeros(2, dtype=torch.int32, device=DEV) if with_counter else None
+    st, ko, vo, err = _abi_gather(kc, vc, bt, rows, offsets, offsets[-1], counter)
     assert st == 0
     ek, ev = _expected(kc, vc, bt, rows, offsets, offsets[-1])
     assert torch.equal(ko, ek) and torch.equal(vo, ev)
     assert err & 2  # MVB_DEV_BLOCK_ID
+    if with_counter:
+        assert counter.tolist() == [0, 0]
+
+
+@pytest.mark.parametrize("short_by", [0, 3])
+def test_abi_batch_above_the_staged_sequence_limit(short_by):
+    """1100 short sequences (0-8 tokens): the offset check takes several
+    rounds per warp and the sequence search three ballot levels.
+    short_by > 0: offsets end before total_tokens, and the tail rows are zero
+    with MVB_DEV_KV_LEN."""
+    rng = np.random.default_rng(33)
+    counts = [int(c) for c in rng.integers(0, 9, size=1100)]
+    need = [max(1, (c + 15) // 16) for c in counts]
+    nb = sum(need) + 2
+    perm = torch.from_numpy(rng.permutation(nb)).to(DEV)
+    bt = torch.zeros((1100, 1), dtype=torch.int64, device=DEV)
+    bt[:, 0] = perm[:1100]
+    kc, vc = _pool(nb, 2, 16, 64, torch.bfloat16, 9)
+    offsets = [0]
+    for n in counts:
+        offsets.append(offsets[-1] + n)
+    total = offsets[-1] + short_by
+    counter = torch.zeros(2, dtype=torch.int32, device=DEV)
+    st, ko, vo, err = _abi_gather(kc, vc, bt, list(range(1100)), offsets, total, counter)
+    assert st == 0 and counter.tolist() == [0, 0]
+    rows = torch.cat([torch.full((n,), i, dtype=torch.int64) for i, n in enumerate(counts)]).to(DEV)
+    tok = torch.cat([torch.arange(n) for n in counts]).to(DEV)
+    blk = bt[rows, 0]
+    ek = torch.zeros((total, 2, 64), dtype=torch.bfloat16, device=DEV)
+    ev = torch.zeros_like(ek)
+    ek[:offsets[-1]], ev[:offsets[-1]] = kc[blk, :, tok, :], vc[blk, :, tok, :]
+    assert torch.equal(ko, ek) and torch.equal(vo, ev)
+    assert (err & 1) == (1 if short_by else 0)
+
+
+def test_abi_work_counter_is_left_zero_and_results_repeat():
+    """With the work counter the tail of the copy is handed out at run time,
+    so warps take different items from call to call; the output must not
+    change, and the two words must be zero after every call."""
+    rng = np.random.default_rng(21)
+    counts = [int(c) for c in rng.integers(1, 1500, size=96)]
+    need = [(c + 15) // 16 for c in counts]
+    nb = sum(need) + 3
+    perm = torch.from_numpy(rng.permutation(nb)).to(DEV)
+    bt = torch.full((96, max(need)), -1, dtype=torch.int64, device=DEV)
+    pos = 0
+    for i, k in enumerate(need):
+        bt[i, :k] = perm[pos:pos + k]
+        pos += k
+    kc, vc = _pool(nb, 2, 16, 64, torch.bfloat16, 8)
+    offsets = [0]
+    for n in counts:
+        offsets.append(offsets[-1] + n)
+    counter = torch.zeros(2, dtype=torch.int32, device=DEV)
+    st, k0, v0, err = _abi_gather(kc, vc, bt, list(range(96)), offsets, offsets[-1])  # static split
+    assert st == 0 and err == 0
+    for _ in range(3):
+        st, k1, v1, err = _abi_gather(kc, vc, bt, list(range(96)), offsets, offsets[-1], counter)
+        assert st == 0 and err == 0
+        assert torch.equal(k1, k0) and torch.equal(v1, v0)
+        assert counter.tolist() == [0, 0]
 
 
 @pytest.mark.parametrize("offsets,total", [([0, 20, 50], 64), ([5, 30, 50], 50), ([0, 40, 30, 70], 70)])
