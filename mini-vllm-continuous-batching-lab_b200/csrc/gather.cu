@@ -181,6 +181,10 @@ __global__ void __launch_bounds__(256, kGatherCtasPerSm) paged_gather_kernel(con
 // tiles as [KHB][16][D]: one 4-D tensor load per tile from the pool (dims D,
 // BS, KH, NB) and one 3-D tensor store per tile into the output viewed with
 // dims (D, T, KH), whose box {D, 16, KHB} has the same shared-memory layout.
+//
+// The MVB_GATHER_* macros are build-time tuning knobs; their defaults are the
+// best of the measured settings (ring depth and size, static share, ticket
+// size) on the config-2 contexts.
 #ifndef MVB_GATHER_TMA_STAGES
 #define MVB_GATHER_TMA_STAGES 4
 #endif
@@ -247,7 +251,6 @@ __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.comm
 template <int N> __device__ __forceinline__ void bulk_wait_read() {
   asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
 }
-
 
 __global__ void __launch_bounds__(kTmaMaxWarps * 32)
     paged_gather_tma_kernel(const __grid_constant__ CUtensorMap kpool, const __grid_constant__ CUtensorMap vpool,
