@@ -20,8 +20,10 @@ only collective of the path.
 
 Printed (rank 0, one JSON line):
   value       aggregate algorithmic HBM GB/s of the device-resident step loop
-              (bytes of the write + decode, SURVEY-style formula in
-              workloads.PagedDecodeSpec) over the max-over-ranks time of K steps
+              (algorithmic bytes of the write + decode: K/V read once per
+              KV head, q read, output written, block-table entries and
+              context lengths read; workloads.PagedDecodeSpec) over the
+              max-over-ranks time of K steps
               replayed from a CUDA graph;
   e2e         the same metric through the public backend API with the step's
               inputs copied from pinned host memory each step and the output
