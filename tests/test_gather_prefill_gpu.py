@@ -287,6 +287,43 @@ def test_abi_offsets_that_are_not_a_prefix_sum(offsets, total):
         assert not (ko == 7.0).all(dim=-1).any() and not (vo == 7.0).all(dim=-1).any()
 
 
+def test_gathers_on_two_streams_at_once():
+    """paged_gather keeps one work counter per stream: gathers queued on two
+    streams without a sync in between run concurrently and each still returns
+    exactly its rows."""
+    rng = np.random.default_rng(41)
+    cases = []
+    for seed in (1, 2):
+        counts = [int(c) for c in rng.integers(1, 1200, size=128)]
+        need = [(c + 15) // 16 for c in counts]
+        nb = sum(need) + 2
+        perm = torch.from_numpy(rng.permutation(nb)).to(DEV)
+        bt = torch.full((128, max(need)), -1, dtype=torch.int64, device=DEV)
+        pos = 0
+        for i, k in enumerate(need):
+            bt[i, :k] = perm[pos:pos + k]
+            pos += k
+        kc, vc = _pool(nb, 2, 16, 64, torch.bfloat16, seed)
+        rows = torch.cat([torch.full((n,), i, dtype=torch.int64) for i, n in enumerate(counts)]).to(DEV)
+        tok = torch.cat([torch.arange(n) for n in counts]).to(DEV)
+        blk = bt[rows, tok // 16]
+        cases.append((kc, vc, bt, counts, kc[blk, :, tok % 16, :], vc[blk, :, tok % 16, :]))
+    streams = [torch.cuda.Stream(DEV), torch.cuda.Stream(DEV)]
+    torch.cuda.synchronize()
+    outs = [[], []]
+    for _ in range(4):
+        for i, st in enumerate(streams):
+            kc, vc, bt, counts = cases[i][:4]
+            with torch.cuda.stream(st):
+                outs[i].append(M.paged_gather(kc, vc, bt, list(range(128)), counts, 16, strict=False))
+    torch.cuda.synchronize()
+    M.check_device_errors(DEV)
+    for i in range(2):
+        ek, ev = cases[i][4], cases[i][5]
+        for gk, gv in outs[i]:
+            assert torch.equal(gk, ek) and torch.equal(gv, ev)
+
+
 # ---- errors ----
 def test_gather_errors():
     kc, vc = _pool(8, 2, 16, 64, torch.bfloat16, 2)
