@@ -26,10 +26,12 @@ from .attention import (
 from .cache import KVCachePool, compute_num_gpu_blocks
 from .engine import StepMetadata, StepMetadataBuilder
 from .model_runner import AttentionGroup, AttentionMetadata, ModelConfig
+from . import staging
 
 __version__ = "0.1.0"
 
 __all__ = [
+    "staging",
     "ArgumentError",
     "AttentionBackend",
     "AttentionBackendB200",

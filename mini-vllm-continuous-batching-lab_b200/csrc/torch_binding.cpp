@@ -17,6 +17,7 @@
 
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
+#include <cuda_runtime_api.h>
 
 #include <cmath>
 #include <mutex>
@@ -169,6 +170,41 @@ std::tuple<int64_t, at::Tensor> decode(const at::Tensor& query, const at::Tensor
   return {st, out};
 }
 
+// Stream-ordered staging for a serving loop, one CUDA call each on raw handles
+// (a torch.cuda.Stream's cuda_stream, a torch.cuda.Event's cuda_event): the
+// torch-level copy_ / wait_event / record / set_stream calls cost about a
+// microsecond of host time each, several per step.  Each returns the CUDA error
+// code (0 = success).
+// Wait (when wait_event != 0) for the event on `stream`, copy `nbytes` from
+// `src` to `dst` (kind 0: host to device, 1: device to host), then record
+// `record_event` (when != 0) on `stream`.
+int64_t stream_copy(int64_t dst, int64_t src, int64_t nbytes, int64_t kind, int64_t stream, int64_t wait_event,
+                    int64_t record_event) {
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaSuccess;
+  if (wait_event != 0) e = cudaStreamWaitEvent(s, reinterpret_cast<cudaEvent_t>(wait_event), 0);
+  if (e == cudaSuccess && nbytes > 0)
+    e = cudaMemcpyAsync(reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src), (size_t)nbytes,
+                        kind == 0 ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess && record_event != 0) e = cudaEventRecord(reinterpret_cast<cudaEvent_t>(record_event), s);
+  return (int64_t)e;
+}
+
+// `stream` waits for each of `events` (0 entries are skipped).
+int64_t stream_wait_events(int64_t stream, const std::vector<int64_t>& events) {
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  for (int64_t ev : events) {
+    if (ev == 0) continue;
+    const cudaError_t e = cudaStreamWaitEvent(s, reinterpret_cast<cudaEvent_t>(ev), 0);
+    if (e != cudaSuccess) return (int64_t)e;
+  }
+  return 0;
+}
+
+int64_t event_record(int64_t event, int64_t stream) {
+  return (int64_t)cudaEventRecord(reinterpret_cast<cudaEvent_t>(event), reinterpret_cast<cudaStream_t>(stream));
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -176,4 +212,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.attr("SLOW_PATH") = kSlowPath;
   m.def("kv_write", &kv_write);
   m.def("decode", &decode);
+  m.def("stream_copy", &stream_copy);
+  m.def("stream_wait_events", &stream_wait_events);
+  m.def("event_record", &event_record);
 }

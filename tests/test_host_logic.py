@@ -233,3 +233,10 @@ def test_gather_host_checks_without_gpu():
         M.paged_gather(kc, kc, torch.zeros(1, 2, dtype=torch.int64), [0], [4], 16)
     with pytest.raises(M.ArgumentError, match="mismatch"):
         M.paged_gather(kc, kc[:2], torch.zeros(1, 2, dtype=torch.int64), [0], [4], 16)
+
+
+def test_staging_rejects_bad_arguments_before_any_cuda_call():
+    """mini_vllm_b200.staging checks its tensors on the host: two host tensors
+    raise ValueError before the binding is reached."""
+    with pytest.raises(ValueError, match="exactly one"):
+        M.staging.stream_copy(torch.zeros(4), torch.zeros(4), None)
