@@ -421,6 +421,29 @@ def decode_plan(
             "num_partitions": np_.value, "workspace_bytes": ws.value}
 
 
+def _decode_fast(query, key_cache, value_cache, block_table, kv_len_after, block_size, scale, out, variant,
+                 partition_tokens, strict, after_write) -> Optional[torch.Tensor]:
+    """The common case of a decode in one C++ call (the direct binding), or
+    None when the full path of paged_decode_attention must run instead (no
+    binding, a conversion to make, an argument to reject, a failed call)."""
+    fast = _native.fast()
+    if fast is None or not query.is_cuda:
+        return None
+    state = _state(query.get_device())
+    status, res = fast.decode(query, key_cache, value_cache, block_table, kv_len_after, block_size,
+                              -1.0 if scale is None else float(scale), out,
+                              _VARIANTS.get(variant, -1) | (_native.DECODE_AFTER_WRITE if after_write else 0),
+                              int(partition_tokens or 0), state.err_ptr)
+    if status != _native.OK:
+        return None
+    if strict:
+        flags = _take_flags(state)
+        if flags:
+            _raise_flags(flags, {"kv_len_after": kv_len_after, "max_blocks": block_table.shape[1],
+                                 "block_size": block_size, "num_blocks": key_cache.shape[0]})
+    return res
+
+
 def paged_decode_attention(
     query: torch.Tensor,
     key_cache: torch.Tensor,
@@ -456,21 +479,11 @@ def paged_decode_attention(
 
     Returns ``[total_decode, num_q_heads, head_dim]`` in the query's dtype.
     """
-    fast = _native.fast()
-    if fast is not None and query.is_cuda:  # direct binding: the common case in one C++ call
-        state = _state(query.get_device())
-        status, res = fast.decode(query, key_cache, value_cache, block_table, kv_len_after, block_size,
-                                            -1.0 if scale is None else float(scale), out,
-                                            _VARIANTS.get(variant, -1) | (_native.DECODE_AFTER_WRITE if after_write else 0),
-                                            int(partition_tokens or 0), state.err_ptr)
-        if status == _native.OK:
-            if strict:
-                flags = _take_flags(state)
-                if flags:
-                    _raise_flags(flags, {"kv_len_after": kv_len_after, "max_blocks": block_table.shape[1],
-                                         "block_size": block_size, "num_blocks": key_cache.shape[0]})
-            return res
-        # anything else takes the full path below
+    res = _decode_fast(query, key_cache, value_cache, block_table, kv_len_after, block_size, scale, out,
+                       variant, partition_tokens, strict, after_write)
+    if res is not None:
+        return res
+    # anything else takes the full path below
     if not (query.dim() == 3 and key_cache.dim() == 4 and key_cache.shape == value_cache.shape
             and query.shape[2] in (64, 128) and block_size > 0 and (block_size & (block_size - 1)) == 0
             and key_cache.shape[2] == block_size and key_cache.shape[3] == query.shape[2]
@@ -844,16 +857,23 @@ class AttentionBackendB200(AttentionBackend):
         last, self._last_write = self._last_write, None  # only the very next decode may overlap
         if query.shape[0] == 0:
             return query
-        group = next((g for g in attn_metadata.groups if g.attention_type == "decode_gpu"), None)
+        group = None
+        for g in attn_metadata.groups:
+            if g.attention_type == "decode_gpu":
+                group = g
+                break
         if group is None:
             return query
         after = last is not None and query.is_cuda and last == (layer_idx, _stream_handle(query.get_device()))
-        return paged_decode_attention(
-            query, pool.key_caches[layer_idx], pool.value_caches[layer_idx],
-            attn_metadata.decode_block_tables, group.kv_len_after, pool.block_size,
-            out=out, variant=self.decode_variant, partition_tokens=self.partition_tokens,
-            strict=self.strict, after_write=after,
-        )
+        kc, vc = pool.key_caches[layer_idx], pool.value_caches[layer_idx]
+        bt, kvl = attn_metadata.decode_block_tables, group.kv_len_after
+        # the common case straight to the binding (per-step host time); else the full path
+        res = _decode_fast(query, kc, vc, bt, kvl, pool.block_size, None, out, self.decode_variant,
+                           self.partition_tokens, self.strict, after)
+        if res is not None:
+            return res
+        return paged_decode_attention(query, kc, vc, bt, kvl, pool.block_size, out=out, variant=self.decode_variant,
+                                      partition_tokens=self.partition_tokens, strict=self.strict, after_write=after)
 
     def prefill_attention(self, layer_idx: int, query: torch.Tensor, key: Optional[torch.Tensor],
                           value: Optional[torch.Tensor], attn_metadata: Any, pool: Any) -> torch.Tensor:
