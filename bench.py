@@ -65,7 +65,7 @@ def parse_args():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--config", type=int, default=2, choices=[2, 3, 4])
     p.add_argument("--layers", type=int, default=24)
-    p.add_argument("--variant", default="auto", choices=["auto", "mma", "fma"])
+    p.add_argument("--variant", default="auto", choices=["auto", "sched", "stream", "mma", "fma"])
     p.add_argument("--partition-tokens", type=int, default=0)
     p.add_argument("--e2e-steps", type=int, default=2000)
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -253,16 +253,29 @@ def ours(args, rank, world, local_rank):
         owned_all = [np.asarray(c, dtype=np.int64) for c in counts]
         gather = sharding.OutputGather(owned_all, spec.num_heads, spec.head_dim, torch.bfloat16, dev)
 
+    plan = M.decode_plan(spec.num_seqs, spec.num_heads, spec.num_kv_heads, spec.head_dim, spec.block_size,
+                         spec.num_blocks, spec.max_blocks, torch.bfloat16, args.variant, pt,
+                         kcs[0].data_ptr())
+    scheduled = plan["variant"] == "sched"
+    sched = None
+
+    def begin_model_step():
+        # kv_len and the block tables are those of every layer of the step: one
+        # schedule serves the step's L layer-steps
+        nonlocal sched
+        if scheduled:
+            sched = M.build_decode_schedule(kvl, spec.num_heads, spec.num_kv_heads, spec.head_dim,
+                                            spec.block_size, spec.num_blocks, spec.max_blocks, torch.bfloat16,
+                                            schedule=sched, strict=False)
+
     def step(layer):
         M.paged_cache_write(nk, nv, kcs[layer], vcs[layer], slots, spec.block_size, strict=False,
                             check_duplicates=False)
         M.paged_decode_attention(q, kcs[layer], vcs[layer], bt, kvl, spec.block_size, out=out,
-                                 variant=args.variant, partition_tokens=pt, strict=False, after_write=True)
+                                 variant=args.variant, partition_tokens=pt, strict=False, after_write=True,
+                                 schedule=sched)
 
-    plan = M.decode_plan(spec.num_seqs, spec.num_heads, spec.num_kv_heads, spec.head_dim, spec.block_size,
-                         spec.num_blocks, spec.max_blocks, torch.bfloat16, args.variant, pt,
-                         kcs[0].data_ptr())
-    launches_per_step = 2 + (1 if plan["num_partitions"] > 1 else 0)
+    launches_per_step = 2 + (1 if plan["num_partitions"] > 1 or plan["variant"] == "stream" else 0)
 
     # correctness gate before timing: one strict step
     M.paged_cache_write(nk, nv, kcs[0], vcs[0], slots, spec.block_size)
@@ -275,6 +288,7 @@ def ours(args, rank, world, local_rank):
     s = torch.cuda.Stream(device=dev)
     s.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.stream(s):
+        begin_model_step()
         for layer in range(L):
             step(layer)
         if gather is not None:
@@ -283,6 +297,7 @@ def ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
+        begin_model_step()
         for layer in range(L):
             step(layer)
         if gather is not None:
@@ -330,7 +345,7 @@ def ours(args, rank, world, local_rank):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
             M.paged_decode_attention(q, kcs[layer], vcs[layer], bt, kvl, spec.block_size, out=out,
-                                     variant=args.variant, partition_tokens=pt, strict=False)
+                                     variant=args.variant, partition_tokens=pt, strict=False, schedule=sched)
         dec_graphs.append(g)
     reps = max(50, min(2000, args.steps // 10))
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]

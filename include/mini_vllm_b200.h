@@ -58,15 +58,22 @@ extern "C" {
 #define MVB_DEV_DUP_SLOT     16   /* two tokens of one write target one slot    */
 #define MVB_DEV_TIMEOUT      32   /* a bounded pipeline wait ran out            */
 #define MVB_DEV_POSITION     64   /* a rope position outside the cos/sin table  */
+#define MVB_DEV_SCHEDULE    128   /* a decode schedule did not fit its workspace
+                                     (internal: the planned bound was wrong)   */
 
 /* ---- decode kernel variants --------------------------------------------- */
-#define MVB_DECODE_AUTO 0  /* STREAM when eligible, else MMA, else FMA           */
+#define MVB_DECODE_AUTO 0  /* SCHED when eligible, else FMA                      */
 #define MVB_DECODE_FMA  1  /* CUDA-core FP32 FMA kernel (any dtype, any BS)      */
 #define MVB_DECODE_MMA  2  /* TMA-staged tensor-core kernel, one CTA per (seq, KV head),
                               split-K + reduction for long contexts (bf16/f16, BS%16==0) */
 #define MVB_DECODE_STREAM 3 /* persistent stream-K variant of MVB_DECODE_MMA: equal tile
                               ranges per warp + a fixup kernel merging cut units
                               (num_seqs <= 4096) */
+#define MVB_DECODE_SCHED 4  /* scheduled persistent variant (AUTO's choice when bf16/f16,
+                              BS%16==0): a schedule kernel lists every (seq, KV head)
+                              unit cut into pieces of <= 32 tiles, longest first; one CTA
+                              per SM takes pieces from a global counter (TMA ring, warp
+                              roles), and the last piece of a split unit merges it */
 
 /* Logical -> physical gather of cached K/V for a batch of sequences (the
  * prefill path's prefix read) into contiguous [total_tokens, KH, D] outputs:
@@ -143,12 +150,15 @@ int mvb_build_step_metadata(const int64_t* blocks, const int64_t* block_starts, 
                             int32_t* error_flags, void* stream);
 
 /* Test hook of the bounded waits — no reference counterpart.  Runs
- * mvb_paged_decode with MVB_DECODE_STREAM, except that the load of local tile
- * `hold_tile` of stream warp `hold_warp` is never issued and every pipeline
- * wait gives up after `wait_limit` (1 .. 2^22) try-waits: that warp's wait
- * runs out, it reports MVB_DEV_TIMEOUT, waits (bounded) for its own loads in
- * flight and leaves; every other warp finishes normally and the context stays
- * usable.  Used by the failure-detection test; never needed in production. */
+ * mvb_paged_decode with `variant` (MVB_DECODE_STREAM or MVB_DECODE_SCHED),
+ * except that the load of one tile is never issued and every pipeline wait
+ * gives up after `wait_limit` (1 .. 2^22) try-waits.  The held tile is local
+ * tile `hold_tile` of stream warp `hold_warp` (MVB_DECODE_STREAM), or tile
+ * number `hold_tile` that CTA `hold_warp` loads (MVB_DECODE_SCHED).  The wait
+ * on it runs out and reports MVB_DEV_TIMEOUT; the kernel's other waits give up
+ * too (the scheduled kernel aborts the whole CTA), each role waits (bounded)
+ * for its own loads in flight and leaves, and the context stays usable.  Used
+ * by the failure-detection test; never needed in production. */
 int mvb_test_decode_wait_timeout(const void* query, int64_t q_stride_seq, int64_t q_stride_head,
                                  const void* key_cache, const void* value_cache,
                                  const int64_t* block_table, int64_t block_table_stride,
@@ -157,7 +167,8 @@ int mvb_test_decode_wait_timeout(const void* query, int64_t q_stride_seq, int64_
                                  int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
                                  int32_t block_size, int32_t num_blocks, float scale, int32_t dtype,
                                  void* workspace, int64_t workspace_bytes, int32_t* error_flags,
-                                 void* stream, int32_t hold_warp, int32_t hold_tile, int32_t wait_limit);
+                                 void* stream, int32_t hold_warp, int32_t hold_tile, int32_t wait_limit,
+                                 int32_t variant);
 
 /* Flag ORed into `variant` of mvb_paged_decode (ignored by the plan): the
  * kernel launched immediately before this call on `stream` is
@@ -169,6 +180,40 @@ int mvb_test_decode_wait_timeout(const void* query, int64_t q_stride_seq, int64_
  * dependents early and still writes query, block_table or kv_len afterwards
  * must not be followed by a call with this flag. */
 #define MVB_DECODE_AFTER_WRITE 0x100
+
+/* Flag ORed into `variant` of mvb_paged_decode with MVB_DECODE_SCHED: the
+ * workspace already holds the schedule of this batch, built by
+ * mvb_paged_decode_schedule from the same kv_len contents and shape arguments
+ * (kv_len and the block tables are the same for every layer of a model step,
+ * so one schedule serves all of them).  Without the flag the call builds the
+ * schedule itself (one extra launch).  The decode reads the schedule before
+ * its grid-dependency wait only when MVB_DECODE_AFTER_WRITE is also set; the
+ * kernel right before it is then the KV write, which starts only after the
+ * schedule kernel has finished. */
+#define MVB_DECODE_SCHEDULE_READY 0x200
+
+/*
+ * Build the decode schedule of a batch (variant MVB_DECODE_SCHED) into
+ * `workspace`: the list of pieces ("chunks") of every (sequence, KV head,
+ * head group) unit, longest first, and the counters the decode hands them out
+ * with.  It reads only kv_len (int32 [num_seqs], device memory); the shape
+ * arguments are those of the decodes that will use it, and workspace_bytes
+ * must be at least the plan's (mvb_paged_decode_plan with variant
+ * MVB_DECODE_SCHED).  A sequence whose kv_len is < 1 or needs more than
+ * max_blocks_per_seq blocks sets MVB_DEV_KV_LEN / MVB_DEV_TABLE_SHORT here and
+ * gets zero output rows from every decode that uses the schedule.  `flags`:
+ * MVB_DECODE_AFTER_WRITE when the kernel launched just before on `stream` is
+ * the KV write (the schedule is then computed while the write runs).  No
+ * reference counterpart: the Triton decode (paged_attention_gpu.py:252-321)
+ * has no per-step set-up; this hoists the work every layer's decode would
+ * repeat out of the per-layer calls.  A decode that reported MVB_DEV_TIMEOUT
+ * leaves the schedule's counters dirty: build it again before the next call.
+ */
+int mvb_paged_decode_schedule(const int32_t* kv_len, int32_t num_seqs, int32_t num_heads,
+                              int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                              int32_t num_blocks, int32_t max_blocks_per_seq, int32_t dtype,
+                              int32_t flags, void* workspace, int64_t workspace_bytes,
+                              int32_t* error_flags, void* stream);
 
 /* ABI version; bumped whenever a signature below changes. */
 int mvb_abi_version(void);

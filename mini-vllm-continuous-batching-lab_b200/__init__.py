@@ -11,6 +11,8 @@ from .attention import (
     ArgumentError,
     AttentionBackend,
     AttentionBackendB200,
+    DecodeSchedule,
+    build_decode_schedule,
     check_device_errors,
     decode_plan,
     gather_paged_kv,
@@ -35,6 +37,8 @@ __all__ = [
     "ArgumentError",
     "AttentionBackend",
     "AttentionBackendB200",
+    "DecodeSchedule",
+    "build_decode_schedule",
     "AttentionGroup",
     "AttentionMetadata",
     "KVCachePool",

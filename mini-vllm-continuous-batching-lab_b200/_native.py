@@ -39,16 +39,19 @@ DEV_SLOT_RANGE = 8
 DEV_DUP_SLOT = 16
 DEV_TIMEOUT = 32
 DEV_POSITION = 64
+DEV_SCHEDULE = 128
 
 # decode variants (MVB_DECODE_*)
 DECODE_AUTO = 0
 DECODE_FMA = 1
 DECODE_MMA = 2
 DECODE_STREAM = 3
-# flag ORed into the decode variant (MVB_DECODE_AFTER_WRITE)
+DECODE_SCHED = 4
+# flags ORed into the decode variant (MVB_DECODE_AFTER_WRITE, MVB_DECODE_SCHEDULE_READY)
 DECODE_AFTER_WRITE = 0x100
+DECODE_SCHEDULE_READY = 0x200
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 # Every symbol include/mini_vllm_b200.h declares, with (restype, argtypes).
 _i32, _i64, _u32, _f32, _vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_uint32, ctypes.c_float, ctypes.c_void_p
@@ -71,6 +74,10 @@ SIGNATURES = {
         [_vp, _i64, _i64, _vp, _vp, _vp, _i64, _i32, _vp, _vp, _i64, _i64,
          _i32, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _i32, _i32, _vp, _i64, _vp, _vp],
     ),
+    "mvb_paged_decode_schedule": (
+        _i32,
+        [_vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _i64, _vp, _vp],
+    ),
     "mvb_paged_gather": (
         _i32,
         [_vp, _vp, _vp, _i64, _i64, _i32, _vp, _vp, _vp, _vp, _i32, _i64, _i32, _i32, _i32, _i32, _i32,
@@ -88,7 +95,7 @@ SIGNATURES = {
     "mvb_test_decode_wait_timeout": (
         _i32,
         [_vp, _i64, _i64, _vp, _vp, _vp, _i64, _i32, _vp, _vp, _i64, _i64,
-         _i32, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _vp, _i64, _vp, _vp, _i32, _i32, _i32],
+         _i32, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _vp, _i64, _vp, _vp, _i32, _i32, _i32, _i32],
     ),
     "mvb_paged_decode_noalloc": (
         _i32,

@@ -52,7 +52,7 @@ _DTYPE_CODES = {
     torch.bfloat16: _native.DTYPE_BF16,
 }
 _VARIANTS = {"auto": _native.DECODE_AUTO, "fma": _native.DECODE_FMA, "mma": _native.DECODE_MMA,
-             "stream": _native.DECODE_STREAM}
+             "stream": _native.DECODE_STREAM, "sched": _native.DECODE_SCHED}
 _VARIANT_NAMES = {v: k for k, v in _VARIANTS.items()}
 
 
@@ -104,10 +104,12 @@ class _DeviceState:
             self._counters[stream] = buf
         return buf.data_ptr()
 
-    def workspace(self, nbytes: int, variant: str) -> torch.Tensor:
-        """Decode workspace of one kernel variant (the stream kernel and the
-        split-K kernels each keep their own buffer), zero-filled when allocated."""
-        key = "stream" if variant == "stream" else "split"
+    def workspace(self, nbytes: int, variant: str, stream: int = 0) -> torch.Tensor:
+        """Decode workspace of one kernel variant (the stream, scheduled and
+        split-K kernels each keep their own buffer), zero-filled when allocated.
+        The scheduled kernel's holds its schedule and hand-out counters, so each
+        stream gets its own."""
+        key = ("sched", stream) if variant == "sched" else variant if variant == "stream" else "split"
         buf = self._workspaces.get(key)
         if buf is None or buf.numel() < nbytes:
             buf = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
@@ -213,7 +215,10 @@ def _raise_flags(flags: int, detail: Optional[Dict[str, Any]]) -> None:
         rows = d.get("table_rows")
         raise IndexError(f"rope position out of range of the cos/sin table ({rows} rows)")
     if flags & _native.DEV_TIMEOUT:
-        raise RuntimeError("paged decode: a bounded pipeline wait timed out on the device")
+        raise RuntimeError("paged decode: a bounded pipeline wait timed out on the device "
+                           "(a decode schedule used by that call must be built again)")
+    if flags & _native.DEV_SCHEDULE:
+        raise RuntimeError("paged decode: the decode schedule did not fit its workspace")
     raise RuntimeError(f"unknown device error flags 0x{flags:x}")
 
 
@@ -422,7 +427,7 @@ def decode_plan(
 
 
 def _decode_fast(query, key_cache, value_cache, block_table, kv_len_after, block_size, scale, out, variant,
-                 partition_tokens, strict, after_write) -> Optional[torch.Tensor]:
+                 partition_tokens, strict, after_write, schedule=None) -> Optional[torch.Tensor]:
     """The common case of a decode in one C++ call (the direct binding), or
     None when the full path of paged_decode_attention must run instead (no
     binding, a conversion to make, an argument to reject, a failed call)."""
@@ -430,10 +435,17 @@ def _decode_fast(query, key_cache, value_cache, block_table, kv_len_after, block
     if fast is None or not query.is_cuda:
         return None
     state = _state(query.get_device())
+    flags = _native.DECODE_AFTER_WRITE if after_write else 0
+    ws = None
+    if schedule is not None:
+        if variant not in ("auto", "sched"):
+            return None
+        flags |= _native.DECODE_SCHEDULE_READY
+        ws = schedule.workspace
     status, res = fast.decode(query, key_cache, value_cache, block_table, kv_len_after, block_size,
                               -1.0 if scale is None else float(scale), out,
-                              _VARIANTS.get(variant, -1) | (_native.DECODE_AFTER_WRITE if after_write else 0),
-                              int(partition_tokens or 0), state.err_ptr)
+                              _VARIANTS.get(variant, -1) | flags,
+                              int(partition_tokens or 0), state.err_ptr, ws)
     if status != _native.OK:
         return None
     if strict:
@@ -442,6 +454,75 @@ def _decode_fast(query, key_cache, value_cache, block_table, kv_len_after, block
             _raise_flags(flags, {"kv_len_after": kv_len_after, "max_blocks": block_table.shape[1],
                                  "block_size": block_size, "num_blocks": key_cache.shape[0]})
     return res
+
+
+class DecodeSchedule:
+    """The per-step work list of the scheduled decode kernel (variant
+    ``"sched"``) and the device workspace it lives in.
+
+    kv_len and the block tables are the same for every layer of a model step,
+    so one schedule, built once per step by ``build_decode_schedule``, serves
+    every layer's ``paged_decode_attention(..., schedule=...)``.  It depends
+    only on the contents of ``kv_len_after`` and on the shapes it was built
+    for; build it again whenever those change, and after a call that raised a
+    device timeout (which leaves its counters dirty).
+    """
+
+    __slots__ = ("workspace", "key")
+
+    def __init__(self, workspace: torch.Tensor, key: tuple) -> None:
+        self.workspace = workspace
+        self.key = key
+
+
+def build_decode_schedule(
+    kv_len_after: torch.Tensor,
+    num_heads: int,
+    num_kv_heads: int,
+    head_dim: int,
+    block_size: int,
+    num_blocks: int,
+    max_blocks_per_seq: int,
+    dtype: torch.dtype,
+    *,
+    schedule: Optional[DecodeSchedule] = None,
+    after_write: bool = False,
+    strict: bool = True,
+) -> DecodeSchedule:
+    """Build the decode schedule of a batch (``mvb_paged_decode_schedule``, one
+    launch on the current stream) for decodes of the given shape.  ``schedule``
+    reuses an earlier schedule's workspace when it is large enough.
+    ``after_write``: the kernel launched just before on the current stream is
+    ``paged_cache_write`` (the schedule is then computed while it runs)."""
+    _require(kv_len_after.dim() == 1 and kv_len_after.is_cuda,
+             lambda: f"kv_len_after must be a 1-D CUDA tensor, got {tuple(kv_len_after.shape)}")
+    if kv_len_after.dtype != torch.int32 or not kv_len_after.is_contiguous():
+        kv_len_after = kv_len_after.to(torch.int32).contiguous()
+    num_seqs = kv_len_after.shape[0]
+    dev_idx = kv_len_after.get_device()
+    plan = _cached_plan(dev_idx, num_seqs, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
+                        max_blocks_per_seq, dtype, "sched", None, 16)
+    nbytes = plan["workspace_bytes"]
+    key = (dev_idx, num_seqs, num_heads, num_kv_heads, head_dim, block_size, num_blocks, max_blocks_per_seq, dtype)
+    if schedule is not None and schedule.workspace.get_device() == dev_idx and schedule.workspace.numel() >= nbytes:
+        ws = schedule.workspace
+    else:
+        ws = torch.zeros(nbytes, dtype=torch.uint8, device=kv_len_after.device)
+    state = _state(dev_idx)
+    status = _native.lib().mvb_paged_decode_schedule(
+        kv_len_after.data_ptr(), num_seqs, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
+        max_blocks_per_seq, _DTYPE_CODES[dtype], _native.DECODE_AFTER_WRITE if after_write else 0,
+        ws.data_ptr(), ws.numel(), state.err_ptr, _stream_handle(dev_idx))
+    _host_status(status, "paged decode schedule")
+    if strict:
+        flags = _take_flags(state)
+        if flags:
+            _raise_flags(flags, {"kv_len_after": kv_len_after, "max_blocks": max_blocks_per_seq,
+                                 "block_size": block_size, "num_blocks": num_blocks})
+    if schedule is not None and schedule.workspace is ws:
+        schedule.key = key
+        return schedule
+    return DecodeSchedule(ws, key)
 
 
 def paged_decode_attention(
@@ -458,6 +539,7 @@ def paged_decode_attention(
     partition_tokens: Optional[int] = None,
     strict: bool = True,
     after_write: bool = False,
+    schedule: Optional[DecodeSchedule] = None,
 ) -> torch.Tensor:
     """Paged decode attention (one query token per sequence) on the B200 kernels.
 
@@ -469,18 +551,22 @@ def paged_decode_attention(
         block_size: tokens per block (power of two).
         scale: softmax scale, default ``head_dim ** -0.5``.
     Keyword-only extensions: ``out`` (write in place), ``variant``
-    (``"auto" | "stream" | "mma" | "fma"``), ``partition_tokens`` (split-K
-    partition length of the ``"mma"`` / ``"fma"`` kernels; ``None`` lets the
-    library choose), ``strict``, ``after_write`` (the kernel launched just
-    before this call on the current stream is ``paged_cache_write``: the stream
-    kernel then reads query, block table and kv_len while the write is still
-    running and waits only before its cache loads; leave it False when any
-    other kernel may run in between and signal its dependents early).
+    (``"auto" | "sched" | "stream" | "mma" | "fma"``; ``"auto"`` is
+    ``"sched"`` for bf16/f16 caches with block sizes that are multiples of 16),
+    ``partition_tokens`` (split-K partition length of the ``"mma"`` / ``"fma"``
+    kernels; ``None`` lets the library choose), ``strict``, ``after_write``
+    (the kernel launched just before this call on the current stream is
+    ``paged_cache_write``: the kernel then reads query, block table, kv_len
+    and schedule while the write is still running and waits only before its
+    cache loads; leave it False when any other kernel may run in between and
+    signal its dependents early), ``schedule`` (a ``DecodeSchedule`` of this
+    batch from ``build_decode_schedule``: the ``"sched"`` kernel then skips its
+    own schedule launch; without it every call builds the schedule first).
 
     Returns ``[total_decode, num_q_heads, head_dim]`` in the query's dtype.
     """
     res = _decode_fast(query, key_cache, value_cache, block_table, kv_len_after, block_size, scale, out,
-                       variant, partition_tokens, strict, after_write)
+                       variant, partition_tokens, strict, after_write, schedule)
     if res is not None:
         return res
     # anything else takes the full path below
@@ -524,7 +610,16 @@ def paged_decode_attention(
                         num_blocks, max_blocks, query.dtype, variant, partition_tokens,
                         16 if key_cache.data_ptr() % 16 == 0 else 8)
     ws_bytes = plan["workspace_bytes"]
-    ws_ptr = state.workspace(ws_bytes, plan["variant"]).data_ptr() if ws_bytes > 0 else None
+    flags = _native.DECODE_AFTER_WRITE if after_write else 0
+    if schedule is not None:
+        _require(plan["variant"] == "sched", lambda: f"schedule= needs the 'sched' kernel, the plan is {plan['variant']!r}")
+        _require(schedule.workspace.get_device() == dev_idx and schedule.workspace.numel() >= ws_bytes,
+                 "the schedule was built for another device or a smaller shape")
+        ws_ptr, ws_bytes = schedule.workspace.data_ptr(), schedule.workspace.numel()
+        flags |= _native.DECODE_SCHEDULE_READY
+    else:
+        ws_ptr = state.workspace(ws_bytes, plan["variant"], _stream_handle(dev_idx)).data_ptr() \
+            if ws_bytes > 0 else None
     status = _native.lib().mvb_paged_decode(
         query.data_ptr(), query.stride(0), query.stride(1),
         key_cache.data_ptr(), value_cache.data_ptr(),
@@ -533,7 +628,7 @@ def paged_decode_attention(
         out.data_ptr(), out.stride(0), out.stride(1),
         total_decode, num_q_heads, num_kv_heads, head_dim, block_size, num_blocks,
         float(scale), _DTYPE_CODES[query.dtype],
-        _VARIANTS[variant] | (_native.DECODE_AFTER_WRITE if after_write else 0), int(partition_tokens or 0),
+        _VARIANTS[variant] | flags, int(partition_tokens or 0),
         ws_ptr, ws_bytes, state.err.data_ptr(), _stream_handle(dev_idx),
     )
     _host_status(status, "paged decode")
@@ -829,6 +924,18 @@ class AttentionBackendB200(AttentionBackend):
         # early and writes the decode's inputs (plain torch kernels do not).
         self.overlap_after_write = overlap_after_write
         self._last_write: Optional[Tuple[int, int]] = None
+        # The decode schedule of the current step (variant "sched"): built at
+        # layer 0 of every step and whenever the metadata object, its
+        # tensors or the shapes change; every other layer reuses it.
+        self._schedule: Optional[DecodeSchedule] = None
+        self._schedule_key: Optional[tuple] = None
+
+    def begin_step(self) -> None:
+        """Forget the current step's decode schedule, so the next decode builds
+        a new one.  Layer 0 and a new metadata object already do this; a
+        caller that rewrites the metadata tensors in place between the layers
+        of a step calls it after doing so."""
+        self._schedule_key = None
 
     def allocate_pool(self, num_layers: int, num_blocks: int, block_size: int, num_kv_heads: int,
                       head_dim: int, dtype: torch.dtype, device: torch.device) -> KVCachePool:
@@ -867,13 +974,44 @@ class AttentionBackendB200(AttentionBackend):
         after = last is not None and query.is_cuda and last == (layer_idx, _stream_handle(query.get_device()))
         kc, vc = pool.key_caches[layer_idx], pool.value_caches[layer_idx]
         bt, kvl = attn_metadata.decode_block_tables, group.kv_len_after
+        schedule = self._step_schedule(layer_idx, query, kc, bt, kvl, attn_metadata, pool.block_size, after)
+        if schedule is not None and self._schedule_built_now:
+            after = False  # the decode now follows the schedule launch, not the write
         # the common case straight to the binding (per-step host time); else the full path
         res = _decode_fast(query, kc, vc, bt, kvl, pool.block_size, None, out, self.decode_variant,
-                           self.partition_tokens, self.strict, after)
+                           self.partition_tokens, self.strict, after, schedule)
         if res is not None:
             return res
         return paged_decode_attention(query, kc, vc, bt, kvl, pool.block_size, out=out, variant=self.decode_variant,
-                                      partition_tokens=self.partition_tokens, strict=self.strict, after_write=after)
+                                      partition_tokens=self.partition_tokens, strict=self.strict, after_write=after,
+                                      schedule=schedule)
+
+    _schedule_built_now = False
+
+    def _step_schedule(self, layer_idx, query, kc, bt, kvl, attn_metadata, block_size, after) -> Optional[DecodeSchedule]:
+        """The decode schedule of this step for the "sched" kernel, built when
+        needed (None when the decode runs another kernel)."""
+        self._schedule_built_now = False
+        if self.decode_variant not in ("auto", "sched") or not (query.is_cuda and kvl.is_cuda and bt.is_cuda):
+            return None
+        if query.dtype not in (torch.bfloat16, torch.float16) or block_size % 16 or kc.dtype != query.dtype:
+            return None
+        key = (id(attn_metadata), bt.data_ptr(), kvl.data_ptr(), tuple(bt.shape), tuple(query.shape[1:]),
+               tuple(kc.shape), query.dtype, kvl.dtype)
+        if layer_idx != 0 and key == self._schedule_key and self._schedule is not None:
+            return self._schedule
+        plan = _cached_plan(query.get_device(), query.shape[0], query.shape[1], kc.shape[1], query.shape[2],
+                            block_size, kc.shape[0], bt.shape[1], query.dtype, self.decode_variant,
+                            self.partition_tokens, 16 if kc.data_ptr() % 16 == 0 else 8)
+        if plan["variant"] != "sched":
+            return None
+        self._schedule_key = None
+        self._schedule = build_decode_schedule(kvl, query.shape[1], kc.shape[1], query.shape[2], block_size,
+                                               kc.shape[0], bt.shape[1], query.dtype, schedule=self._schedule,
+                                               after_write=after, strict=False)
+        self._schedule_key = key
+        self._schedule_built_now = True
+        return self._schedule
 
     def prefill_attention(self, layer_idx: int, query: torch.Tensor, key: Optional[torch.Tensor],
                           value: Optional[torch.Tensor], attn_metadata: Any, pool: Any) -> torch.Tensor:

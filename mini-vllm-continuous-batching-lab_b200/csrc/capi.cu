@@ -24,6 +24,12 @@ cudaError_t launch_decode_stream(const CUtensorMap& tmk, const CUtensorMap& tmv,
                                  int sm_count, cudaStream_t stream);
 int stream_warps_per_cta(int head_dim);
 int stream_smem_bytes(int head_dim, int num_seqs);
+SchedLayout sched_layout(int num_seqs, int num_kv_heads, int head_groups, int G, int max_blocks,
+                         int block_size, int head_dim, int ctas);
+cudaError_t launch_decode_schedule(const DecodeArgs& a, const SchedLayout& l, void* ws, int ctas, bool wait_at_end,
+                                   cudaStream_t stream);
+cudaError_t launch_decode_sched(const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a, int dtype,
+                                int head_dim, const SchedLayout& l, void* ws, int ctas, cudaStream_t stream);
 
 // cuTensorMapEncodeTiled from the driver (nullptr when the driver lacks it);
 // shared by the decode (pool maps) and the gather (output maps).
@@ -43,7 +49,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 namespace {
 
-constexpr int kAbiVersion = 2;
+constexpr int kAbiVersion = 3;
 // Longest context the auto plan serves with one CTA per (sequence, KV head);
 // beyond it the flash-decoding split is used.
 constexpr int64_t kUnsplitMaxTokens = 8192;
@@ -99,6 +105,7 @@ struct Plan {
   int64_t off_m, off_l;  // workspace offsets of the m / l arrays
   int max_warps;         // stream variant: warps the partial-state slots cover
   int64_t off_part;      // stream variant: workspace offset of the partial slots
+  SchedLayout sched;     // sched variant: workspace layout
 };
 
 int make_plan(int num_seqs, int num_heads, int num_kv_heads, int head_dim, int block_size,
@@ -122,11 +129,31 @@ int make_plan(int num_seqs, int num_heads, int num_kv_heads, int head_dim, int b
   const int khg16 = num_kv_heads * ((G + kMmaHeadGroup - 1) / kMmaHeadGroup);
   const bool stream_ok = mma_ok && num_seqs <= kStreamMaxSeqs &&
                          (int64_t)num_seqs * khg16 * max_ctx_tiles < ((int64_t)1 << 31);
+  const int hg16 = (G + kMmaHeadGroup - 1) / kMmaHeadGroup;
+  SchedLayout sl = sched_layout(num_seqs, num_kv_heads, hg16, G, max_blocks, block_size, head_dim,
+                                sm_count_current());
+  const bool sched_ok = mma_ok && sl.max_chunks < ((int64_t)1 << 30);
   int v = variant;
-  if (v == MVB_DECODE_AUTO) v = stream_ok ? MVB_DECODE_STREAM : mma_ok ? MVB_DECODE_MMA : MVB_DECODE_FMA;
-  if (v != MVB_DECODE_FMA && v != MVB_DECODE_MMA && v != MVB_DECODE_STREAM) return MVB_ERR_VARIANT;
+  if (v == MVB_DECODE_AUTO) v = sched_ok ? MVB_DECODE_SCHED : MVB_DECODE_FMA;
+  if (v != MVB_DECODE_FMA && v != MVB_DECODE_MMA && v != MVB_DECODE_STREAM && v != MVB_DECODE_SCHED)
+    return MVB_ERR_VARIANT;
   if (v == MVB_DECODE_MMA && !mma_ok) return MVB_ERR_VARIANT;
   if (v == MVB_DECODE_STREAM && !stream_ok) return MVB_ERR_VARIANT;
+  if (v == MVB_DECODE_SCHED && !sched_ok) return MVB_ERR_VARIANT;
+  pl->sched = sl;
+
+  if (v == MVB_DECODE_SCHED) {
+    pl->variant = v;
+    pl->part_tokens = 0;
+    pl->num_parts = 0;
+    pl->head_groups = hg16;
+    pl->maxg = kMmaHeadGroup;
+    pl->max_bids = 0;
+    pl->max_warps = 0;
+    pl->off_m = pl->off_l = pl->off_part = 0;
+    pl->ws_bytes = sl.bytes;
+    return MVB_OK;
+  }
 
   if (v == MVB_DECODE_STREAM) {
     // One contiguous tile range per warp; workspace = one 32-byte cut-unit
@@ -310,7 +337,7 @@ int mvb_paged_decode_plan(int32_t num_seqs, int32_t num_heads, int32_t num_kv_he
                           int32_t* partition_tokens_out, int32_t* num_partitions_out,
                           int64_t* workspace_bytes_out) {
   Plan pl;
-  variant &= ~MVB_DECODE_AFTER_WRITE;  // a launch-ordering hint: no effect on the plan
+  variant &= ~(MVB_DECODE_AFTER_WRITE | MVB_DECODE_SCHEDULE_READY);  // launch-ordering hints: no effect on the plan
   const int st = make_plan(num_seqs, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
                            max_blocks_per_seq, dtype, variant, partition_tokens, cache_ptr, &pl);
   if (st != MVB_OK) return st;
@@ -333,7 +360,8 @@ int mvb_paged_decode(const void* query, int64_t q_stride_seq, int64_t q_stride_h
   mvb::NvtxRange nvtx_range("mvb_paged_decode");
   Plan pl;
   const bool after_write = (variant & MVB_DECODE_AFTER_WRITE) != 0;
-  variant &= ~MVB_DECODE_AFTER_WRITE;
+  const bool sched_ready = (variant & MVB_DECODE_SCHEDULE_READY) != 0;
+  variant &= ~(MVB_DECODE_AFTER_WRITE | MVB_DECODE_SCHEDULE_READY);
   const int st = make_plan(num_seqs, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
                            max_blocks_per_seq, dtype, variant, partition_tokens, key_cache, &pl);
   if (st != MVB_OK) return st;
@@ -391,6 +419,22 @@ int mvb_paged_decode(const void* query, int64_t q_stride_seq, int64_t q_stride_h
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e;
+  if (pl.variant == MVB_DECODE_SCHED) {
+    const int64_t rows = (int64_t)num_blocks * num_kv_heads * block_size;
+    CUtensorMap tmk, tmv;
+    if (!pool_tensor_map(key_cache, rows, head_dim, dtype, &tmk) ||
+        !pool_tensor_map(value_cache, rows, head_dim, dtype, &tmv))
+      return MVB_ERR_TENSOR_MAP;
+    const int ctas = sm_count_current();
+    if (!sched_ready) {
+      // build the schedule first; the decode then waits for it before reading anything
+      e = launch_decode_schedule(a, pl.sched, workspace, ctas, after_write, s);
+      if (e != cudaSuccess) return MVB_ERR_CUDA;
+      a.early_inputs = 0;
+    }
+    e = launch_decode_sched(tmk, tmv, a, dtype, head_dim, pl.sched, workspace, ctas, s);
+    return e == cudaSuccess ? MVB_OK : MVB_ERR_CUDA;
+  }
   if (pl.variant == MVB_DECODE_STREAM) {
     const int64_t rows = (int64_t)num_blocks * num_kv_heads * block_size;
     CUtensorMap tmk, tmv;
@@ -420,6 +464,38 @@ int mvb_paged_decode(const void* query, int64_t q_stride_seq, int64_t q_stride_h
   return MVB_OK;
 }
 
+int mvb_paged_decode_schedule(const int32_t* kv_len, int32_t num_seqs, int32_t num_heads,
+                              int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                              int32_t num_blocks, int32_t max_blocks_per_seq, int32_t dtype,
+                              int32_t flags, void* workspace, int64_t workspace_bytes,
+                              int32_t* error_flags, void* stream) {
+  mvb::NvtxRange nvtx_range("mvb_paged_decode_schedule");
+  Plan pl;
+  const int st = make_plan(num_seqs, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
+                           max_blocks_per_seq, dtype, MVB_DECODE_SCHED, 0, nullptr, &pl);
+  if (st != MVB_OK) return st;
+  if ((flags & ~MVB_DECODE_AFTER_WRITE) != 0) return MVB_ERR_INVALID_ARG;
+  if (num_seqs == 0) return MVB_OK;
+  if (!kv_len || !error_flags) return MVB_ERR_INVALID_ARG;
+  if (workspace == nullptr || workspace_bytes < pl.ws_bytes || !aligned_to(workspace, 256))
+    return MVB_ERR_WORKSPACE;
+  DecodeArgs a = {};
+  a.kv_len = kv_len;
+  a.num_seqs = num_seqs;
+  a.num_heads = num_heads;
+  a.num_kv_heads = num_kv_heads;
+  a.G = num_heads / num_kv_heads;
+  a.head_groups = pl.head_groups;
+  a.block_size = block_size;
+  a.max_blocks = max_blocks_per_seq;
+  a.num_blocks = num_blocks;
+  a.err = error_flags;
+  const cudaError_t e = launch_decode_schedule(a, pl.sched, workspace, sm_count_current(),
+                                               (flags & MVB_DECODE_AFTER_WRITE) != 0,
+                                               static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MVB_OK : MVB_ERR_CUDA;
+}
+
 }  // extern "C"
 
 extern "C" int mvb_test_decode_wait_timeout(
@@ -428,15 +504,16 @@ extern "C" int mvb_test_decode_wait_timeout(
     const int32_t* kv_len, void* out, int64_t out_stride_seq, int64_t out_stride_head, int32_t num_seqs,
     int32_t num_heads, int32_t num_kv_heads, int32_t head_dim, int32_t block_size, int32_t num_blocks,
     float scale, int32_t dtype, void* workspace, int64_t workspace_bytes, int32_t* error_flags, void* stream,
-    int32_t hold_warp, int32_t hold_tile, int32_t wait_limit) {
+    int32_t hold_warp, int32_t hold_tile, int32_t wait_limit, int32_t variant) {
   if (hold_warp < 0 || hold_tile < 0 || wait_limit <= 0 || wait_limit > kWaitSpinLimit) return MVB_ERR_INVALID_ARG;
+  if (variant != MVB_DECODE_STREAM && variant != MVB_DECODE_SCHED) return MVB_ERR_VARIANT;
   g_hold_warp = hold_warp;
   g_hold_tile = hold_tile;
   g_wait_limit = wait_limit;
   const int st = mvb_paged_decode(query, q_stride_seq, q_stride_head, key_cache, value_cache, block_table,
                                   block_table_stride, max_blocks_per_seq, kv_len, out, out_stride_seq,
                                   out_stride_head, num_seqs, num_heads, num_kv_heads, head_dim, block_size,
-                                  num_blocks, scale, dtype, MVB_DECODE_STREAM, 0, workspace, workspace_bytes,
+                                  num_blocks, scale, dtype, variant, 0, workspace, workspace_bytes,
                                   error_flags, stream);
   g_hold_warp = -1;
   g_hold_tile = -1;

@@ -56,7 +56,8 @@ extern "C" int mvb_paged_decode_noalloc(
   mvb::NvtxRange nvtx_range("mvb_paged_decode_noalloc");
   // The split-K family only: tensor-core kernel when eligible, else CUDA cores.
   variant &= ~MVB_DECODE_AFTER_WRITE;  // the split-K kernels read every input after the wait
-  if (variant == MVB_DECODE_STREAM) return MVB_ERR_VARIANT;
+  if (variant != MVB_DECODE_AUTO && variant != MVB_DECODE_FMA && variant != MVB_DECODE_MMA)
+    return MVB_ERR_VARIANT;  // the stream and scheduled kernels, flags, unknown values
   int32_t v = variant, pt = 0, parts = 0;
   int64_t ws = 0;
   int st = MVB_ERR_VARIANT;

@@ -1,0 +1,634 @@
+// Scheduled persistent paged decode (bf16 / f16, block_size a multiple of 16).
+//
+// Two kernels.
+//
+// decode_schedule_kernel (once per model step: kv_len and the block tables are
+// the same for every layer of a step) cuts every unit — (sequence, KV head,
+// head group of <= 16 query heads) — into pieces of at most `piece` 16-token
+// tiles, split evenly (piece sizes of one unit differ by at most one tile),
+// and lists the pieces ("chunks") longest first: units are bucketed by piece
+// size, buckets in decreasing order, and the pieces of one unit are adjacent.
+// `piece` is chosen from the step's total tile count so that there are about
+// two chunks per CTA of the decode grid or more (4..32 tiles).
+//
+// decode_sched_kernel runs one CTA per SM over that list.  Each CTA takes its
+// first chunk by index (blockIdx.x) and every further one from a global
+// counter, so SMs that stream faster take more chunks and the last chunks
+// handed out are the smallest: no per-warp static range, no random tail.
+// Warp roles inside the CTA:
+//   * fetcher (warp 0): takes the next chunk index, loads its descriptor, the
+//     block ids of its tiles (validated, turned into pool rows) and the query
+//     rows of its head group, and publishes them in one of 4 chunk slots;
+//   * issuer (warp 1, lane 0): walks the published chunks and issues two 2-D
+//     TMA tile loads (K and V, 16 rows x D, 128-byte swizzle) per tile into a
+//     STAGES-deep ring (one full / one empty mbarrier per stage);
+//   * consumers (warps 2-5): tile i of a chunk goes to consumer i % 4, which
+//     runs attend_tile (mma.sync m16n8k16, online softmax, fp32 accumulate);
+//     at the chunk end the four states are merged through shared memory.
+// A chunk that holds a whole unit is normalised and written to `out`; a piece
+// of a longer unit writes its partial state (O, m, l per head row) and counts
+// itself in on the unit's arrival counter, and the last piece to arrive merges
+// all pieces in piece order (deterministic) and writes the unit.  While the
+// consumers merge, the fetcher and the issuer keep the ring full.
+//
+// Every wait is bounded (DecodeArgs::wait_limit); a wait that runs out sets
+// MVB_DEV_TIMEOUT and a CTA-wide abort flag that every other wait polls, the
+// issuer then waits (bounded) for its loads in flight, and every role leaves.
+// The work counters are then left dirty: the schedule must be rebuilt (the
+// schedule kernel resets every counter it hands to the decode).
+#include "mma_tile.cuh"
+
+namespace mvb {
+
+constexpr int kSchedMaxPiece = 32;  // tiles per chunk at most: one block id per fetcher lane
+constexpr int kSchedMinPiece = 4;
+constexpr int kSchedSlots = 4;      // chunk slots between the fetcher and the other roles
+constexpr int kSchedConsumers = 4;  // consumer warps
+constexpr int kSchedThreads = (2 + kSchedConsumers) * 32;
+constexpr int kSchedBuildThreads = 1024;
+
+// Workspace header (256 bytes at the start of the workspace).
+struct SchedHeader {
+  int n_chunks;
+  int piece;        // tiles per chunk at most, as chosen
+  int next;         // chunk hand-out counter (zero at rest)
+  int done;         // CTAs whose fetcher saw the end of the list (zero at rest)
+  int total_tiles;  // tiles of all units
+  int pad[59];
+};
+static_assert(sizeof(SchedHeader) == 256, "header is 256 bytes");
+
+// Chunk descriptor: two int4
+//   {sequence, unit of the sequence (kvh * head_groups + hg), first tile, tiles}
+//   {first chunk of the unit, pieces of the unit, kv_len, bad sequence flag}
+// A bad sequence (kv_len < 1 or a block table too short) has one chunk of zero
+// tiles per unit: its output rows are written as zeros.
+struct SchedArgs {
+  SchedHeader* hdr;
+  const int4* desc;  // [max_chunks][2]
+  int* ucnt;         // [max_chunks] arrival counters, indexed by a unit's first chunk
+  float* part;       // [max_chunks][mg][D + 4] partial O (D), m, l
+  int max_chunks;
+  int mg;            // partial rows per chunk: min(16, G)
+};
+
+// ---------------------------------------------------------------------------
+// schedule
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int sched_seq_error(int ctx, int block_size, int max_blocks) {
+  if (ctx < 1) return MVB_DEV_KV_LEN;
+  const int64_t need = ((int64_t)ctx + block_size - 1) / block_size;
+  if (need > max_blocks) return MVB_DEV_TABLE_SHORT;
+  return 0;
+}
+
+// One CTA.  wait_at_end: the previous kernel in the stream may still be running
+// and writes none of this kernel's inputs (the KV write); the kernel computes
+// first and waits for it only before exiting, so that a dependent of this
+// kernel that waits for it also waits for that previous kernel.
+__global__ void __launch_bounds__(kSchedBuildThreads)
+decode_schedule_kernel(const int* __restrict__ kv_len, int num_seqs, int units_per_seq, int block_size,
+                       int max_blocks, int ctas, SchedHeader* hdr, int4* desc, int* ucnt, int max_chunks,
+                       int* err, int wait_at_end) {
+  __shared__ int s_hist[kSchedMaxPiece + 1];
+  __shared__ int s_base[kSchedMaxPiece + 1];
+  __shared__ long long s_red[kSchedBuildThreads / 32];
+  __shared__ int s_piece, s_overflow;
+  if (!wait_at_end) grid_dependency_wait();
+  grid_launch_dependents();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid <= kSchedMaxPiece) s_hist[tid] = 0;
+
+  // total tiles of all units
+  long long tiles = 0;
+  for (int s = tid; s < num_seqs; s += blockDim.x) {
+    const int ctx = __ldg(kv_len + s);
+    if (!sched_seq_error(ctx, block_size, max_blocks)) tiles += (ctx + kTile - 1) / kTile;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) tiles += __shfl_xor_sync(0xffffffffu, tiles, o);
+  if (lane == 0) s_red[warp] = tiles;
+  __syncthreads();
+  if (tid == 0) {
+    long long t = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += s_red[w];
+    t *= units_per_seq;
+    long long pc = (t + 2LL * ctas - 1) / (2LL * ctas);
+    if (pc < kSchedMinPiece) pc = kSchedMinPiece;
+    if (pc > kSchedMaxPiece) pc = kSchedMaxPiece;
+    s_piece = (int)pc;
+    hdr->piece = (int)pc;
+    hdr->total_tiles = (int)(t < 0x7fffffffLL ? t : 0x7fffffffLL);
+  }
+  __syncthreads();
+  const int piece = s_piece;
+
+  // histogram of chunks by piece size (bucket 0: bad sequences)
+  for (int s = tid; s < num_seqs; s += blockDim.x) {
+    const int ctx = __ldg(kv_len + s);
+    const bool bad = sched_seq_error(ctx, block_size, max_blocks) != 0;
+    const int nt = bad ? 0 : (ctx + kTile - 1) / kTile;
+    const int p = bad ? 1 : (nt + piece - 1) / piece;
+    const int ps = bad ? 0 : (nt + p - 1) / p;
+    atomicAdd(&s_hist[ps], p * units_per_seq);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int run = 0;
+    for (int b = kSchedMaxPiece; b >= 0; --b) {
+      s_base[b] = run;
+      run += s_hist[b];
+    }
+    s_overflow = run > max_chunks;
+    if (s_overflow) {  // cannot happen with the host's bound; refuse rather than overrun
+      atomicOr(err, MVB_DEV_SCHEDULE);
+      run = 0;
+    }
+    hdr->n_chunks = run;
+    hdr->next = 0;
+    hdr->done = 0;
+  }
+  __syncthreads();
+  const bool overflow = s_overflow != 0;
+
+  // descriptors; within a bucket the order is arbitrary (it only affects which
+  // CTA takes a chunk, never the arithmetic of any output)
+  for (int s = tid; s < num_seqs; s += blockDim.x) {
+    const int ctx = __ldg(kv_len + s);
+    const int bad = sched_seq_error(ctx, block_size, max_blocks);
+    if (bad) atomicOr(err, bad);
+    if (overflow) continue;
+    const int nt = bad ? 0 : (ctx + kTile - 1) / kTile;
+    const int p = bad ? 1 : (nt + piece - 1) / piece;
+    const int ps = bad ? 0 : (nt + p - 1) / p;
+    const int c0 = atomicAdd(&s_base[ps], p * units_per_seq);
+    for (int k = 0; k < units_per_seq; ++k) {
+      const int first = c0 + k * p;
+      ucnt[first] = 0;
+      for (int i = 0; i < p; ++i) {
+        const int b0 = (int)((int64_t)i * nt / p), b1 = (int)((int64_t)(i + 1) * nt / p);
+        desc[2 * (first + i)] = make_int4(s, k, b0, b1 - b0);
+        desc[2 * (first + i) + 1] = make_int4(first, p, ctx, bad ? 1 : 0);
+      }
+    }
+  }
+  if (wait_at_end) grid_dependency_wait();
+}
+
+// ---------------------------------------------------------------------------
+// decode
+// ---------------------------------------------------------------------------
+template <int D, int STAGES> struct SchedSmem {
+  using Geo = MmaGeom<D>;
+  static constexpr int QP = D + 8;  // query row pitch (elements): conflict-free fragment loads
+  static constexpr int SLOT_BYTES = 32 + 4 * kSchedMaxPiece + 16 * QP * 2;
+  static constexpr int RING = 0;
+  static constexpr int SLOTS = RING + STAGES * Geo::STAGE_BYTES;
+  static constexpr int MERGE_O = SLOTS + kSchedSlots * SLOT_BYTES;          // float [2][4][16][D]
+  static constexpr int MERGE_ML = MERGE_O + 2 * kSchedConsumers * 16 * D * 4;  // float2 [2][4][16]
+  static constexpr int BARS = MERGE_ML + 2 * kSchedConsumers * 16 * 8;
+  static constexpr int NBARS = 2 * STAGES + 2 * kSchedSlots + 1;
+  static constexpr int STAGE_BAD = BARS + NBARS * 8;
+  static constexpr int MISC = STAGE_BAD + STAGES * 4;
+  static constexpr int BYTES = MISC + 16;
+  static_assert(SLOTS % 16 == 0 && MERGE_O % 16 == 0 && BARS % 8 == 0, "alignment");
+};
+
+// Bounded wait that also gives up when another role has aborted the CTA.
+__device__ __forceinline__ bool sched_wait(uint32_t bar, uint32_t parity, int limit, volatile int* abort_flag,
+                                           int* err) {
+  for (int i = 0; i < limit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 31) == 31 && *abort_flag) return false;
+  }
+  *abort_flag = 1;
+  atomicOr(err, MVB_DEV_TIMEOUT);
+  return false;
+}
+
+// The same for all 32 lanes of a warp (true only when every lane got the phase).
+__device__ __forceinline__ bool sched_wait_warp(uint32_t bar, uint32_t parity, int limit,
+                                                volatile int* abort_flag, int* err) {
+  const bool ok = sched_wait(bar, parity, limit, abort_flag, err);
+  return __all_sync(0xffffffffu, ok);
+}
+
+template <typename T, int D, int STAGES>
+__global__ void __launch_bounds__(kSchedThreads, 1)
+decode_sched_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                    const DecodeArgs a, const SchedArgs sa) {
+  using Geo = MmaGeom<D>;
+  using L = SchedSmem<D, STAGES>;
+  constexpr int KC = D / 16, NO = D / 8, QP = L::QP, PR = D + 4;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem =
+      reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = smem + L::RING;
+  uint8_t* slots = smem + L::SLOTS;
+  float* merge_o = reinterpret_cast<float*>(smem + L::MERGE_O);
+  float2* merge_ml = reinterpret_cast<float2*>(smem + L::MERGE_ML);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BARS);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* cfull = bars + 2 * STAGES;
+  uint64_t* cempty = cfull + kSchedSlots;
+  uint64_t* cbar = cempty + kSchedSlots;
+  volatile int* stage_bad = reinterpret_cast<volatile int*>(smem + L::STAGE_BAD);
+  volatile int* misc = reinterpret_cast<volatile int*>(smem + L::MISC);  // [0] abort, [1] arrival broadcast
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(full + s), 1);
+      mbar_init(smem_u32(empty + s), 32);  // every lane of the consuming warp
+    }
+    for (int c = 0; c < kSchedSlots; ++c) {
+      mbar_init(smem_u32(cfull + c), 32);                        // every fetcher lane
+      mbar_init(smem_u32(cempty + c), 1 + kSchedConsumers * 32);  // issuer + every consumer lane
+    }
+    mbar_init(smem_u32(cbar), kSchedConsumers * 32);
+    misc[0] = 0;
+    misc[1] = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();  // the only CTA-wide barrier
+  grid_launch_dependents();
+  volatile int* abort_flag = misc;
+  const int limit = a.wait_limit;
+
+  auto slot_desc = [&](int slot) { return reinterpret_cast<int4*>(slots + slot * L::SLOT_BYTES); };
+  auto slot_rows = [&](int slot) { return reinterpret_cast<int*>(slots + slot * L::SLOT_BYTES + 32); };
+  auto slot_q = [&](int slot) {
+    return reinterpret_cast<T*>(slots + slot * L::SLOT_BYTES + 32 + 4 * kSchedMaxPiece);
+  };
+
+  if (warp == 0) {
+    // ================================ fetcher ================================
+    if (!a.early_inputs) grid_dependency_wait();
+    bool waited = a.early_inputs == 0;
+    const int n_chunks = __ldcg(&sa.hdr->n_chunks);
+    int idx = blockIdx.x;
+    bool aborted = false;
+    for (int k = 0;; ++k) {
+      const int slot = k % kSchedSlots;
+      const bool have = idx < n_chunks;
+      int4 d0 = make_int4(0, 0, 0, -1), d1 = make_int4(0, 0, 0, 0);
+      if (have) {
+        d0 = __ldcg(sa.desc + 2 * idx);
+        d1 = __ldcg(sa.desc + 2 * idx + 1);
+      }
+      const int seq = d0.x, uk = d0.y, begin = d0.z, n = d0.w;
+      const int kvh = uk / a.head_groups, hg = uk - kvh * a.head_groups;
+      const int h0 = kvh * a.G + hg * 16, nh = min(16, a.G - hg * 16);
+      // block id -> pool row of tile `lane` of the chunk
+      int row = -1;
+      if (lane < n) {
+        const int tok = (begin + lane) * kTile;
+        const int bi = tok / a.block_size;
+        const int64_t b = __ldg(a.bt + (int64_t)seq * a.bt_s0 + bi);
+        if (b >= 0 && b < a.num_blocks)
+          row = ((int)b * a.num_kv_heads + kvh) * a.block_size + (tok - bi * a.block_size);
+        else
+          atomicOr(a.err, MVB_DEV_BLOCK_ID);
+      }
+      // query rows of the head group, 16 x D, zero past nh (4-byte words)
+      constexpr int QW = 16 * D / 2 / 32;  // words per lane
+      uint32_t qw[QW];
+      const T* qbase = static_cast<const T*>(a.q) + (int64_t)seq * a.q_s0 + (int64_t)h0 * a.q_s1;
+#pragma unroll
+      for (int v = 0; v < QW; ++v) {
+        const int e = lane + 32 * v, r = e / (D / 2), c = e - r * (D / 2);
+        qw[v] = (n > 0 && r < nh) ? ld_u32(qbase + (int64_t)r * a.q_s1 + 2 * c) : 0u;
+      }
+      if (!waited) {  // the hand-out counter is reset by the previous decode
+        grid_dependency_wait();
+        waited = true;
+      }
+      int nxt = 0;
+      if (have) {
+        if (lane == 0) nxt = (int)gridDim.x + atomicAdd(&sa.hdr->next, 1);
+        nxt = __shfl_sync(0xffffffffu, nxt, 0);
+      }
+      if (k >= kSchedSlots &&
+          !sched_wait_warp(smem_u32(cempty + slot), (uint32_t)((k / kSchedSlots - 1) & 1), limit, abort_flag,
+                           a.err)) {
+        aborted = true;
+        break;
+      }
+      if (lane == 0) {
+        slot_desc(slot)[0] = d0;
+        slot_desc(slot)[1] = make_int4(d1.x, d1.y, d1.z, idx);  // .w: the chunk's own index
+      }
+      slot_rows(slot)[lane] = row;
+      uint32_t* qs = reinterpret_cast<uint32_t*>(slot_q(slot));
+#pragma unroll
+      for (int v = 0; v < QW; ++v) {
+        const int e = lane + 32 * v, r = e / (D / 2), c = e - r * (D / 2);
+        qs[r * (QP / 2) + c] = qw[v];
+      }
+      mbar_arrive(smem_u32(cfull + slot));
+      if (!have) break;  // the end marker is published
+      idx = nxt;
+    }
+    if (!aborted && lane == 0) {
+      // the last CTA to reach the end of the list resets the counters
+      const int prev = atomicAdd(&sa.hdr->done, 1);
+      if (prev == (int)gridDim.x - 1) {
+        atomicExch(&sa.hdr->next, 0);
+        atomicExch(&sa.hdr->done, 0);
+      }
+    }
+    return;
+  }
+
+  if (warp == 1) {
+    // ================================ issuer =================================
+    if (lane != 0) return;
+    grid_dependency_wait();  // the cache is complete from here on
+    prefetch_tensormap(&tmk);
+    prefetch_tensormap(&tmv);
+    const uint64_t pol = l2_policy_evict_first();
+    int j = 0;
+    for (int k = 0;; ++k) {
+      const int slot = k % kSchedSlots;
+      if (!sched_wait(smem_u32(cfull + slot), (uint32_t)((k / kSchedSlots) & 1), limit, abort_flag, a.err))
+        break;
+      const int n = slot_desc(slot)[0].w;
+      if (n < 0) break;
+      const int* rows = slot_rows(slot);
+      bool ok = true;
+      for (int i = 0; i < n; ++i, ++j) {
+        const int st = j % STAGES;
+        if (j >= STAGES &&
+            !sched_wait(smem_u32(empty + st), (uint32_t)((j / STAGES - 1) & 1), limit, abort_flag, a.err)) {
+          ok = false;
+          break;
+        }
+        const int row = rows[i];
+        stage_bad[st] = row < 0;
+        const uint32_t fb = smem_u32(full + st);
+        if ((int)blockIdx.x == a.hold_warp && j == a.hold_tile) continue;  // test hook: never completes
+        if (row < 0) {
+          mbar_arrive(fb);
+          continue;
+        }
+        mbar_arrive_expect_tx(fb, Geo::STAGE_BYTES);
+        const uint32_t dk = smem_u32(ring + st * Geo::STAGE_BYTES);
+#pragma unroll
+        for (int p = 0; p < Geo::SUB; ++p) {
+          tma_load_2d(dk + p * Geo::PANEL_BYTES, &tmk, p * 64, row, fb, pol);
+          tma_load_2d(dk + Geo::TILE_BYTES + p * Geo::PANEL_BYTES, &tmv, p * 64, row, fb, pol);
+        }
+      }
+      if (!ok) break;
+      mbar_arrive(smem_u32(cempty + slot));
+    }
+    // Wait (bounded, without the abort shortcut) for the loads still in flight,
+    // the latest use of every stage, so no copy lands after the CTA has left.
+    for (int jj = j - 1; jj >= 0 && jj >= j - STAGES; --jj) {
+      if ((int)blockIdx.x == a.hold_warp && jj == a.hold_tile) continue;
+      mbar_wait_bounded(smem_u32(full + jj % STAGES), (uint32_t)((jj / STAGES) & 1), limit);
+    }
+    return;
+  }
+
+  // ================================ consumers ================================
+  const int c = warp - 2;
+  const int g0 = lane >> 2, qd = lane & 3;
+  uint32_t cbar_phase = 0;
+  auto cons_sync = [&]() -> bool {
+    mbar_arrive(smem_u32(cbar));
+    const bool ok = sched_wait_warp(smem_u32(cbar), cbar_phase, limit, abort_flag, a.err);
+    cbar_phase ^= 1u;
+    return ok;
+  };
+  T* const outp = static_cast<T*>(a.out);
+  int j_base = 0;
+  for (int k = 0;; ++k) {
+    const int slot = k % kSchedSlots;
+    if (!sched_wait_warp(smem_u32(cfull + slot), (uint32_t)((k / kSchedSlots) & 1), limit, abort_flag, a.err))
+      return;
+    const int4 d0 = slot_desc(slot)[0], d1 = slot_desc(slot)[1];
+    const int n = d0.w;
+    if (n < 0) return;
+    const int seq = d0.x, uk = d0.y, begin = d0.z;
+    const int first = d1.x, p = d1.y, ctx = d1.z;
+    const int kvh = uk / a.head_groups, hg = uk - kvh * a.head_groups;
+    const int h0 = kvh * a.G + hg * 16, nh = min(16, a.G - hg * 16);
+    uint32_t qa[KC][4];
+    {
+      const uint32_t* qs = reinterpret_cast<const uint32_t*>(slot_q(slot));
+#pragma unroll
+      for (int kc = 0; kc < KC; ++kc) {
+        const int w = kc * 8 + qd;  // word column of element kc * 16 + 2 qd
+        qa[kc][0] = qs[g0 * (QP / 2) + w];
+        qa[kc][1] = qs[(g0 + 8) * (QP / 2) + w];
+        qa[kc][2] = qs[g0 * (QP / 2) + w + 4];
+        qa[kc][3] = qs[(g0 + 8) * (QP / 2) + w + 4];
+      }
+    }
+    mbar_arrive(smem_u32(cempty + slot));  // the slot's descriptor and query are in registers
+
+    float o[NO][4];
+#pragma unroll
+    for (int nn = 0; nn < NO; ++nn) o[nn][0] = o[nn][1] = o[nn][2] = o[nn][3] = 0.f;
+    float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+    for (int i = c; i < n; i += kSchedConsumers) {
+      const int jj = j_base + i, st = jj % STAGES;
+      if (!sched_wait_warp(smem_u32(full + st), (uint32_t)((jj / STAGES) & 1), limit, abort_flag, a.err))
+        return;
+      if (!stage_bad[st]) {
+        const int valid = min(kTile, ctx - (begin + i) * kTile);
+        const uint32_t kb = smem_u32(ring + st * Geo::STAGE_BYTES);
+        attend_tile<T, D>(kb, kb + Geo::TILE_BYTES, valid, a.scale_log2, qa, o, mrow, lrow);
+        if (valid < kTile) fence_proxy_async_smem();  // V rows zeroed through the generic proxy
+      }
+      mbar_arrive(smem_u32(empty + st));
+    }
+    j_base += n;
+
+    // ---- merge the four consumer states of this chunk ----
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 1);
+      lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 2);
+    }
+    const int mb = k & 1;
+    float* mo = merge_o + ((mb * kSchedConsumers + c) * 16) * D;
+    float2* mml = merge_ml + (mb * kSchedConsumers + c) * 16;
+#pragma unroll
+    for (int nn = 0; nn < NO; ++nn) {
+      const int d = nn * 8 + 2 * qd;
+      if (g0 < nh) *reinterpret_cast<float2*>(mo + g0 * D + d) = make_float2(o[nn][0], o[nn][1]);
+      if (g0 + 8 < nh) *reinterpret_cast<float2*>(mo + (g0 + 8) * D + d) = make_float2(o[nn][2], o[nn][3]);
+    }
+    if (qd == 0) {
+      if (g0 < nh) mml[g0] = make_float2(mrow[0], lrow[0]);
+      if (g0 + 8 < nh) mml[g0 + 8] = make_float2(mrow[1], lrow[1]);
+    }
+    if (!cons_sync()) return;
+    constexpr int DPL = D / 32;  // columns per lane
+    const float* mo_all = merge_o + (mb * kSchedConsumers * 16) * D;
+    const float2* mml_all = merge_ml + mb * kSchedConsumers * 16;
+    const int me = d1.w;  // this chunk's index (the fetcher publishes it here)
+    for (int r = c; r < nh; r += kSchedConsumers) {
+      float M = -INFINITY;
+#pragma unroll
+      for (int s = 0; s < kSchedConsumers; ++s) M = fmaxf(M, mml_all[s * 16 + r].x);
+      float Lsum = 0.f, acc[DPL];
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
+      if (M > -INFINITY) {
+#pragma unroll
+        for (int s = 0; s < kSchedConsumers; ++s) {
+          const float2 ml = mml_all[s * 16 + r];
+          const float w = fast_exp2(ml.x - M);
+          Lsum = fmaf(ml.y, w, Lsum);
+#pragma unroll
+          for (int i = 0; i < DPL; ++i) acc[i] = fmaf(mo_all[(s * 16 + r) * D + lane * DPL + i], w, acc[i]);
+        }
+      }
+      if (p == 1) {
+        const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
+        T* po = outp + (int64_t)seq * a.o_s0 + (int64_t)(h0 + r) * a.o_s1 + lane * DPL;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) po[i] = from_f32<T>(acc[i] * inv);
+      } else {
+        float* pp = sa.part + ((int64_t)me * sa.mg + r) * PR;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) pp[lane * DPL + i] = acc[i];
+        if (lane == 0) *reinterpret_cast<float2*>(pp + D) = make_float2(M, Lsum);
+      }
+    }
+    if (p == 1) continue;
+
+    // ---- a piece of a split unit: count in; the last piece merges the unit ----
+    __threadfence();  // this piece's partial is visible GPU-wide before the arrival
+    if (!cons_sync()) return;
+    if (c == 0 && lane == 0) misc[1] = atomicAdd(sa.ucnt + first, 1);
+    if (!cons_sync()) return;
+    if (misc[1] != p - 1) continue;
+    __threadfence();  // acquire side: the other pieces' partials
+    for (int r = c; r < nh; r += kSchedConsumers) {
+      // M and L over the pieces, 32 pieces per round (lane i: piece base + i)
+      float M = -INFINITY;
+      for (int base = 0; base < p; base += 32) {
+        const int i = base + lane;
+        float mi = i < p ? __ldcg(sa.part + ((int64_t)(first + i) * sa.mg + r) * PR + D) : -INFINITY;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mi = fmaxf(mi, __shfl_xor_sync(0xffffffffu, mi, o));
+        M = fmaxf(M, mi);
+      }
+      float Lsum = 0.f;
+      for (int base = 0; base < p; base += 32) {
+        const int i = base + lane;
+        float li = 0.f;
+        if (i < p) {
+          const float2 ml = __ldcg(reinterpret_cast<const float2*>(sa.part + ((int64_t)(first + i) * sa.mg + r) * PR + D));
+          li = ml.y * fast_exp2(ml.x - M);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) li += __shfl_xor_sync(0xffffffffu, li, o);
+        Lsum += li;
+      }
+      const float inv = 1.f / Lsum;
+      float acc[DPL];
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
+      for (int base = 0; base < p; base += 32) {
+        const int i = base + lane;
+        float wi = 0.f;
+        if (i < p) wi = fast_exp2(__ldcg(sa.part + ((int64_t)(first + i) * sa.mg + r) * PR + D) - M) * inv;
+        const int cnt = min(32, p - base);
+        for (int t = 0; t < cnt; ++t) {
+          const float w = __shfl_sync(0xffffffffu, wi, t);
+          const float* src = sa.part + ((int64_t)(first + base + t) * sa.mg + r) * PR + lane * DPL;
+#pragma unroll
+          for (int q = 0; q < DPL; ++q) acc[q] = fmaf(__ldcg(src + q), w, acc[q]);
+        }
+      }
+      T* po = outp + (int64_t)seq * a.o_s0 + (int64_t)(h0 + r) * a.o_s1 + lane * DPL;
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) po[i] = from_f32<T>(acc[i]);
+    }
+    if (c == 0 && lane == 0) sa.ucnt[first] = 0;  // zero at rest for the next decode of this schedule
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+#ifndef MVB_SCHED64_STAGES
+#define MVB_SCHED64_STAGES 32
+#endif
+#ifndef MVB_SCHED128_STAGES
+#define MVB_SCHED128_STAGES 16
+#endif
+
+SchedLayout sched_layout(int num_seqs, int num_kv_heads, int head_groups, int G, int max_blocks,
+                         int block_size, int head_dim, int ctas) {
+  SchedLayout l = {};
+  const int64_t units = (int64_t)num_seqs * num_kv_heads * head_groups;
+  const int64_t max_tiles = ((int64_t)max_blocks * block_size + kTile - 1) / kTile;
+  const int64_t per_unit = (max_tiles + kSchedMaxPiece - 1) / kSchedMaxPiece;
+  // sum over units of ceil(tiles / piece) <= total / piece + units, and the
+  // schedule's choice of piece keeps total / piece <= max(units * per_unit, 2 * ctas)
+  int64_t mc = units * per_unit;
+  if (mc < 2LL * ctas) mc = 2LL * ctas;
+  mc += units;
+  if (mc < 1) mc = 1;
+  l.max_chunks = mc;
+  l.mg = G < 16 ? G : 16;
+  auto up = [](int64_t v) { return (v + 255) / 256 * 256; };
+  l.off_desc = 256;
+  l.off_ucnt = l.off_desc + up(mc * 32);
+  l.off_part = l.off_ucnt + up(mc * 4);
+  l.bytes = l.off_part + up(mc * l.mg * (head_dim + 4) * 4);
+  return l;
+}
+
+int sched_smem_bytes(int head_dim) {
+  return 1024 + (head_dim == 64 ? SchedSmem<64, MVB_SCHED64_STAGES>::BYTES : SchedSmem<128, MVB_SCHED128_STAGES>::BYTES);
+}
+
+cudaError_t launch_decode_schedule(const DecodeArgs& a, const SchedLayout& l, void* ws, int ctas, bool wait_at_end,
+                                   cudaStream_t stream) {
+  char* w = static_cast<char*>(ws);
+  auto kern = decode_schedule_kernel;
+  cudaError_t e = ensure_kernel_attrs(kern, 0);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(kern, dim3(1), dim3(kSchedBuildThreads), 0, stream, a.kv_len, a.num_seqs,
+                    a.num_kv_heads * a.head_groups, a.block_size, a.max_blocks, ctas,
+                    reinterpret_cast<SchedHeader*>(w), reinterpret_cast<int4*>(w + l.off_desc),
+                    reinterpret_cast<int*>(w + l.off_ucnt), (int)l.max_chunks, a.err, wait_at_end ? 1 : 0);
+}
+
+template <typename T, int D, int STAGES>
+cudaError_t launch_sched_t(const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a,
+                           const SchedLayout& l, void* ws, int ctas, cudaStream_t stream) {
+  auto kern = decode_sched_kernel<T, D, STAGES>;
+  const int smem = 1024 + SchedSmem<D, STAGES>::BYTES;
+  cudaError_t e = ensure_kernel_attrs(kern, smem);
+  if (e != cudaSuccess) return e;
+  char* w = static_cast<char*>(ws);
+  SchedArgs sa;
+  sa.hdr = reinterpret_cast<SchedHeader*>(w);
+  sa.desc = reinterpret_cast<const int4*>(w + l.off_desc);
+  sa.ucnt = reinterpret_cast<int*>(w + l.off_ucnt);
+  sa.part = reinterpret_cast<float*>(w + l.off_part);
+  sa.max_chunks = (int)l.max_chunks;
+  sa.mg = l.mg;
+  return launch_pdl(kern, dim3(ctas), dim3(kSchedThreads), smem, stream, tmk, tmv, a, sa);
+}
+
+cudaError_t launch_decode_sched(const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a, int dtype,
+                                int head_dim, const SchedLayout& l, void* ws, int ctas, cudaStream_t stream) {
+  if (dtype == MVB_DTYPE_BF16)
+    return head_dim == 64 ? launch_sched_t<__nv_bfloat16, 64, MVB_SCHED64_STAGES>(tmk, tmv, a, l, ws, ctas, stream)
+                          : launch_sched_t<__nv_bfloat16, 128, MVB_SCHED128_STAGES>(tmk, tmv, a, l, ws, ctas, stream);
+  return head_dim == 64 ? launch_sched_t<__half, 64, MVB_SCHED64_STAGES>(tmk, tmv, a, l, ws, ctas, stream)
+                        : launch_sched_t<__half, 128, MVB_SCHED128_STAGES>(tmk, tmv, a, l, ws, ctas, stream);
+}
+
+}  // namespace mvb

@@ -49,12 +49,22 @@ struct DecodeArgs {
   float* part_l;     // [num_seqs][num_heads][num_parts] sum of exp2(x - m)
   int* err;
   int early_inputs;  // read query / block table / kv_len before the grid-dependency wait
-  // Test hook of the bounded waits (stream kernel): the load of local tile
-  // `hold_tile` of warp `hold_warp` is never issued, so that warp's wait on it
-  // runs out after `wait_limit` try-waits and reports MVB_DEV_TIMEOUT.
+  // Test hook of the bounded waits: the load of local tile `hold_tile` of
+  // stream warp `hold_warp` (stream kernel), or of tile number `hold_tile` of
+  // CTA `hold_warp` (scheduled kernel), is never issued, so the wait on it runs
+  // out after `wait_limit` try-waits and reports MVB_DEV_TIMEOUT.
   // Production calls: hold_warp = -1, wait_limit = kWaitSpinLimit.
   int hold_warp, hold_tile;
   int wait_limit;
+};
+
+// Workspace layout of the scheduled decode (MVB_DECODE_SCHED): a 256-byte
+// header, the chunk descriptors, the per-unit arrival counters and the partial
+// states, each 256-byte aligned.
+struct SchedLayout {
+  int64_t max_chunks;  // upper bound on the chunks any schedule of this shape lists
+  int mg;              // partial-state rows per chunk (query heads per unit)
+  int64_t off_desc, off_ucnt, off_part, bytes;
 };
 
 // ---------------------------------------------------------------------------

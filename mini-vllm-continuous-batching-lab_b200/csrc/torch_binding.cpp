@@ -40,13 +40,32 @@ int dtype_code(at::ScalarType t) {
 }
 
 // Decode workspaces owned by this binding, per device and per kernel family
-// (the stream kernel and the split-K kernels never share one), grown on demand
+// (the stream, split-K and scheduled kernels never share one), grown on demand
 // and zero-filled when allocated.
 std::mutex g_ws_mu;
-std::vector<at::Tensor> g_ws[2];
+std::vector<at::Tensor> g_ws[3];
 
-at::Tensor workspace(int dev, int kind, int64_t nbytes) {
+// The scheduled kernel's workspace holds its schedule and hand-out counters,
+// so calls on different streams, which may overlap, each get their own.
+struct StreamWorkspace {
+  int dev;
+  cudaStream_t stream;
+  at::Tensor t;
+};
+std::vector<StreamWorkspace> g_ws_stream;
+
+at::Tensor workspace(int dev, int kind, int64_t nbytes, cudaStream_t stream) {
   std::lock_guard<std::mutex> lock(g_ws_mu);
+  if (kind == 2) {
+    for (StreamWorkspace& w : g_ws_stream) {
+      if (w.dev != dev || w.stream != stream) continue;
+      if (w.t.numel() < nbytes)
+        w.t = at::zeros({nbytes}, at::TensorOptions().dtype(at::kByte).device(at::kCUDA, dev));
+      return w.t;
+    }
+    g_ws_stream.push_back({dev, stream, at::zeros({nbytes}, at::TensorOptions().dtype(at::kByte).device(at::kCUDA, dev))});
+    return g_ws_stream.back().t;
+  }
   std::vector<at::Tensor>& v = g_ws[kind];
   if ((int)v.size() <= dev) v.resize(dev + 1);
   at::Tensor& t = v[dev];
@@ -116,7 +135,8 @@ std::tuple<int64_t, at::Tensor> decode(const at::Tensor& query, const at::Tensor
                                        const at::Tensor& value_cache, const at::Tensor& block_table,
                                        const at::Tensor& kv_len, int64_t block_size, double scale,
                                        const c10::optional<at::Tensor>& out_opt, int64_t variant,
-                                       int64_t partition_tokens, int64_t err_ptr) {
+                                       int64_t partition_tokens, int64_t err_ptr,
+                                       const c10::optional<at::Tensor>& ws_opt) {
   const at::Tensor none;
   if (!(query.dim() == 3 && key_cache.dim() == 4 && key_cache.sizes() == value_cache.sizes() &&
         (query.size(2) == 64 || query.size(2) == 128) && block_size > 0 &&
@@ -156,10 +176,19 @@ std::tuple<int64_t, at::Tensor> decode(const at::Tensor& query, const at::Tensor
       (int32_t)block_size, (int32_t)key_cache.size(0), (int32_t)block_table.size(1), dt, (int32_t)variant,
       (int32_t)partition_tokens, key_cache.data_ptr(), &v, &pt, &parts, &ws_bytes);
   if (st != MVB_OK) return {st, out};
-  void* ws = nullptr;
-  if (ws_bytes > 0) ws = workspace(dev, v == MVB_DECODE_STREAM ? 0 : 1, ws_bytes).data_ptr();
-  if (scale < 0) scale = std::pow((double)query.size(2), -0.5);  // the wrapper's default
   cudaStream_t stream = c10::cuda::getCurrentCUDAStream(dev).stream();
+  void* ws = nullptr;
+  if (ws_opt.has_value() && ws_opt->defined()) {
+    // the caller's workspace (a decode schedule built for this batch)
+    const at::Tensor& w = *ws_opt;
+    if (!(w.is_cuda() && w.get_device() == dev && w.numel() * w.element_size() >= ws_bytes))
+      return {kSlowPath, none};
+    ws = w.data_ptr();
+    ws_bytes = w.numel() * w.element_size();
+  } else if (ws_bytes > 0) {
+    ws = workspace(dev, v == MVB_DECODE_STREAM ? 0 : v == MVB_DECODE_SCHED ? 2 : 1, ws_bytes, stream).data_ptr();
+  }
+  if (scale < 0) scale = std::pow((double)query.size(2), -0.5);  // the wrapper's default
   st = mvb_paged_decode(query.data_ptr(), query.stride(0), query.stride(1), key_cache.data_ptr(),
                         value_cache.data_ptr(), block_table.data_ptr<int64_t>(), block_table.stride(0),
                         (int32_t)block_table.size(1), kv_len.data_ptr<int32_t>(), out.data_ptr(), out.stride(0),

@@ -47,7 +47,7 @@ def assert_close(gpu: torch.Tensor, ref: np.ndarray, dtype: str, msg: str = ""):
 def variants_for(dtype: str, block_size: int, head_dim: int):
     v = ["auto", "fma"]
     if dtype != "f32" and block_size % 16 == 0 and head_dim in (64, 128):
-        v += ["mma", "stream"]
+        v += ["mma", "stream", "sched"]
     return v
 
 
@@ -81,7 +81,7 @@ def test_golden_decodes_all_variants(golden, kind):
 
 
 @pytest.mark.parametrize("variant,partition_tokens", [
-    ("stream", None), ("mma", None), ("mma", 16), ("mma", 48), ("mma", 512), ("mma", 1024),
+    ("sched", None), ("stream", None), ("mma", None), ("mma", 16), ("mma", 48), ("mma", 512), ("mma", 1024),
     ("fma", None), ("fma", 512),
 ])
 def test_config2_full_size_vs_oracle(variant, partition_tokens):
@@ -110,13 +110,13 @@ def test_config3_long_context_split_k_vs_oracle():
                             torch_to_np(t["value_caches"][0], "bf16"), spec.block_tables,
                             spec.context_lens, spec.block_size, "bf16")
     assert (st == 0).all()
-    for v in ("mma", "stream"):
+    for v in ("mma", "stream", "sched"):
         out = M.paged_decode_attention(t["query"], t["key_caches"][0], t["value_caches"][0],
                                        t["block_tables"], t["kv_len"], spec.block_size, variant=v)
         assert_close(out, ref, "bf16", f"config3 {v}")
 
 
-@pytest.mark.parametrize("variant", ["stream", "mma", "fma"])
+@pytest.mark.parametrize("variant", ["sched", "stream", "mma", "fma"])
 def test_config4_gqa4_d128_vs_oracle(variant):
     """BASELINE config 4 shape (32/8/128, lognormal ctx), a 96-sequence shard."""
     spec = W.make_spec(4, seed=2, num_seqs=96)
@@ -166,7 +166,7 @@ def test_gqa_group_sizes(heads):
     ref, _ = oracle.decode(torch_to_np(t["query"], "f16"), torch_to_np(t["key_caches"][0], "f16"),
                            torch_to_np(t["value_caches"][0], "f16"), spec.block_tables, spec.context_lens,
                            16, "f16")
-    for v in ("stream", "mma", "fma"):
+    for v in ("sched", "stream", "mma", "fma"):
         out = M.paged_decode_attention(t["query"], t["key_caches"][0], t["value_caches"][0],
                                        t["block_tables"], t["kv_len"], 16, variant=v)
         assert_close(out, ref, "f16", f"G={h // kh} {v}")
@@ -211,7 +211,7 @@ def test_nan_garbage_past_context_is_never_used():
         last = int(spec.block_tables[s][(n - 1) // 16])
         kc[last, :, (n % 16 or 16):] = float("nan")
         vc[last, :, (n % 16 or 16):] = float("inf")
-    for v in ("stream", "mma", "fma"):
+    for v in ("sched", "stream", "mma", "fma"):
         out = M.paged_decode_attention(t["query"], kc, vc, t["block_tables"], t["kv_len"], 16, variant=v)
         assert torch.isfinite(out.float()).all(), v
     ref, _ = oracle.decode(torch_to_np(t["query"], "bf16"), torch_to_np(kc, "bf16"), torch_to_np(vc, "bf16"),
@@ -219,7 +219,7 @@ def test_nan_garbage_past_context_is_never_used():
     assert_close(out, ref, "bf16", "nan garbage")
 
 
-@pytest.mark.parametrize("variant", ["stream", "mma", "fma"])
+@pytest.mark.parametrize("variant", ["sched", "stream", "mma", "fma"])
 def test_deterministic_bits(variant):
     spec = W.make_spec(2, seed=8, num_seqs=64)
     t = W.torch_tensors(spec, torch.bfloat16, DEV)
@@ -271,7 +271,7 @@ def _small():
     return q, kc, kc.clone()
 
 
-@pytest.mark.parametrize("variant", ["stream", "mma", "fma"])
+@pytest.mark.parametrize("variant", ["sched", "stream", "mma", "fma"])
 def test_kv_len_zero_raises_value_error(variant):
     q, kc, vc = _small()
     bt = torch.tensor([[0, -1], [1, 2]], device=DEV)
@@ -280,7 +280,7 @@ def test_kv_len_zero_raises_value_error(variant):
         M.triton_decode_attention(q, kc, vc, bt, kvl, 16, variant=variant)
 
 
-@pytest.mark.parametrize("variant", ["stream", "mma", "fma"])
+@pytest.mark.parametrize("variant", ["sched", "stream", "mma", "fma"])
 def test_table_too_short_raises_index_error(variant):
     q, kc, vc = _small()
     bt = torch.tensor([[0], [1]], device=DEV)
@@ -289,7 +289,7 @@ def test_table_too_short_raises_index_error(variant):
         M.paged_decode_attention(q, kc, vc, bt, kvl, 16, variant=variant)
 
 
-@pytest.mark.parametrize("variant", ["stream", "mma", "fma"])
+@pytest.mark.parametrize("variant", ["sched", "stream", "mma", "fma"])
 @pytest.mark.parametrize("bad", [-1, 8, 1 << 40])
 def test_bad_block_id_within_context_raises(variant, bad):
     q, kc, vc = _small()

@@ -59,6 +59,9 @@ def test_header_constants_match_binding():
     assert consts["MVB_DECODE_MMA"] == _native.DECODE_MMA
     assert consts["MVB_DECODE_STREAM"] == _native.DECODE_STREAM
     assert consts["MVB_DECODE_AFTER_WRITE"] == _native.DECODE_AFTER_WRITE
+    assert consts["MVB_DECODE_SCHED"] == _native.DECODE_SCHED
+    assert consts["MVB_DECODE_SCHEDULE_READY"] == _native.DECODE_SCHEDULE_READY
+    assert consts["MVB_DEV_SCHEDULE"] == _native.DEV_SCHEDULE
 
 
 def _plan(**kw):
@@ -68,8 +71,18 @@ def _plan(**kw):
     return M.decode_plan(**args)
 
 
-def test_plan_headline_config_uses_the_stream_kernel():
+def test_plan_headline_config_uses_the_scheduled_kernel():
     p = _plan()
+    assert p["variant"] == "sched" and p["num_partitions"] == 0
+    # header + per chunk: a 32-byte descriptor, an arrival counter and a partial
+    # state of 7 head rows x (64 + 4) floats, for the bound of
+    # max(512 units x 4 pieces, 2 x 148 CTAs) + 512 chunks
+    chunks = max(512 * 4, 2 * 148) + 512
+    assert p["workspace_bytes"] >= 256 + chunks * (32 + 4 + 7 * 68 * 4)
+
+
+def test_plan_stream_kernel_when_asked():
+    p = _plan(variant="stream")
     assert p["variant"] == "stream" and p["num_partitions"] == 0
     # tile prefix + context lengths, then two partial slots (16 rows x (64 + 2) floats) per warp
     assert p["workspace_bytes"] >= (2 * 256 + 1) * 4 + 2 * 16 * 66 * 4 * 148
@@ -81,8 +94,8 @@ def test_plan_one_cta_per_sequence_and_kv_head_when_asked():
 
 
 def test_plan_stream_limits():
-    assert _plan(num_seqs=4096)["variant"] == "stream"
-    assert _plan(num_seqs=4097)["variant"] == "mma"
+    assert _plan(num_seqs=4096, variant="stream")["variant"] == "stream"
+    assert _plan(num_seqs=4097)["variant"] == "sched"  # the scheduled kernel has no batch limit
     with pytest.raises(RuntimeError, match="variant"):
         _plan(num_seqs=4097, variant="stream")
 
@@ -101,6 +114,8 @@ def test_plan_fp32_and_small_blocks_use_fma():
         _plan(dtype=torch.float32, variant="stream")
     with pytest.raises(RuntimeError, match="variant"):
         _plan(dtype=torch.float32, variant="mma")
+    with pytest.raises(RuntimeError, match="variant"):
+        _plan(block_size=8, max_blocks_per_seq=256, variant="sched")
 
 
 def test_plan_explicit_partition_rounds_to_16():
@@ -147,6 +162,21 @@ def test_decode_host_checks_without_gpu():
     assert call(1, nh=7, nkv=2) == _native.ERR_HEADS
 
 
+def test_schedule_host_checks_without_gpu():
+    lib = _native.lib()
+
+    def call(num_seqs, kv_len=None, ws=None, wsb=0, flags=0, dtype=_native.DTYPE_BF16, err=None):
+        return lib.mvb_paged_decode_schedule(kv_len, num_seqs, 14, 2, 64, 16, 100, 8, dtype, flags, ws, wsb,
+                                             err, None)
+
+    assert call(0) == _native.OK  # empty batch: nothing launched
+    assert call(1) == _native.ERR_INVALID_ARG  # null kv_len
+    assert call(1, dtype=_native.DTYPE_F32) == _native.ERR_VARIANT  # the scheduled kernel is bf16 / f16 only
+    assert call(1, kv_len=16, err=16, flags=0x400) == _native.ERR_INVALID_ARG  # unknown flag
+    assert call(1, kv_len=16, err=16) == _native.ERR_WORKSPACE  # no workspace
+    assert call(1, kv_len=16, err=16, ws=256 * 7 + 16, wsb=1 << 30) == _native.ERR_WORKSPACE  # misaligned
+
+
 def test_direct_binding_loads_and_routes_cpu_tensors_to_the_full_path():
     """The C++ binding of the per-step calls loads without a GPU and declines
     (SLOW_PATH) anything but CUDA tensors, leaving the Python wrapper's checks
@@ -158,5 +188,5 @@ def test_direct_binding_loads_and_routes_cpu_tensors_to_the_full_path():
     assert fast.kv_write(k, k, kc, kc, torch.zeros(2, dtype=torch.int64), 16, True, 0) == fast.SLOW_PATH
     q = torch.zeros(2, 4, 64, dtype=torch.bfloat16)
     st, out = fast.decode(q, kc, kc, torch.zeros(2, 1, dtype=torch.int64), torch.ones(2, dtype=torch.int32), 16,
-                          -1.0, None, _native.DECODE_AUTO, 0, 0)
+                          -1.0, None, _native.DECODE_AUTO, 0, 0, None)
     assert st == fast.SLOW_PATH and out is None
