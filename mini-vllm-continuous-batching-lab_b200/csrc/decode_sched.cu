@@ -18,18 +18,31 @@
 // Warp roles inside the CTA:
 //   * fetcher (warp 0): takes the next chunk index, loads its descriptor, the
 //     block ids of its tiles (validated, turned into pool rows) and the query
-//     rows of its head group, and publishes them in one of 4 chunk slots;
-//   * issuer (warp 1, lane 0): walks the published chunks and issues two 2-D
-//     TMA tile loads (K and V, 16 rows x D, 128-byte swizzle) per tile into a
-//     STAGES-deep ring (one full / one empty mbarrier per stage);
-//   * consumers (warps 2-5): tile i of a chunk goes to consumer i % 4, which
-//     runs attend_tile (mma.sync m16n8k16, online softmax, fp32 accumulate);
-//     at the chunk end the four states are merged through shared memory.
-// A chunk that holds a whole unit is normalised and written to `out`; a piece
-// of a longer unit writes its partial state (O, m, l per head row) and counts
-// itself in on the unit's arrival counter, and the last piece to arrive merges
-// all pieces in piece order (deterministic) and writes the unit.  While the
-// consumers merge, the fetcher and the issuer keep the ring full.
+//     rows of its head group, and publishes them in one of 4 chunk slots.  It
+//     is software-pipelined: while chunk k's block ids and query rows load,
+//     chunk k+1's descriptor and the index after it are in flight;
+//   * issuer (warp 1): walks the published chunks and issues two 2-D TMA tile
+//     loads (K and V, 16 rows x D, 128-byte swizzle) per tile into a
+//     STAGES-deep ring (one full / one empty mbarrier per stage), up to 8 tiles
+//     at once, one per lane (one thread alone issues a tile only every ~250 ns,
+//     a third of what an SM streams);
+//   * consumers (warps 2 .. NC+1): tile j of the CTA's tile sequence goes to
+//     consumer j % NC, which runs attend_tile (mma.sync m16n8k16, online
+//     softmax, fp32 accumulate) and at the chunk end hands its state to the
+//     merger.  Every stage thus has one consumer, which waits on its phases in
+//     order (a parity wait is sound only while its waiter is at most one phase
+//     away; consumers sharing stages drifted further apart than the ring).  A
+//     chunk's tiles start on a multiple of NC of the sequence — the places
+//     skipped are virtual tiles that pass through the ring without a load — so
+//     tile i of a chunk always goes to consumer i % NC and the result does not
+//     depend on timing;
+//   * merger (last warp): merges the NC consumer states of the chunk.  A chunk
+//     that holds a whole unit is normalised and written to `out`; a piece of a
+//     longer unit writes its partial state (O, m, l per head row) and counts
+//     itself in on the unit's arrival counter, and the last piece to arrive
+//     merges all pieces in piece order (deterministic) and writes the unit.
+// The consumers never wait for global memory, so the ring keeps streaming
+// while the merger works.
 //
 // Every wait is bounded (DecodeArgs::wait_limit); a wait that runs out sets
 // MVB_DEV_TIMEOUT and a CTA-wide abort flag that every other wait polls, the
@@ -43,8 +56,7 @@ namespace mvb {
 constexpr int kSchedMaxPiece = 32;  // tiles per chunk at most: one block id per fetcher lane
 constexpr int kSchedMinPiece = 4;
 constexpr int kSchedSlots = 4;      // chunk slots between the fetcher and the other roles
-constexpr int kSchedConsumers = 4;  // consumer warps
-constexpr int kSchedThreads = (2 + kSchedConsumers) * 32;
+constexpr int kSchedIssueLanes = 8;  // tiles the issuer warp issues at once, one per lane
 constexpr int kSchedBuildThreads = 1024;
 
 // Workspace header (256 bytes at the start of the workspace).
@@ -178,20 +190,58 @@ decode_schedule_kernel(const int* __restrict__ kv_len, int num_seqs, int units_p
 // ---------------------------------------------------------------------------
 // decode
 // ---------------------------------------------------------------------------
-template <int D, int STAGES> struct SchedSmem {
+// Per head dim: ring stages, consumer warps (two per SM sub-partition at D 64,
+// so one warp's MMA / shuffle / exp latency chain hides behind another's) and
+// merge buffers between the consumers and the merger.  The ring holds 128 KB in
+// flight per SM; shared memory (ring + slots + NB buffers of NC states) caps
+// NC at 4 for D = 128.
+// (Overridable at build time for tuning sweeps.)
+#ifndef MVB_SCHED64_STAGES
+#define MVB_SCHED64_STAGES 32
+#endif
+#ifndef MVB_SCHED64_NC
+#define MVB_SCHED64_NC 8
+#endif
+#ifndef MVB_SCHED64_NB
+#define MVB_SCHED64_NB 2
+#endif
+#ifndef MVB_SCHED128_STAGES
+#define MVB_SCHED128_STAGES 16
+#endif
+#ifndef MVB_SCHED128_NC
+#define MVB_SCHED128_NC 4
+#endif
+#ifndef MVB_SCHED128_NB
+#define MVB_SCHED128_NB 2
+#endif
+template <int D> struct SchedConfig;
+template <> struct SchedConfig<64> {
+  static constexpr int STAGES = MVB_SCHED64_STAGES, NC = MVB_SCHED64_NC, NB = MVB_SCHED64_NB;
+};
+template <> struct SchedConfig<128> {
+  static constexpr int STAGES = MVB_SCHED128_STAGES, NC = MVB_SCHED128_NC, NB = MVB_SCHED128_NB;
+};
+
+template <int D> struct SchedSmem {
   using Geo = MmaGeom<D>;
+  static constexpr int STAGES = SchedConfig<D>::STAGES, NC = SchedConfig<D>::NC, NB = SchedConfig<D>::NB;
+  static_assert(STAGES % NC == 0, "each stage belongs to one consumer");
+  static constexpr int THREADS = (3 + NC) * 32;  // fetcher, issuer, consumers, merger
   static constexpr int QP = D + 8;  // query row pitch (elements): conflict-free fragment loads
   static constexpr int SLOT_BYTES = 32 + 4 * kSchedMaxPiece + 16 * QP * 2;
+  // merge buffer: header (2 x int4), (m, l) [consumers][16], O [consumers][16][D]
+  static constexpr int MB_ML = 32;
+  static constexpr int MB_O = MB_ML + NC * 16 * 8;
+  static constexpr int MB_BYTES = MB_O + NC * 16 * D * 4;
   static constexpr int RING = 0;
   static constexpr int SLOTS = RING + STAGES * Geo::STAGE_BYTES;
-  static constexpr int MERGE_O = SLOTS + kSchedSlots * SLOT_BYTES;          // float [2][4][16][D]
-  static constexpr int MERGE_ML = MERGE_O + 2 * kSchedConsumers * 16 * D * 4;  // float2 [2][4][16]
-  static constexpr int BARS = MERGE_ML + 2 * kSchedConsumers * 16 * 8;
-  static constexpr int NBARS = 2 * STAGES + 2 * kSchedSlots + 1;
+  static constexpr int MERGE = SLOTS + kSchedSlots * SLOT_BYTES;
+  static constexpr int BARS = MERGE + NB * MB_BYTES;
+  static constexpr int NBARS = 2 * STAGES + 2 * kSchedSlots + 2 * NB;
   static constexpr int STAGE_BAD = BARS + NBARS * 8;
   static constexpr int MISC = STAGE_BAD + STAGES * 4;
   static constexpr int BYTES = MISC + 16;
-  static_assert(SLOTS % 16 == 0 && MERGE_O % 16 == 0 && BARS % 8 == 0, "alignment");
+  static_assert(SLOTS % 16 == 0 && MERGE % 16 == 0 && MB_BYTES % 16 == 0 && BARS % 8 == 0, "alignment");
 };
 
 // Bounded wait that also gives up when another role has aborted the CTA.
@@ -213,43 +263,55 @@ __device__ __forceinline__ bool sched_wait_warp(uint32_t bar, uint32_t parity, i
   return __all_sync(0xffffffffu, ok);
 }
 
-template <typename T, int D, int STAGES>
-__global__ void __launch_bounds__(kSchedThreads, 1)
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
+// One arrival for a whole warp: __syncwarp orders every lane's shared-memory
+// accesses before lane 0's arrive (release), as one arrival per lane would,
+// at a thirty-second of the barrier traffic.
+__device__ __forceinline__ void warp_arrive(uint32_t bar, int lane) {
+  __syncwarp();
+  if (lane == 0) mbar_arrive(bar);
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(SchedSmem<D>::THREADS, 1)
 decode_sched_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                     const DecodeArgs a, const SchedArgs sa) {
   using Geo = MmaGeom<D>;
-  using L = SchedSmem<D, STAGES>;
-  constexpr int KC = D / 16, NO = D / 8, QP = L::QP, PR = D + 4;
+  using L = SchedSmem<D>;
+  constexpr int KC = D / 16, NO = D / 8, QP = L::QP, PR = D + 4, NB = L::NB, NC = L::NC, STAGES = L::STAGES;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem =
       reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = smem + L::RING;
   uint8_t* slots = smem + L::SLOTS;
-  float* merge_o = reinterpret_cast<float*>(smem + L::MERGE_O);
-  float2* merge_ml = reinterpret_cast<float2*>(smem + L::MERGE_ML);
+  uint8_t* merge = smem + L::MERGE;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BARS);
-  uint64_t* full = bars;
-  uint64_t* empty = bars + STAGES;
-  uint64_t* cfull = bars + 2 * STAGES;
-  uint64_t* cempty = cfull + kSchedSlots;
-  uint64_t* cbar = cempty + kSchedSlots;
+  uint64_t* full = bars;                   // [STAGES] tile landed
+  uint64_t* empty = bars + STAGES;         // [STAGES] tile consumed
+  uint64_t* cfull = bars + 2 * STAGES;     // [slots] chunk published
+  uint64_t* cempty = cfull + kSchedSlots;  // [slots] chunk read by the issuer and the consumers
+  uint64_t* mfull = cempty + kSchedSlots;  // [NB] consumer states written
+  uint64_t* mempty = mfull + NB;           // [NB] states read by the merger
   volatile int* stage_bad = reinterpret_cast<volatile int*>(smem + L::STAGE_BAD);
-  volatile int* misc = reinterpret_cast<volatile int*>(smem + L::MISC);  // [0] abort, [1] arrival broadcast
+  volatile int* misc = reinterpret_cast<volatile int*>(smem + L::MISC);  // [0] abort flag
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(smem_u32(full + s), 1);
-      mbar_init(smem_u32(empty + s), 32);  // every lane of the consuming warp
+      mbar_init(smem_u32(empty + s), 1);  // the consuming warp
     }
     for (int c = 0; c < kSchedSlots; ++c) {
-      mbar_init(smem_u32(cfull + c), 32);                        // every fetcher lane
-      mbar_init(smem_u32(cempty + c), 1 + kSchedConsumers * 32);  // issuer + every consumer lane
+      mbar_init(smem_u32(cfull + c), 1);        // the fetcher warp
+      mbar_init(smem_u32(cempty + c), 1 + NC);  // the issuer and consumer warps
     }
-    mbar_init(smem_u32(cbar), kSchedConsumers * 32);
+    for (int b = 0; b < NB; ++b) {
+      mbar_init(smem_u32(mfull + b), NC);  // the consumer warps
+      mbar_init(smem_u32(mempty + b), 1);  // the merger warp
+    }
     misc[0] = 0;
-    misc[1] = 0;
     fence_mbar_init();
   }
   __syncthreads();  // the only CTA-wide barrier
@@ -262,22 +324,24 @@ decode_sched_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_consta
   auto slot_q = [&](int slot) {
     return reinterpret_cast<T*>(slots + slot * L::SLOT_BYTES + 32 + 4 * kSchedMaxPiece);
   };
+  auto mb_hdr = [&](int b) { return reinterpret_cast<int4*>(merge + b * L::MB_BYTES); };
+  auto mb_ml = [&](int b) { return reinterpret_cast<float2*>(merge + b * L::MB_BYTES + L::MB_ML); };
+  auto mb_o = [&](int b) { return reinterpret_cast<float*>(merge + b * L::MB_BYTES + L::MB_O); };
 
   if (warp == 0) {
-    // ================================ fetcher ================================
+    // ================================= fetcher =================================
     if (!a.early_inputs) grid_dependency_wait();
     bool waited = a.early_inputs == 0;
     const int n_chunks = __ldcg(&sa.hdr->n_chunks);
+    const int4 stop = make_int4(0, 0, 0, -1);
     int idx = blockIdx.x;
+    bool have = idx < n_chunks;
+    int4 d0 = have ? __ldcg(sa.desc + 2 * idx) : stop;
+    int4 d1 = have ? __ldcg(sa.desc + 2 * idx + 1) : make_int4(0, 0, 0, 0);
+    int idx_n = -1;  // the next chunk (not taken yet)
     bool aborted = false;
     for (int k = 0;; ++k) {
       const int slot = k % kSchedSlots;
-      const bool have = idx < n_chunks;
-      int4 d0 = make_int4(0, 0, 0, -1), d1 = make_int4(0, 0, 0, 0);
-      if (have) {
-        d0 = __ldcg(sa.desc + 2 * idx);
-        d1 = __ldcg(sa.desc + 2 * idx + 1);
-      }
       const int seq = d0.x, uk = d0.y, begin = d0.z, n = d0.w;
       const int kvh = uk / a.head_groups, hg = uk - kvh * a.head_groups;
       const int h0 = kvh * a.G + hg * 16, nh = min(16, a.G - hg * 16);
@@ -305,11 +369,20 @@ decode_sched_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_consta
         grid_dependency_wait();
         waited = true;
       }
-      int nxt = 0;
-      if (have) {
-        if (lane == 0) nxt = (int)gridDim.x + atomicAdd(&sa.hdr->next, 1);
-        nxt = __shfl_sync(0xffffffffu, nxt, 0);
+      if (idx_n < 0) {  // first chunk: take the second one now
+        int tk = n_chunks;
+        if (have && lane == 0) tk = (int)gridDim.x + atomicAdd(&sa.hdr->next, 1);
+        idx_n = __shfl_sync(0xffffffffu, tk, 0);
       }
+      // in flight during the publication below: the next descriptor, the index after it
+      const bool have_n = idx_n < n_chunks;
+      int4 n0 = stop, n1 = make_int4(0, 0, 0, 0);
+      if (have_n) {
+        n0 = __ldcg(sa.desc + 2 * idx_n);
+        n1 = __ldcg(sa.desc + 2 * idx_n + 1);
+      }
+      int t_nn = n_chunks;
+      if (have_n && lane == 0) t_nn = (int)gridDim.x + atomicAdd(&sa.hdr->next, 1);
       if (k >= kSchedSlots &&
           !sched_wait_warp(smem_u32(cempty + slot), (uint32_t)((k / kSchedSlots - 1) & 1), limit, abort_flag,
                            a.err)) {
@@ -327,9 +400,13 @@ decode_sched_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_consta
         const int e = lane + 32 * v, r = e / (D / 2), c = e - r * (D / 2);
         qs[r * (QP / 2) + c] = qw[v];
       }
-      mbar_arrive(smem_u32(cfull + slot));
+      warp_arrive(smem_u32(cfull + slot), lane);
       if (!have) break;  // the end marker is published
-      idx = nxt;
+      idx = idx_n;
+      have = have_n;
+      d0 = n0;
+      d1 = n1;
+      idx_n = __shfl_sync(0xffffffffu, t_nn, 0);
     }
     if (!aborted && lane == 0) {
       // the last CTA to reach the end of the list resets the counters
@@ -343,228 +420,281 @@ decode_sched_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_consta
   }
 
   if (warp == 1) {
-    // ================================ issuer =================================
-    if (lane != 0) return;
+    // ================================= issuer =================================
+    // Up to kSchedIssueLanes tiles at once, one per lane: each lane waits for
+    // its stage's previous tile to be consumed, then arms the stage's barrier
+    // and issues the K and V loads.
     grid_dependency_wait();  // the cache is complete from here on
-    prefetch_tensormap(&tmk);
-    prefetch_tensormap(&tmv);
+    if (lane == 0) {
+      prefetch_tensormap(&tmk);
+      prefetch_tensormap(&tmv);
+    }
     const uint64_t pol = l2_policy_evict_first();
-    int j = 0;
+    int j_base = 0, j_last = -1;  // the CTA's tile sequence; the last tile issued
     for (int k = 0;; ++k) {
       const int slot = k % kSchedSlots;
-      if (!sched_wait(smem_u32(cfull + slot), (uint32_t)((k / kSchedSlots) & 1), limit, abort_flag, a.err))
+      if (!sched_wait_warp(smem_u32(cfull + slot), (uint32_t)((k / kSchedSlots) & 1), limit, abort_flag, a.err))
         break;
       const int n = slot_desc(slot)[0].w;
       if (n < 0) break;
       const int* rows = slot_rows(slot);
+      const int j_start = (j_base + NC - 1) / NC * NC, j_end = j_start + n;  // before j_start: virtual tiles
       bool ok = true;
-      for (int i = 0; i < n; ++i, ++j) {
-        const int st = j % STAGES;
-        if (j >= STAGES &&
-            !sched_wait(smem_u32(empty + st), (uint32_t)((j / STAGES - 1) & 1), limit, abort_flag, a.err)) {
+      for (int j0 = j_base; j0 < j_end; j0 += kSchedIssueLanes) {
+        const int j = j0 + lane, st = j % STAGES;
+        const bool mine = lane < kSchedIssueLanes && j < j_end;
+        bool got = true;
+        if (mine && j >= STAGES)
+          got = sched_wait(smem_u32(empty + st), (uint32_t)((j / STAGES - 1) & 1), limit, abort_flag, a.err);
+        if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           break;
         }
-        const int row = rows[i];
-        stage_bad[st] = row < 0;
-        const uint32_t fb = smem_u32(full + st);
-        if ((int)blockIdx.x == a.hold_warp && j == a.hold_tile) continue;  // test hook: never completes
-        if (row < 0) {
-          mbar_arrive(fb);
-          continue;
-        }
-        mbar_arrive_expect_tx(fb, Geo::STAGE_BYTES);
-        const uint32_t dk = smem_u32(ring + st * Geo::STAGE_BYTES);
+        if (mine && !((int)blockIdx.x == a.hold_warp && j == a.hold_tile)) {  // test hook: never completes
+          const int row = j < j_start ? -1 : rows[j - j_start];
+          stage_bad[st] = row < 0;
+          const uint32_t fb = smem_u32(full + st);
+          if (row < 0) {
+            mbar_arrive(fb);
+          } else {
+            mbar_arrive_expect_tx(fb, Geo::STAGE_BYTES);
+            const uint32_t dk = smem_u32(ring + st * Geo::STAGE_BYTES);
 #pragma unroll
-        for (int p = 0; p < Geo::SUB; ++p) {
-          tma_load_2d(dk + p * Geo::PANEL_BYTES, &tmk, p * 64, row, fb, pol);
-          tma_load_2d(dk + Geo::TILE_BYTES + p * Geo::PANEL_BYTES, &tmv, p * 64, row, fb, pol);
+            for (int p = 0; p < Geo::SUB; ++p) {
+              tma_load_2d(dk + p * Geo::PANEL_BYTES, &tmk, p * 64, row, fb, pol);
+              tma_load_2d(dk + Geo::TILE_BYTES + p * Geo::PANEL_BYTES, &tmv, p * 64, row, fb, pol);
+            }
+          }
         }
+        j_last = min(j0 + kSchedIssueLanes, j_end) - 1;
       }
       if (!ok) break;
-      mbar_arrive(smem_u32(cempty + slot));
+      j_base = j_end;
+      warp_arrive(smem_u32(cempty + slot), lane);
     }
     // Wait (bounded, without the abort shortcut) for the loads still in flight,
     // the latest use of every stage, so no copy lands after the CTA has left.
-    for (int jj = j - 1; jj >= 0 && jj >= j - STAGES; --jj) {
-      if ((int)blockIdx.x == a.hold_warp && jj == a.hold_tile) continue;
+    for (int i = lane; i < STAGES; i += 32) {
+      const int jj = j_last - i;
+      if (jj < 0 || ((int)blockIdx.x == a.hold_warp && jj == a.hold_tile)) continue;
       mbar_wait_bounded(smem_u32(full + jj % STAGES), (uint32_t)((jj / STAGES) & 1), limit);
     }
     return;
   }
 
-  // ================================ consumers ================================
-  const int c = warp - 2;
-  const int g0 = lane >> 2, qd = lane & 3;
-  uint32_t cbar_phase = 0;
-  auto cons_sync = [&]() -> bool {
-    mbar_arrive(smem_u32(cbar));
-    const bool ok = sched_wait_warp(smem_u32(cbar), cbar_phase, limit, abort_flag, a.err);
-    cbar_phase ^= 1u;
-    return ok;
-  };
-  T* const outp = static_cast<T*>(a.out);
-  int j_base = 0;
-  for (int k = 0;; ++k) {
-    const int slot = k % kSchedSlots;
-    if (!sched_wait_warp(smem_u32(cfull + slot), (uint32_t)((k / kSchedSlots) & 1), limit, abort_flag, a.err))
-      return;
-    const int4 d0 = slot_desc(slot)[0], d1 = slot_desc(slot)[1];
-    const int n = d0.w;
-    if (n < 0) return;
-    const int seq = d0.x, uk = d0.y, begin = d0.z;
-    const int first = d1.x, p = d1.y, ctx = d1.z;
-    const int kvh = uk / a.head_groups, hg = uk - kvh * a.head_groups;
-    const int h0 = kvh * a.G + hg * 16, nh = min(16, a.G - hg * 16);
-    uint32_t qa[KC][4];
-    {
-      const uint32_t* qs = reinterpret_cast<const uint32_t*>(slot_q(slot));
-#pragma unroll
-      for (int kc = 0; kc < KC; ++kc) {
-        const int w = kc * 8 + qd;  // word column of element kc * 16 + 2 qd
-        qa[kc][0] = qs[g0 * (QP / 2) + w];
-        qa[kc][1] = qs[(g0 + 8) * (QP / 2) + w];
-        qa[kc][2] = qs[g0 * (QP / 2) + w + 4];
-        qa[kc][3] = qs[(g0 + 8) * (QP / 2) + w + 4];
-      }
-    }
-    mbar_arrive(smem_u32(cempty + slot));  // the slot's descriptor and query are in registers
-
-    float o[NO][4];
-#pragma unroll
-    for (int nn = 0; nn < NO; ++nn) o[nn][0] = o[nn][1] = o[nn][2] = o[nn][3] = 0.f;
-    float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
-    for (int i = c; i < n; i += kSchedConsumers) {
-      const int jj = j_base + i, st = jj % STAGES;
-      if (!sched_wait_warp(smem_u32(full + st), (uint32_t)((jj / STAGES) & 1), limit, abort_flag, a.err))
+  if (warp < 2 + NC) {
+    // ================================ consumers ================================
+    const int c = warp - 2;
+    const int g0 = lane >> 2, qd = lane & 3;
+    int j_base = 0;
+    for (int k = 0;; ++k) {
+      const int slot = k % kSchedSlots;
+      if (!sched_wait_warp(smem_u32(cfull + slot), (uint32_t)((k / kSchedSlots) & 1), limit, abort_flag, a.err))
         return;
-      if (!stage_bad[st]) {
-        const int valid = min(kTile, ctx - (begin + i) * kTile);
-        const uint32_t kb = smem_u32(ring + st * Geo::STAGE_BYTES);
-        attend_tile<T, D>(kb, kb + Geo::TILE_BYTES, valid, a.scale_log2, qa, o, mrow, lrow);
-        if (valid < kTile) fence_proxy_async_smem();  // V rows zeroed through the generic proxy
-      }
-      mbar_arrive(smem_u32(empty + st));
-    }
-    j_base += n;
-
-    // ---- merge the four consumer states of this chunk ----
+      const int4 d0 = slot_desc(slot)[0], d1 = slot_desc(slot)[1];
+      const int n = d0.w;
+      const int begin = d0.z, ctx = d1.z;
+      uint32_t qa[KC][4];
+      if (n > 0) {
+        const uint32_t* qs = reinterpret_cast<const uint32_t*>(slot_q(slot));
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 1);
-      lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 2);
-    }
-    const int mb = k & 1;
-    float* mo = merge_o + ((mb * kSchedConsumers + c) * 16) * D;
-    float2* mml = merge_ml + (mb * kSchedConsumers + c) * 16;
-#pragma unroll
-    for (int nn = 0; nn < NO; ++nn) {
-      const int d = nn * 8 + 2 * qd;
-      if (g0 < nh) *reinterpret_cast<float2*>(mo + g0 * D + d) = make_float2(o[nn][0], o[nn][1]);
-      if (g0 + 8 < nh) *reinterpret_cast<float2*>(mo + (g0 + 8) * D + d) = make_float2(o[nn][2], o[nn][3]);
-    }
-    if (qd == 0) {
-      if (g0 < nh) mml[g0] = make_float2(mrow[0], lrow[0]);
-      if (g0 + 8 < nh) mml[g0 + 8] = make_float2(mrow[1], lrow[1]);
-    }
-    if (!cons_sync()) return;
-    constexpr int DPL = D / 32;  // columns per lane
-    const float* mo_all = merge_o + (mb * kSchedConsumers * 16) * D;
-    const float2* mml_all = merge_ml + mb * kSchedConsumers * 16;
-    const int me = d1.w;  // this chunk's index (the fetcher publishes it here)
-    for (int r = c; r < nh; r += kSchedConsumers) {
-      float M = -INFINITY;
-#pragma unroll
-      for (int s = 0; s < kSchedConsumers; ++s) M = fmaxf(M, mml_all[s * 16 + r].x);
-      float Lsum = 0.f, acc[DPL];
-#pragma unroll
-      for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
-      if (M > -INFINITY) {
-#pragma unroll
-        for (int s = 0; s < kSchedConsumers; ++s) {
-          const float2 ml = mml_all[s * 16 + r];
-          const float w = fast_exp2(ml.x - M);
-          Lsum = fmaf(ml.y, w, Lsum);
-#pragma unroll
-          for (int i = 0; i < DPL; ++i) acc[i] = fmaf(mo_all[(s * 16 + r) * D + lane * DPL + i], w, acc[i]);
+        for (int kc = 0; kc < KC; ++kc) {
+          const int w = kc * 8 + qd;  // word column of element kc * 16 + 2 qd
+          qa[kc][0] = qs[g0 * (QP / 2) + w];
+          qa[kc][1] = qs[(g0 + 8) * (QP / 2) + w];
+          qa[kc][2] = qs[g0 * (QP / 2) + w + 4];
+          qa[kc][3] = qs[(g0 + 8) * (QP / 2) + w + 4];
         }
       }
+      if (n >= 0) warp_arrive(smem_u32(cempty + slot), lane);  // descriptor and query are in registers
+
+      float o[NO][4];
+#pragma unroll
+      for (int nn = 0; nn < NO; ++nn) o[nn][0] = o[nn][1] = o[nn][2] = o[nn][3] = 0.f;
+      float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+      // tile j of the sequence is this consumer's when j % NC == c; the chunk's
+      // tiles start at j_start (a multiple of NC; before it, virtual tiles)
+      const int j_start = (j_base + NC - 1) / NC * NC;
+      const int j_end = n >= 0 ? j_start + n : j_base;  // the end marker has no tiles, virtual or real
+      for (int jj = j_base + (c - j_base % NC + NC) % NC; jj < j_end; jj += NC) {
+        const int st = jj % STAGES;
+        if (!sched_wait_warp(smem_u32(full + st), (uint32_t)((jj / STAGES) & 1), limit, abort_flag, a.err))
+          return;
+        if (!stage_bad[st]) {
+          const int i = jj - j_start;
+          const int valid = min(kTile, ctx - (begin + i) * kTile);
+          const uint32_t kb = smem_u32(ring + st * Geo::STAGE_BYTES);
+          attend_tile<T, D>(kb, kb + Geo::TILE_BYTES, valid, a.scale_log2, qa, o, mrow, lrow);
+          if (valid < kTile) fence_proxy_async_smem();  // V rows zeroed through the generic proxy
+        }
+        warp_arrive(smem_u32(empty + st), lane);
+      }
+      j_base = j_end;
+
+      // ---- hand this consumer's state (or the end marker) to the merger ----
+      const int b = k % NB;
+      if (k >= NB &&
+          !sched_wait_warp(smem_u32(mempty + b), (uint32_t)((k / NB - 1) & 1), limit, abort_flag, a.err))
+        return;
+      if (n >= 0) {
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 1);
+          lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 2);
+        }
+        const int nh = min(16, a.G - (d0.y % a.head_groups) * 16);
+        float* mo = mb_o(b) + c * 16 * D;
+#pragma unroll
+        for (int nn = 0; nn < NO; ++nn) {
+          const int d = nn * 8 + 2 * qd;
+          if (g0 < nh) *reinterpret_cast<float2*>(mo + g0 * D + d) = make_float2(o[nn][0], o[nn][1]);
+          if (g0 + 8 < nh) *reinterpret_cast<float2*>(mo + (g0 + 8) * D + d) = make_float2(o[nn][2], o[nn][3]);
+        }
+        if (qd == 0) {
+          float2* mml = mb_ml(b) + c * 16;
+          if (g0 < nh) mml[g0] = make_float2(mrow[0], lrow[0]);
+          if (g0 + 8 < nh) mml[g0 + 8] = make_float2(mrow[1], lrow[1]);
+        }
+      }
+      if (c == 0 && lane == 0) {
+        mb_hdr(b)[0] = d0;
+        mb_hdr(b)[1] = d1;
+      }
+      warp_arrive(smem_u32(mfull + b), lane);
+      if (n < 0) return;
+    }
+  }
+
+  // ================================== merger ==================================
+  // Lane l takes head row r = l / 4 (+ 8 on a second pass for more than 8 heads)
+  // and column quarter l % 4 (CQ = D / 4 columns).
+  {
+    constexpr int CQ = D / 4;
+    const int rq = lane >> 2, cq = (lane & 3) * CQ;
+    T* const outp = static_cast<T*>(a.out);
+    for (int k = 0;; ++k) {
+      const int b = k % NB;
+      if (!sched_wait_warp(smem_u32(mfull + b), (uint32_t)((k / NB) & 1), limit, abort_flag, a.err)) return;
+      const int4 d0 = mb_hdr(b)[0], d1 = mb_hdr(b)[1];
+      if (d0.w < 0) return;  // end marker
+      const int seq = d0.x, uk = d0.y;
+      const int first = d1.x, p = d1.y, me = d1.w;
+      const int kvh = uk / a.head_groups, hg = uk - kvh * a.head_groups;
+      const int h0 = kvh * a.G + hg * 16, nh = min(16, a.G - hg * 16);
+      // the NC consumer states of each row -> (M, L, O) of the chunk
+      float Mr[2], Lr[2], Or[2][CQ];
+#pragma unroll
+      for (int pass = 0; pass < 2; ++pass) {
+        const int r = rq + 8 * pass;
+        Mr[pass] = -INFINITY;
+        Lr[pass] = 0.f;
+#pragma unroll
+        for (int i = 0; i < CQ; ++i) Or[pass][i] = 0.f;
+        if (r >= nh) continue;
+        float2 ml[NC];
+#pragma unroll
+        for (int s = 0; s < NC; ++s) {
+          ml[s] = mb_ml(b)[s * 16 + r];
+          Mr[pass] = fmaxf(Mr[pass], ml[s].x);
+        }
+        if (Mr[pass] == -INFINITY) continue;  // no token (a bad sequence): zeros
+#pragma unroll
+        for (int s = 0; s < NC; ++s) {
+          const float w = fast_exp2(ml[s].x - Mr[pass]);
+          Lr[pass] = fmaf(ml[s].y, w, Lr[pass]);
+          const float4* src = reinterpret_cast<const float4*>(mb_o(b) + (s * 16 + r) * D + cq);
+#pragma unroll
+          for (int i = 0; i < CQ / 4; ++i) {
+            const float4 v = src[i];
+            Or[pass][4 * i] = fmaf(v.x, w, Or[pass][4 * i]);
+            Or[pass][4 * i + 1] = fmaf(v.y, w, Or[pass][4 * i + 1]);
+            Or[pass][4 * i + 2] = fmaf(v.z, w, Or[pass][4 * i + 2]);
+            Or[pass][4 * i + 3] = fmaf(v.w, w, Or[pass][4 * i + 3]);
+          }
+        }
+      }
+      warp_arrive(smem_u32(mempty + b), lane);  // the states are in registers: the buffer is free
+
       if (p == 1) {
-        const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
-        T* po = outp + (int64_t)seq * a.o_s0 + (int64_t)(h0 + r) * a.o_s1 + lane * DPL;
 #pragma unroll
-        for (int i = 0; i < DPL; ++i) po[i] = from_f32<T>(acc[i] * inv);
-      } else {
+        for (int pass = 0; pass < 2; ++pass) {
+          const int r = rq + 8 * pass;
+          if (r >= nh) continue;
+          const float inv = Lr[pass] > 0.f ? 1.f / Lr[pass] : 0.f;
+          T* po = outp + (int64_t)seq * a.o_s0 + (int64_t)(h0 + r) * a.o_s1 + cq;
+#pragma unroll
+          for (int i = 0; i < CQ; ++i) po[i] = from_f32<T>(Or[pass][i] * inv);
+        }
+        continue;
+      }
+      // a piece of a split unit: store the partial, count in; the last piece merges
+#pragma unroll
+      for (int pass = 0; pass < 2; ++pass) {
+        const int r = rq + 8 * pass;
+        if (r >= nh) continue;
         float* pp = sa.part + ((int64_t)me * sa.mg + r) * PR;
+        float4* dst = reinterpret_cast<float4*>(pp + cq);
 #pragma unroll
-        for (int i = 0; i < DPL; ++i) pp[lane * DPL + i] = acc[i];
-        if (lane == 0) *reinterpret_cast<float2*>(pp + D) = make_float2(M, Lsum);
+        for (int i = 0; i < CQ / 4; ++i)
+          dst[i] = make_float4(Or[pass][4 * i], Or[pass][4 * i + 1], Or[pass][4 * i + 2], Or[pass][4 * i + 3]);
+        if ((lane & 3) == 0) *reinterpret_cast<float2*>(pp + D) = make_float2(Mr[pass], Lr[pass]);
       }
-    }
-    if (p == 1) continue;
-
-    // ---- a piece of a split unit: count in; the last piece merges the unit ----
-    __threadfence();  // this piece's partial is visible GPU-wide before the arrival
-    if (!cons_sync()) return;
-    if (c == 0 && lane == 0) misc[1] = atomicAdd(sa.ucnt + first, 1);
-    if (!cons_sync()) return;
-    if (misc[1] != p - 1) continue;
-    __threadfence();  // acquire side: the other pieces' partials
-    for (int r = c; r < nh; r += kSchedConsumers) {
-      // M and L over the pieces, 32 pieces per round (lane i: piece base + i)
-      float M = -INFINITY;
-      for (int base = 0; base < p; base += 32) {
-        const int i = base + lane;
-        float mi = i < p ? __ldcg(sa.part + ((int64_t)(first + i) * sa.mg + r) * PR + D) : -INFINITY;
+      fence_acq_rel_gpu();  // this lane's partial is visible GPU-wide before the arrival
+      __syncwarp();
+      int arrived = 0;
+      if (lane == 0) arrived = atomicAdd(sa.ucnt + first, 1);
+      arrived = __shfl_sync(0xffffffffu, arrived, 0);
+      if (arrived != p - 1) continue;
+      fence_acq_rel_gpu();  // acquire side: the other pieces' partials
+      // online merge of the pieces in piece order (deterministic), 4 at a time
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mi = fmaxf(mi, __shfl_xor_sync(0xffffffffu, mi, o));
-        M = fmaxf(M, mi);
-      }
-      float Lsum = 0.f;
-      for (int base = 0; base < p; base += 32) {
-        const int i = base + lane;
-        float li = 0.f;
-        if (i < p) {
-          const float2 ml = __ldcg(reinterpret_cast<const float2*>(sa.part + ((int64_t)(first + i) * sa.mg + r) * PR + D));
-          li = ml.y * fast_exp2(ml.x - M);
+      for (int pass = 0; pass < 2; ++pass) {
+        const int r = rq + 8 * pass;
+        if (r >= nh) continue;  // lane-divergent: no warp collectives below
+        float M = -INFINITY, Lsum = 0.f, acc[CQ];
+#pragma unroll
+        for (int i = 0; i < CQ; ++i) acc[i] = 0.f;
+        for (int i0 = 0; i0 < p; i0 += 4) {
+          float2 ml[4];
+          float4 ov[4][CQ / 4];
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const int i = i0 + t < p ? i0 + t : p - 1;
+            const float* pp = sa.part + ((int64_t)(first + i) * sa.mg + r) * PR;
+            ml[t] = __ldcg(reinterpret_cast<const float2*>(pp + D));
+#pragma unroll
+            for (int v = 0; v < CQ / 4; ++v) ov[t][v] = __ldcg(reinterpret_cast<const float4*>(pp + cq) + v);
+          }
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            if (i0 + t >= p) break;
+            const float mn = fmaxf(M, ml[t].x);
+            const float sa_ = fast_exp2(M - mn), sb = fast_exp2(ml[t].x - mn);
+            Lsum = Lsum * sa_ + ml[t].y * sb;
+#pragma unroll
+            for (int v = 0; v < CQ / 4; ++v) {
+              acc[4 * v] = acc[4 * v] * sa_ + ov[t][v].x * sb;
+              acc[4 * v + 1] = acc[4 * v + 1] * sa_ + ov[t][v].y * sb;
+              acc[4 * v + 2] = acc[4 * v + 2] * sa_ + ov[t][v].z * sb;
+              acc[4 * v + 3] = acc[4 * v + 3] * sa_ + ov[t][v].w * sb;
+            }
+            M = mn;
+          }
         }
+        const float inv = 1.f / Lsum;
+        T* po = outp + (int64_t)seq * a.o_s0 + (int64_t)(h0 + r) * a.o_s1 + cq;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) li += __shfl_xor_sync(0xffffffffu, li, o);
-        Lsum += li;
+        for (int i = 0; i < CQ; ++i) po[i] = from_f32<T>(acc[i] * inv);
       }
-      const float inv = 1.f / Lsum;
-      float acc[DPL];
-#pragma unroll
-      for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
-      for (int base = 0; base < p; base += 32) {
-        const int i = base + lane;
-        float wi = 0.f;
-        if (i < p) wi = fast_exp2(__ldcg(sa.part + ((int64_t)(first + i) * sa.mg + r) * PR + D) - M) * inv;
-        const int cnt = min(32, p - base);
-        for (int t = 0; t < cnt; ++t) {
-          const float w = __shfl_sync(0xffffffffu, wi, t);
-          const float* src = sa.part + ((int64_t)(first + base + t) * sa.mg + r) * PR + lane * DPL;
-#pragma unroll
-          for (int q = 0; q < DPL; ++q) acc[q] = fmaf(__ldcg(src + q), w, acc[q]);
-        }
-      }
-      T* po = outp + (int64_t)seq * a.o_s0 + (int64_t)(h0 + r) * a.o_s1 + lane * DPL;
-#pragma unroll
-      for (int i = 0; i < DPL; ++i) po[i] = from_f32<T>(acc[i]);
+      __syncwarp();
+      if (lane == 0) sa.ucnt[first] = 0;  // zero at rest for the next decode of this schedule
     }
-    if (c == 0 && lane == 0) sa.ucnt[first] = 0;  // zero at rest for the next decode of this schedule
   }
 }
 
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
-#ifndef MVB_SCHED64_STAGES
-#define MVB_SCHED64_STAGES 32
-#endif
-#ifndef MVB_SCHED128_STAGES
-#define MVB_SCHED128_STAGES 16
-#endif
 
 SchedLayout sched_layout(int num_seqs, int num_kv_heads, int head_groups, int G, int max_blocks,
                          int block_size, int head_dim, int ctas) {
@@ -589,7 +719,7 @@ SchedLayout sched_layout(int num_seqs, int num_kv_heads, int head_groups, int G,
 }
 
 int sched_smem_bytes(int head_dim) {
-  return 1024 + (head_dim == 64 ? SchedSmem<64, MVB_SCHED64_STAGES>::BYTES : SchedSmem<128, MVB_SCHED128_STAGES>::BYTES);
+  return 1024 + (head_dim == 64 ? SchedSmem<64>::BYTES : SchedSmem<128>::BYTES);
 }
 
 cudaError_t launch_decode_schedule(const DecodeArgs& a, const SchedLayout& l, void* ws, int ctas, bool wait_at_end,
@@ -604,11 +734,11 @@ cudaError_t launch_decode_schedule(const DecodeArgs& a, const SchedLayout& l, vo
                     reinterpret_cast<int*>(w + l.off_ucnt), (int)l.max_chunks, a.err, wait_at_end ? 1 : 0);
 }
 
-template <typename T, int D, int STAGES>
+template <typename T, int D>
 cudaError_t launch_sched_t(const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a,
                            const SchedLayout& l, void* ws, int ctas, cudaStream_t stream) {
-  auto kern = decode_sched_kernel<T, D, STAGES>;
-  const int smem = 1024 + SchedSmem<D, STAGES>::BYTES;
+  auto kern = decode_sched_kernel<T, D>;
+  const int smem = 1024 + SchedSmem<D>::BYTES;
   cudaError_t e = ensure_kernel_attrs(kern, smem);
   if (e != cudaSuccess) return e;
   char* w = static_cast<char*>(ws);
@@ -619,16 +749,16 @@ cudaError_t launch_sched_t(const CUtensorMap& tmk, const CUtensorMap& tmv, const
   sa.part = reinterpret_cast<float*>(w + l.off_part);
   sa.max_chunks = (int)l.max_chunks;
   sa.mg = l.mg;
-  return launch_pdl(kern, dim3(ctas), dim3(kSchedThreads), smem, stream, tmk, tmv, a, sa);
+  return launch_pdl(kern, dim3(ctas), dim3(SchedSmem<D>::THREADS), smem, stream, tmk, tmv, a, sa);
 }
 
 cudaError_t launch_decode_sched(const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a, int dtype,
                                 int head_dim, const SchedLayout& l, void* ws, int ctas, cudaStream_t stream) {
   if (dtype == MVB_DTYPE_BF16)
-    return head_dim == 64 ? launch_sched_t<__nv_bfloat16, 64, MVB_SCHED64_STAGES>(tmk, tmv, a, l, ws, ctas, stream)
-                          : launch_sched_t<__nv_bfloat16, 128, MVB_SCHED128_STAGES>(tmk, tmv, a, l, ws, ctas, stream);
-  return head_dim == 64 ? launch_sched_t<__half, 64, MVB_SCHED64_STAGES>(tmk, tmv, a, l, ws, ctas, stream)
-                        : launch_sched_t<__half, 128, MVB_SCHED128_STAGES>(tmk, tmv, a, l, ws, ctas, stream);
+    return head_dim == 64 ? launch_sched_t<__nv_bfloat16, 64>(tmk, tmv, a, l, ws, ctas, stream)
+                          : launch_sched_t<__nv_bfloat16, 128>(tmk, tmv, a, l, ws, ctas, stream);
+  return head_dim == 64 ? launch_sched_t<__half, 64>(tmk, tmv, a, l, ws, ctas, stream)
+                        : launch_sched_t<__half, 128>(tmk, tmv, a, l, ws, ctas, stream);
 }
 
 }  // namespace mvb
