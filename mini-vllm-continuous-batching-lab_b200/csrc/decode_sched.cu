@@ -21,12 +21,13 @@
 //     rows of its head group, and publishes them in one of 4 chunk slots.  It
 //     is software-pipelined: while chunk k's block ids and query rows load,
 //     chunk k+1's descriptor and the index after it are in flight;
-//   * issuer (warp 1): walks the published chunks and issues two 2-D TMA tile
-//     loads (K and V, 16 rows x D, 128-byte swizzle) per tile into a
-//     STAGES-deep ring (one full / one empty mbarrier per stage), up to 8 tiles
-//     at once, one per lane (one thread alone issues a tile only every ~250 ns,
-//     a third of what an SM streams);
-//   * consumers (warps 2 .. NC+1): tile j of the CTA's tile sequence goes to
+//   * issuers (warps 1 .. NI): walk the published chunks and issue two 2-D TMA
+//     tile loads (K and V, 16 rows x D, 128-byte swizzle) per tile into a
+//     STAGES-deep ring (one full / one empty mbarrier per stage), in batches of
+//     8 tiles, one per lane, the batches alternating between the issuer warps:
+//     the bulk copies of one warp are accepted one after another (~60 ns each),
+//     so a single issuing warp would cap the CTA near 8 tiles per microsecond;
+//   * consumers (the next NC warps): tile j of the CTA's tile sequence goes to
 //     consumer j % NC, which runs attend_tile (mma.sync m16n8k16, online
 //     softmax, fp32 accumulate) and at the chunk end hands its state to the
 //     merger.  Every stage thus has one consumer, which waits on its phases in
@@ -36,7 +37,8 @@
 //     skipped are virtual tiles that pass through the ring without a load — so
 //     tile i of a chunk always goes to consumer i % NC and the result does not
 //     depend on timing;
-//   * merger (last warp): merges the NC consumer states of the chunk.  A chunk
+//   * mergers (the last NM warps; chunk k is merger k % NM's): merge the NC
+//     consumer states of the chunk.  A chunk
 //     that holds a whole unit is normalised and written to `out`; a piece of a
 //     longer unit writes its partial state (O, m, l per head row) and counts
 //     itself in on the unit's arrival counter, and the last piece to arrive
@@ -190,20 +192,29 @@ decode_schedule_kernel(const int* __restrict__ kv_len, int num_seqs, int units_p
 // ---------------------------------------------------------------------------
 // decode
 // ---------------------------------------------------------------------------
-// Per head dim: ring stages, consumer warps (two per SM sub-partition at D 64,
-// so one warp's MMA / shuffle / exp latency chain hides behind another's) and
-// merge buffers between the consumers and the merger.  The ring holds 128 KB in
-// flight per SM; shared memory (ring + slots + NB buffers of NC states) caps
-// NC at 4 for D = 128.
+// Per head dim: ring stages, consumer warps, merge buffers between the
+// consumers and the mergers, issuer warps (the bulk copies one warp issues are
+// accepted one after another, ~60 ns each, so a single warp caps a CTA near 8
+// tiles per microsecond) and merger warps (under full streaming load each L2
+// round trip of a merge — partial stores and fence, the arrival atomic, the
+// other pieces' partials — takes 1-2 us, so one merger warp falls behind the
+// ~7 split pieces a CTA streams at config 2).  The ring holds 128 KB in flight
+// per SM; shared memory (ring + slots + NB buffers of NC states) sets NB.
 // (Overridable at build time for tuning sweeps.)
 #ifndef MVB_SCHED64_STAGES
 #define MVB_SCHED64_STAGES 32
 #endif
 #ifndef MVB_SCHED64_NC
-#define MVB_SCHED64_NC 8
+#define MVB_SCHED64_NC 4
 #endif
 #ifndef MVB_SCHED64_NB
-#define MVB_SCHED64_NB 2
+#define MVB_SCHED64_NB 4
+#endif
+#ifndef MVB_SCHED64_NM
+#define MVB_SCHED64_NM 4
+#endif
+#ifndef MVB_SCHED64_NI
+#define MVB_SCHED64_NI 2
 #endif
 #ifndef MVB_SCHED128_STAGES
 #define MVB_SCHED128_STAGES 16
@@ -214,19 +225,30 @@ decode_schedule_kernel(const int* __restrict__ kv_len, int num_seqs, int units_p
 #ifndef MVB_SCHED128_NB
 #define MVB_SCHED128_NB 2
 #endif
+#ifndef MVB_SCHED128_NM
+#define MVB_SCHED128_NM 2
+#endif
+#ifndef MVB_SCHED128_NI
+#define MVB_SCHED128_NI 2
+#endif
 template <int D> struct SchedConfig;
 template <> struct SchedConfig<64> {
-  static constexpr int STAGES = MVB_SCHED64_STAGES, NC = MVB_SCHED64_NC, NB = MVB_SCHED64_NB;
+  static constexpr int STAGES = MVB_SCHED64_STAGES, NC = MVB_SCHED64_NC, NB = MVB_SCHED64_NB, NI = MVB_SCHED64_NI,
+                       NM = MVB_SCHED64_NM;
 };
 template <> struct SchedConfig<128> {
-  static constexpr int STAGES = MVB_SCHED128_STAGES, NC = MVB_SCHED128_NC, NB = MVB_SCHED128_NB;
+  static constexpr int STAGES = MVB_SCHED128_STAGES, NC = MVB_SCHED128_NC, NB = MVB_SCHED128_NB,
+                       NI = MVB_SCHED128_NI, NM = MVB_SCHED128_NM;
 };
 
 template <int D> struct SchedSmem {
   using Geo = MmaGeom<D>;
   static constexpr int STAGES = SchedConfig<D>::STAGES, NC = SchedConfig<D>::NC, NB = SchedConfig<D>::NB;
+  static constexpr int NI = SchedConfig<D>::NI, NM = SchedConfig<D>::NM;
   static_assert(STAGES % NC == 0, "each stage belongs to one consumer");
-  static constexpr int THREADS = (3 + NC) * 32;  // fetcher, issuer, consumers, merger
+  static_assert(STAGES % (NI * kSchedIssueLanes) == 0, "each stage belongs to one issuer");
+  static_assert(NB % NM == 0, "each merge buffer belongs to one merger");
+  static constexpr int THREADS = (1 + NI + NC + NM) * 32;  // fetcher, issuers, consumers, mergers
   static constexpr int QP = D + 8;  // query row pitch (elements): conflict-free fragment loads
   static constexpr int SLOT_BYTES = 32 + 4 * kSchedMaxPiece + 16 * QP * 2;
   // merge buffer: header (2 x int4), (m, l) [consumers][16], O [consumers][16][D]
@@ -280,6 +302,7 @@ decode_sched_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_consta
   using Geo = MmaGeom<D>;
   using L = SchedSmem<D>;
   constexpr int KC = D / 16, NO = D / 8, QP = L::QP, PR = D + 4, NB = L::NB, NC = L::NC, STAGES = L::STAGES;
+  constexpr int NI = L::NI, NM = L::NM;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem =
@@ -305,7 +328,7 @@ decode_sched_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_consta
     }
     for (int c = 0; c < kSchedSlots; ++c) {
       mbar_init(smem_u32(cfull + c), 1);        // the fetcher warp
-      mbar_init(smem_u32(cempty + c), 1 + NC);  // the issuer and consumer warps
+      mbar_init(smem_u32(cempty + c), NI + NC);  // the issuer and consumer warps
     }
     for (int b = 0; b < NB; ++b) {
       mbar_init(smem_u32(mfull + b), NC);  // the consumer warps
@@ -332,13 +355,17 @@ decode_sched_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_consta
     // ================================= fetcher =================================
     if (!a.early_inputs) grid_dependency_wait();
     bool waited = a.early_inputs == 0;
-    const int n_chunks = __ldcg(&sa.hdr->n_chunks);
     const int4 stop = make_int4(0, 0, 0, -1);
-    int idx = blockIdx.x;
+    int idx = blockIdx.x;  // the first chunk by index; its descriptor is read before the chunk
+                           // count (blockIdx.x < gridDim.x <= max_chunks: in bounds either way)
+    int4 d0 = __ldcg(sa.desc + 2 * idx), d1 = __ldcg(sa.desc + 2 * idx + 1);
+    const int n_chunks = __ldcg(&sa.hdr->n_chunks);
     bool have = idx < n_chunks;
-    int4 d0 = have ? __ldcg(sa.desc + 2 * idx) : stop;
-    int4 d1 = have ? __ldcg(sa.desc + 2 * idx + 1) : make_int4(0, 0, 0, 0);
-    int idx_n = -1;  // the next chunk (not taken yet)
+    if (!have) {
+      d0 = stop;
+      d1 = make_int4(0, 0, 0, 0);
+    }
+    int idx_n = -1;  // the next chunk (from the second iteration on)
     bool aborted = false;
     for (int k = 0;; ++k) {
       const int slot = k % kSchedSlots;
@@ -369,20 +396,21 @@ decode_sched_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_consta
         grid_dependency_wait();
         waited = true;
       }
-      if (idx_n < 0) {  // first chunk: take the second one now
-        int tk = n_chunks;
-        if (have && lane == 0) tk = (int)gridDim.x + atomicAdd(&sa.hdr->next, 1);
-        idx_n = __shfl_sync(0xffffffffu, tk, 0);
-      }
-      // in flight during the publication below: the next descriptor, the index after it
-      const bool have_n = idx_n < n_chunks;
+      // In flight during the publication below: on the first chunk the index of
+      // the second; afterwards the next descriptor and the index after it.
+      bool have_n = false;
       int4 n0 = stop, n1 = make_int4(0, 0, 0, 0);
-      if (have_n) {
-        n0 = __ldcg(sa.desc + 2 * idx_n);
-        n1 = __ldcg(sa.desc + 2 * idx_n + 1);
-      }
       int t_nn = n_chunks;
-      if (have_n && lane == 0) t_nn = (int)gridDim.x + atomicAdd(&sa.hdr->next, 1);
+      if (k == 0) {
+        if (have && lane == 0) t_nn = (int)gridDim.x + atomicAdd(&sa.hdr->next, 1);
+      } else {
+        have_n = idx_n < n_chunks;
+        if (have_n) {
+          n0 = __ldcg(sa.desc + 2 * idx_n);
+          n1 = __ldcg(sa.desc + 2 * idx_n + 1);
+          if (lane == 0) t_nn = (int)gridDim.x + atomicAdd(&sa.hdr->next, 1);
+        }
+      }
       if (k >= kSchedSlots &&
           !sched_wait_warp(smem_u32(cempty + slot), (uint32_t)((k / kSchedSlots - 1) & 1), limit, abort_flag,
                            a.err)) {
@@ -402,11 +430,21 @@ decode_sched_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_consta
       }
       warp_arrive(smem_u32(cfull + slot), lane);
       if (!have) break;  // the end marker is published
-      idx = idx_n;
-      have = have_n;
-      d0 = n0;
-      d1 = n1;
-      idx_n = __shfl_sync(0xffffffffu, t_nn, 0);
+      if (k == 0) {  // the second chunk's descriptor, and the third's index: the pipeline from here on
+        idx = __shfl_sync(0xffffffffu, t_nn, 0);
+        have = idx < n_chunks;
+        d0 = have ? __ldcg(sa.desc + 2 * idx) : stop;
+        d1 = have ? __ldcg(sa.desc + 2 * idx + 1) : make_int4(0, 0, 0, 0);
+        int t = n_chunks;
+        if (have && lane == 0) t = (int)gridDim.x + atomicAdd(&sa.hdr->next, 1);
+        idx_n = __shfl_sync(0xffffffffu, t, 0);
+      } else {
+        idx = idx_n;
+        have = have_n;
+        d0 = n0;
+        d1 = n1;
+        idx_n = __shfl_sync(0xffffffffu, t_nn, 0);
+      }
     }
     if (!aborted && lane == 0) {
       // the last CTA to reach the end of the list resets the counters
@@ -419,18 +457,20 @@ decode_sched_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_consta
     return;
   }
 
-  if (warp == 1) {
-    // ================================= issuer =================================
-    // Up to kSchedIssueLanes tiles at once, one per lane: each lane waits for
-    // its stage's previous tile to be consumed, then arms the stage's barrier
-    // and issues the K and V loads.
+  if (warp <= NI) {
+    // ================================= issuers =================================
+    // The tile sequence in batches of kSchedIssueLanes: batch j / kSchedIssueLanes
+    // is issuer warp (j / kSchedIssueLanes) % NI's, one tile per lane.  Each lane
+    // waits for its stage's previous tile to be consumed, then arms the stage's
+    // barrier and issues the K and V loads.
+    const int w = warp - 1;
     grid_dependency_wait();  // the cache is complete from here on
-    if (lane == 0) {
+    if (w == 0 && lane == 0) {
       prefetch_tensormap(&tmk);
       prefetch_tensormap(&tmv);
     }
     const uint64_t pol = l2_policy_evict_first();
-    int j_base = 0, j_last = -1;  // the CTA's tile sequence; the last tile issued
+    int j_base = 0, j_last = -1;  // the CTA's tile sequence; the end of this issuer's last batch
     for (int k = 0;; ++k) {
       const int slot = k % kSchedSlots;
       if (!sched_wait_warp(smem_u32(cfull + slot), (uint32_t)((k / kSchedSlots) & 1), limit, abort_flag, a.err))
@@ -440,9 +480,10 @@ decode_sched_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_consta
       const int* rows = slot_rows(slot);
       const int j_start = (j_base + NC - 1) / NC * NC, j_end = j_start + n;  // before j_start: virtual tiles
       bool ok = true;
-      for (int j0 = j_base; j0 < j_end; j0 += kSchedIssueLanes) {
+      for (int j0 = j_base / kSchedIssueLanes * kSchedIssueLanes; j0 < j_end; j0 += kSchedIssueLanes) {
+        if ((j0 / kSchedIssueLanes) % NI != w) continue;
         const int j = j0 + lane, st = j % STAGES;
-        const bool mine = lane < kSchedIssueLanes && j < j_end;
+        const bool mine = lane < kSchedIssueLanes && j >= j_base && j < j_end;
         bool got = true;
         if (mine && j >= STAGES)
           got = sched_wait(smem_u32(empty + st), (uint32_t)((j / STAGES - 1) & 1), limit, abort_flag, a.err);
@@ -472,19 +513,21 @@ decode_sched_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_consta
       j_base = j_end;
       warp_arrive(smem_u32(cempty + slot), lane);
     }
-    // Wait (bounded, without the abort shortcut) for the loads still in flight,
-    // the latest use of every stage, so no copy lands after the CTA has left.
+    // Wait (bounded, without the abort shortcut) for this issuer's loads still in
+    // flight, the latest use of each of its stages, so no copy lands after the
+    // CTA has left.
     for (int i = lane; i < STAGES; i += 32) {
       const int jj = j_last - i;
-      if (jj < 0 || ((int)blockIdx.x == a.hold_warp && jj == a.hold_tile)) continue;
+      if (jj < 0 || (jj / kSchedIssueLanes) % NI != w || ((int)blockIdx.x == a.hold_warp && jj == a.hold_tile))
+        continue;
       mbar_wait_bounded(smem_u32(full + jj % STAGES), (uint32_t)((jj / STAGES) & 1), limit);
     }
     return;
   }
 
-  if (warp < 2 + NC) {
+  if (warp < 1 + NI + NC) {
     // ================================ consumers ================================
-    const int c = warp - 2;
+    const int c = warp - 1 - NI;
     const int g0 = lane >> 2, qd = lane & 3;
     int j_base = 0;
     for (int k = 0;; ++k) {
@@ -531,48 +574,53 @@ decode_sched_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_consta
       }
       j_base = j_end;
 
-      // ---- hand this consumer's state (or the end marker) to the merger ----
-      const int b = k % NB;
-      if (k >= NB &&
-          !sched_wait_warp(smem_u32(mempty + b), (uint32_t)((k / NB - 1) & 1), limit, abort_flag, a.err))
-        return;
-      if (n >= 0) {
+      // ---- hand this consumer's state to the chunk's merger; at the end, the
+      // end marker to every merger (chunks k .. k + NM - 1) ----
+      for (int e = 0; e < (n < 0 ? NM : 1); ++e) {
+        const int kk = k + e, b = kk % NB;
+        if (kk >= NB &&
+            !sched_wait_warp(smem_u32(mempty + b), (uint32_t)((kk / NB - 1) & 1), limit, abort_flag, a.err))
+          return;
+        if (n >= 0) {
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
-          lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 1);
-          lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 2);
-        }
-        const int nh = min(16, a.G - (d0.y % a.head_groups) * 16);
-        float* mo = mb_o(b) + c * 16 * D;
+          for (int r = 0; r < 2; ++r) {
+            lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 1);
+            lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 2);
+          }
+          const int nh = min(16, a.G - (d0.y % a.head_groups) * 16);
+          float* mo = mb_o(b) + c * 16 * D;
 #pragma unroll
-        for (int nn = 0; nn < NO; ++nn) {
-          const int d = nn * 8 + 2 * qd;
-          if (g0 < nh) *reinterpret_cast<float2*>(mo + g0 * D + d) = make_float2(o[nn][0], o[nn][1]);
-          if (g0 + 8 < nh) *reinterpret_cast<float2*>(mo + (g0 + 8) * D + d) = make_float2(o[nn][2], o[nn][3]);
+          for (int nn = 0; nn < NO; ++nn) {
+            const int d = nn * 8 + 2 * qd;
+            if (g0 < nh) *reinterpret_cast<float2*>(mo + g0 * D + d) = make_float2(o[nn][0], o[nn][1]);
+            if (g0 + 8 < nh) *reinterpret_cast<float2*>(mo + (g0 + 8) * D + d) = make_float2(o[nn][2], o[nn][3]);
+          }
+          if (qd == 0) {
+            float2* mml = mb_ml(b) + c * 16;
+            if (g0 < nh) mml[g0] = make_float2(mrow[0], lrow[0]);
+            if (g0 + 8 < nh) mml[g0 + 8] = make_float2(mrow[1], lrow[1]);
+          }
         }
-        if (qd == 0) {
-          float2* mml = mb_ml(b) + c * 16;
-          if (g0 < nh) mml[g0] = make_float2(mrow[0], lrow[0]);
-          if (g0 + 8 < nh) mml[g0 + 8] = make_float2(mrow[1], lrow[1]);
+        if (c == 0 && lane == 0) {
+          mb_hdr(b)[0] = d0;
+          mb_hdr(b)[1] = d1;
         }
+        warp_arrive(smem_u32(mfull + b), lane);
       }
-      if (c == 0 && lane == 0) {
-        mb_hdr(b)[0] = d0;
-        mb_hdr(b)[1] = d1;
-      }
-      warp_arrive(smem_u32(mfull + b), lane);
       if (n < 0) return;
     }
   }
 
-  // ================================== merger ==================================
-  // Lane l takes head row r = l / 4 (+ 8 on a second pass for more than 8 heads)
-  // and column quarter l % 4 (CQ = D / 4 columns).
+  // ================================== mergers =================================
+  // Merger m takes chunks k with k % NM == m, through its own buffers
+  // b = k % NB (b % NM == m).  Lane l takes head row r = l / 4 (+ 8 on a second
+  // pass for more than 8 heads) and column quarter l % 4 (CQ = D / 4 columns).
   {
     constexpr int CQ = D / 4;
+    const int m = warp - (1 + NI + NC);
     const int rq = lane >> 2, cq = (lane & 3) * CQ;
     T* const outp = static_cast<T*>(a.out);
-    for (int k = 0;; ++k) {
+    for (int k = m;; k += NM) {
       const int b = k % NB;
       if (!sched_wait_warp(smem_u32(mfull + b), (uint32_t)((k / NB) & 1), limit, abort_flag, a.err)) return;
       const int4 d0 = mb_hdr(b)[0], d1 = mb_hdr(b)[1];
