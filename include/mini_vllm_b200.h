@@ -62,15 +62,15 @@ extern "C" {
                                      (internal: the planned bound was wrong)   */
 
 /* ---- decode kernel variants --------------------------------------------- */
-#define MVB_DECODE_AUTO 0  /* SCHED when eligible, else FMA                      */
+#define MVB_DECODE_AUTO 0  /* STREAM when eligible, else SCHED, else FMA          */
 #define MVB_DECODE_FMA  1  /* CUDA-core FP32 FMA kernel (any dtype, any BS)      */
 #define MVB_DECODE_MMA  2  /* TMA-staged tensor-core kernel, one CTA per (seq, KV head),
                               split-K + reduction for long contexts (bf16/f16, BS%16==0) */
 #define MVB_DECODE_STREAM 3 /* persistent stream-K variant of MVB_DECODE_MMA: equal tile
                               ranges per warp + a fixup kernel merging cut units
                               (num_seqs <= 4096) */
-#define MVB_DECODE_SCHED 4  /* scheduled persistent variant (AUTO's choice when bf16/f16,
-                              BS%16==0): a schedule kernel lists every (seq, KV head)
+#define MVB_DECODE_SCHED 4  /* scheduled persistent variant (bf16/f16, BS%16==0, any batch
+                              size): a schedule kernel lists every (seq, KV head)
                               unit cut into pieces of <= 32 tiles, longest first; one CTA
                               per SM takes pieces from a global counter (TMA ring, warp
                               roles), and the last piece of a split unit merges it */

@@ -134,7 +134,9 @@ int make_plan(int num_seqs, int num_heads, int num_kv_heads, int head_dim, int b
                                 sm_count_current());
   const bool sched_ok = mma_ok && sl.max_chunks < ((int64_t)1 << 30);
   int v = variant;
-  if (v == MVB_DECODE_AUTO) v = sched_ok ? MVB_DECODE_SCHED : MVB_DECODE_FMA;
+  // AUTO: the stream kernel where it applies (measured fastest at configs 2-4),
+  // else the scheduled kernel (any batch size), else CUDA cores
+  if (v == MVB_DECODE_AUTO) v = stream_ok ? MVB_DECODE_STREAM : sched_ok ? MVB_DECODE_SCHED : MVB_DECODE_FMA;
   if (v != MVB_DECODE_FMA && v != MVB_DECODE_MMA && v != MVB_DECODE_STREAM && v != MVB_DECODE_SCHED)
     return MVB_ERR_VARIANT;
   if (v == MVB_DECODE_MMA && !mma_ok) return MVB_ERR_VARIANT;

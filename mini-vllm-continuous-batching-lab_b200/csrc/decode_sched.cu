@@ -205,13 +205,13 @@ decode_schedule_kernel(const int* __restrict__ kv_len, int num_seqs, int units_p
 #define MVB_SCHED64_STAGES 32
 #endif
 #ifndef MVB_SCHED64_NC
-#define MVB_SCHED64_NC 4
+#define MVB_SCHED64_NC 8
 #endif
 #ifndef MVB_SCHED64_NB
-#define MVB_SCHED64_NB 4
+#define MVB_SCHED64_NB 2
 #endif
 #ifndef MVB_SCHED64_NM
-#define MVB_SCHED64_NM 4
+#define MVB_SCHED64_NM 2
 #endif
 #ifndef MVB_SCHED64_NI
 #define MVB_SCHED64_NI 2

@@ -15,9 +15,13 @@ keep the test short; weights ~ N(0, 0.02)) serves the same requests on two
 engines, one with the reference's torch backend ("reference") and one with
 "b200".  Chunked prefill (64-token chunks over prompts of up to 300 tokens)
 reads cached prefixes through the gather kernel, and every decode step runs
-the scheduled decode kernel.  The logits of every step must agree within
-LOGIT_ATOL, and the greedy tokens must agree wherever the top-2 margin of the
-reference's logits exceeds twice that bound.
+the scheduled decode kernel.  Every step's logits must agree within
+LOGIT_ATOL row by row (rows are sequences), and the greedy tokens must agree
+wherever the reference's top-2 margin exceeds twice that bound.  Where the
+margin is smaller (a near-tie: random weights make logits of ~8k tokens
+close), the two engines may sample different tokens; that sequence then
+continues from a different token in each engine, and its later rows are no
+longer compared.
 """
 
 from __future__ import annotations
@@ -71,7 +75,7 @@ def _run_engine(model_path: str, backend: str, prompts, max_new_tokens: int):
 
     def record(model_input):
         out = inner(model_input)
-        logits.append(out.float().cpu())
+        logits.append((out.float().cpu(), _sampled_ids(model_input)))
         return out
 
     runner.execute_model = record
@@ -79,6 +83,11 @@ def _run_engine(model_path: str, backend: str, prompts, max_new_tokens: int):
         eng.add_request(RE.prompt_text(ids), max_new_tokens=max_new_tokens)
     outputs = eng.run_until_done()
     return outputs, logits, type(eng._executor._attention_backend).__name__
+
+
+def _sampled_ids(model_input):
+    """The sequence of each logits row: the sequences with a sample index, in order."""
+    return [info.sequence_id for info in model_input.sequence_info if info.sample_output_index is not None]
 
 
 def test_engine_logits_match_the_reference_backend(checkpoint):
@@ -89,18 +98,25 @@ def test_engine_logits_match_the_reference_backend(checkpoint):
     b2_out, b2_logits, b2_cls = _run_engine(checkpoint, "b200", prompts, 12)
     assert ref_cls == "AttentionBackendRef" and b2_cls == "AttentionBackendB200"
     assert len(ref_logits) == len(b2_logits) > 12  # prefill chunks, then decode steps
-    worst = 0.0
-    for step, (a, b) in enumerate(zip(ref_logits, b2_logits)):
-        assert a.shape == b.shape, step
+    worst, compared, diverged = 0.0, 0, set()
+    for step, ((a, ids_a), (b, ids_b)) in enumerate(zip(ref_logits, b2_logits)):
+        assert ids_a == ids_b and a.shape == b.shape, step
         assert torch.isfinite(b).all(), step
-        d = (a - b).abs().max().item()
-        worst = max(worst, d)
-        assert d <= LOGIT_ATOL, f"step {step}: max |logit diff| {d:.3e}"
-        top2 = a.topk(2, dim=-1).values
-        clear = (top2[:, 0] - top2[:, 1]) > 2 * LOGIT_ATOL
-        assert torch.equal(a.argmax(-1)[clear], b.argmax(-1)[clear]), step
+        for row, sid in enumerate(ids_a):
+            if sid in diverged:
+                continue
+            d = (a[row] - b[row]).abs().max().item()
+            worst = max(worst, d)
+            compared += 1
+            assert d <= LOGIT_ATOL, f"step {step} sequence {sid}: max |logit diff| {d:.3e}"
+            if a[row].argmax() != b[row].argmax():
+                top2 = a[row].topk(2).values
+                assert top2[0] - top2[1] <= 2 * LOGIT_ATOL, f"step {step} sequence {sid}: tokens differ"
+                diverged.add(sid)  # a near-tie: the engines continue from different tokens
+    assert compared > 40 and len(diverged) <= 2
     assert sorted(ref_out) == sorted(b2_out)
-    print(f"engine drop-in: {len(ref_logits)} steps, max |logit diff| {worst:.3e}")
+    print(f"engine drop-in: {len(ref_logits)} steps, {compared} rows compared, max |logit diff| {worst:.3e}, "
+          f"near-tie divergences {len(diverged)}")
 
 
 def test_unknown_backend_still_raises(checkpoint):

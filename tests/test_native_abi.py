@@ -71,8 +71,12 @@ def _plan(**kw):
     return M.decode_plan(**args)
 
 
-def test_plan_headline_config_uses_the_scheduled_kernel():
-    p = _plan()
+def test_plan_headline_config_uses_the_stream_kernel():
+    assert _plan()["variant"] == "stream"
+
+
+def test_plan_scheduled_kernel_when_asked():
+    p = _plan(variant="sched")
     assert p["variant"] == "sched" and p["num_partitions"] == 0
     # header + per chunk: a 32-byte descriptor, an arrival counter and a partial
     # state of 7 head rows x (64 + 4) floats, for the bound of
