@@ -343,8 +343,8 @@ def ours(args, rank, world, local_rank):
         # schedule serves the step's L layer-steps
         nonlocal sched
         if scheduled:
-            sched = M.build_decode_schedule(kvl, spec.num_heads, spec.num_kv_heads, spec.head_dim,
-                                            spec.block_size, spec.num_blocks, spec.max_blocks, torch.bfloat16,
+            sched = M.build_decode_schedule(kvl, bt, spec.num_heads, spec.num_kv_heads, spec.head_dim,
+                                            spec.block_size, spec.num_blocks, torch.bfloat16,
                                             schedule=sched, strict=False)
 
     def step(layer):

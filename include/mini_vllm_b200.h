@@ -69,11 +69,12 @@ extern "C" {
 #define MVB_DECODE_STREAM 3 /* persistent stream-K variant of MVB_DECODE_MMA: equal tile
                               ranges per warp + a fixup kernel merging cut units
                               (num_seqs <= 4096) */
-#define MVB_DECODE_SCHED 4  /* scheduled persistent variant (bf16/f16, BS%16==0, any batch
-                              size): a schedule kernel lists every (seq, KV head)
-                              unit cut into pieces of <= 32 tiles, longest first; one CTA
-                              per SM takes pieces from a global counter (TMA ring, warp
-                              roles), and the last piece of a split unit merges it */
+#define MVB_DECODE_SCHED 4  /* scheduled persistent variant (bf16/f16, BS%16==0, up to 16384
+                              sequences): a per-step schedule cuts the tile stream of every
+                              (seq, KV head) unit into one equal range per SM and resolves
+                              its pool rows; one CTA per SM streams its range with
+                              self-issuing consumer warps, and the last piece of a unit cut
+                              by a range boundary merges it */
 
 /* Logical -> physical gather of cached K/V for a batch of sequences (the
  * prefill path's prefix read) into contiguous [total_tokens, KH, D] outputs:
@@ -154,7 +155,8 @@ int mvb_build_step_metadata(const int64_t* blocks, const int64_t* block_starts, 
  * except that the load of one tile is never issued and every pipeline wait
  * gives up after `wait_limit` (1 .. 2^22) try-waits.  The held tile is local
  * tile `hold_tile` of stream warp `hold_warp` (MVB_DECODE_STREAM), or tile
- * number `hold_tile` that CTA `hold_warp` loads (MVB_DECODE_SCHED).  The wait
+ * number `hold_tile` of consumer warp `hold_warp` (CTA * consumers per CTA +
+ * consumer, 11 consumers at head_dim 64 and 6 at 128; MVB_DECODE_SCHED).  The wait
  * on it runs out and reports MVB_DEV_TIMEOUT; the kernel's other waits give up
  * too (the scheduled kernel aborts the whole CTA), each role waits (bounded)
  * for its own loads in flight and leaves, and the context stays usable.  Used
@@ -183,8 +185,8 @@ int mvb_test_decode_wait_timeout(const void* query, int64_t q_stride_seq, int64_
 
 /* Flag ORed into `variant` of mvb_paged_decode with MVB_DECODE_SCHED: the
  * workspace already holds the schedule of this batch, built by
- * mvb_paged_decode_schedule from the same kv_len contents and shape arguments
- * (kv_len and the block tables are the same for every layer of a model step,
+ * mvb_paged_decode_schedule from the same kv_len and block-table contents and
+ * shape arguments (kv_len and the block tables are the same for every layer of a model step,
  * so one schedule serves all of them).  Without the flag the call builds the
  * schedule itself (one extra launch).  The decode reads the schedule before
  * its grid-dependency wait only when MVB_DECODE_AFTER_WRITE is also set; the
@@ -194,22 +196,27 @@ int mvb_test_decode_wait_timeout(const void* query, int64_t q_stride_seq, int64_
 
 /*
  * Build the decode schedule of a batch (variant MVB_DECODE_SCHED) into
- * `workspace`: the list of pieces ("chunks") of every (sequence, KV head,
- * head group) unit, longest first, and the counters the decode hands them out
- * with.  It reads only kv_len (int32 [num_seqs], device memory); the shape
- * arguments are those of the decodes that will use it, and workspace_bytes
- * must be at least the plan's (mvb_paged_decode_plan with variant
- * MVB_DECODE_SCHED).  A sequence whose kv_len is < 1 or needs more than
- * max_blocks_per_seq blocks sets MVB_DEV_KV_LEN / MVB_DEV_TABLE_SHORT here and
- * gets zero output rows from every decode that uses the schedule.  `flags`:
+ * `workspace`: the stream of 16-token tiles of every (sequence, KV head, head
+ * group) unit cut into one contiguous range per SM, each range's pieces (the
+ * units it covers, the ones cut by its ends first) and the pool row of every
+ * tile.  It reads kv_len (int32 [num_seqs]) and the block tables (int64,
+ * row stride block_table_stride), both in device memory; the shape arguments
+ * are those of the decodes that will use it, and workspace_bytes must be at
+ * least the plan's (mvb_paged_decode_plan with variant MVB_DECODE_SCHED).  A
+ * sequence whose kv_len is < 1 or needs more than max_blocks_per_seq blocks
+ * sets MVB_DEV_KV_LEN / MVB_DEV_TABLE_SHORT and gets zero output rows from
+ * every decode that uses the schedule; a block id outside [0, num_blocks)
+ * sets MVB_DEV_BLOCK_ID and its tile is skipped.  `flags`:
  * MVB_DECODE_AFTER_WRITE when the kernel launched just before on `stream` is
  * the KV write (the schedule is then computed while the write runs).  No
  * reference counterpart: the Triton decode (paged_attention_gpu.py:252-321)
  * has no per-step set-up; this hoists the work every layer's decode would
- * repeat out of the per-layer calls.  A decode that reported MVB_DEV_TIMEOUT
- * leaves the schedule's counters dirty: build it again before the next call.
+ * repeat (the block-table walk) out of the per-layer calls.  A decode that
+ * reported MVB_DEV_TIMEOUT may leave the schedule's counters dirty: build it
+ * again before the next call.
  */
-int mvb_paged_decode_schedule(const int32_t* kv_len, int32_t num_seqs, int32_t num_heads,
+int mvb_paged_decode_schedule(const int32_t* kv_len, const int64_t* block_table,
+                              int64_t block_table_stride, int32_t num_seqs, int32_t num_heads,
                               int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
                               int32_t num_blocks, int32_t max_blocks_per_seq, int32_t dtype,
                               int32_t flags, void* workspace, int64_t workspace_bytes,

@@ -440,6 +440,7 @@ def _decode_fast(query, key_cache, value_cache, block_table, kv_len_after, block
     if schedule is not None:
         if variant not in ("auto", "sched"):
             return None
+        variant = "sched"  # a schedule is the scheduled kernel's
         flags |= _native.DECODE_SCHEDULE_READY
         ws = schedule.workspace
     status, res = fast.decode(query, key_cache, value_cache, block_table, kv_len_after, block_size,
@@ -458,14 +459,15 @@ def _decode_fast(query, key_cache, value_cache, block_table, kv_len_after, block
 
 class DecodeSchedule:
     """The per-step work list of the scheduled decode kernel (variant
-    ``"sched"``) and the device workspace it lives in.
+    ``"sched"``) and the device workspace it lives in: every SM's range of the
+    step's KV tiles, its pieces and the pool row of each tile.
 
     kv_len and the block tables are the same for every layer of a model step,
     so one schedule, built once per step by ``build_decode_schedule``, serves
-    every layer's ``paged_decode_attention(..., schedule=...)``.  It depends
-    only on the contents of ``kv_len_after`` and on the shapes it was built
-    for; build it again whenever those change, and after a call that raised a
-    device timeout (which leaves its counters dirty).
+    every layer's ``paged_decode_attention(..., schedule=...)``.  It depends on
+    the contents of ``kv_len_after`` and ``block_tables`` and on the shapes it
+    was built for; build it again whenever those change, and after a call that
+    raised a device timeout (which may leave its counters dirty).
     """
 
     __slots__ = ("workspace", "key")
@@ -477,12 +479,12 @@ class DecodeSchedule:
 
 def build_decode_schedule(
     kv_len_after: torch.Tensor,
+    block_tables: torch.Tensor,
     num_heads: int,
     num_kv_heads: int,
     head_dim: int,
     block_size: int,
     num_blocks: int,
-    max_blocks_per_seq: int,
     dtype: torch.dtype,
     *,
     schedule: Optional[DecodeSchedule] = None,
@@ -490,16 +492,23 @@ def build_decode_schedule(
     strict: bool = True,
 ) -> DecodeSchedule:
     """Build the decode schedule of a batch (``mvb_paged_decode_schedule``, one
-    launch on the current stream) for decodes of the given shape.  ``schedule``
-    reuses an earlier schedule's workspace when it is large enough.
-    ``after_write``: the kernel launched just before on the current stream is
-    ``paged_cache_write`` (the schedule is then computed while it runs)."""
+    launch on the current stream) for decodes of the given shape, with
+    ``block_tables`` ``[num_seqs, max_blocks_per_seq]`` (``-1`` padded).
+    ``schedule`` reuses an earlier schedule's workspace when it is large
+    enough.  ``after_write``: the kernel launched just before on the current
+    stream is ``paged_cache_write`` (the schedule is then computed while it
+    runs)."""
     _require(kv_len_after.dim() == 1 and kv_len_after.is_cuda,
              lambda: f"kv_len_after must be a 1-D CUDA tensor, got {tuple(kv_len_after.shape)}")
     if kv_len_after.dtype != torch.int32 or not kv_len_after.is_contiguous():
         kv_len_after = kv_len_after.to(torch.int32).contiguous()
     num_seqs = kv_len_after.shape[0]
     dev_idx = kv_len_after.get_device()
+    _require(block_tables.dim() == 2 and block_tables.shape[0] == num_seqs,
+             lambda: f"block_tables must be [num_seqs={num_seqs}, max_blocks], got {tuple(block_tables.shape)}")
+    if block_tables.dtype != torch.int64 or block_tables.get_device() != dev_idx or block_tables.stride(1) != 1:
+        block_tables = block_tables.to(device=kv_len_after.device, dtype=torch.int64).contiguous()
+    max_blocks_per_seq = block_tables.shape[1]
     plan = _cached_plan(dev_idx, num_seqs, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
                         max_blocks_per_seq, dtype, "sched", None, 16)
     nbytes = plan["workspace_bytes"]
@@ -510,7 +519,8 @@ def build_decode_schedule(
         ws = torch.zeros(nbytes, dtype=torch.uint8, device=kv_len_after.device)
     state = _state(dev_idx)
     status = _native.lib().mvb_paged_decode_schedule(
-        kv_len_after.data_ptr(), num_seqs, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
+        kv_len_after.data_ptr(), block_tables.data_ptr(), block_tables.stride(0), num_seqs, num_heads,
+        num_kv_heads, head_dim, block_size, num_blocks,
         max_blocks_per_seq, _DTYPE_CODES[dtype], _native.DECODE_AFTER_WRITE if after_write else 0,
         ws.data_ptr(), ws.numel(), state.err_ptr, _stream_handle(dev_idx))
     _host_status(status, "paged decode schedule")
@@ -552,7 +562,9 @@ def paged_decode_attention(
         scale: softmax scale, default ``head_dim ** -0.5``.
     Keyword-only extensions: ``out`` (write in place), ``variant``
     (``"auto" | "sched" | "stream" | "mma" | "fma"``; ``"auto"`` is
-    ``"sched"`` for bf16/f16 caches with block sizes that are multiples of 16),
+    ``"stream"`` for bf16/f16 caches with block sizes that are multiples of 16
+    and batches it serves, else ``"sched"`` where that applies, else ``"fma"``;
+    with ``schedule`` it is ``"sched"``),
     ``partition_tokens`` (split-K partition length of the ``"mma"`` / ``"fma"``
     kernels; ``None`` lets the library choose), ``strict``, ``after_write``
     (the kernel launched just before this call on the current stream is
@@ -565,6 +577,8 @@ def paged_decode_attention(
 
     Returns ``[total_decode, num_q_heads, head_dim]`` in the query's dtype.
     """
+    if schedule is not None and variant == "auto":
+        variant = "sched"
     res = _decode_fast(query, key_cache, value_cache, block_table, kv_len_after, block_size, scale, out,
                        variant, partition_tokens, strict, after_write, schedule)
     if res is not None:
@@ -1006,8 +1020,8 @@ class AttentionBackendB200(AttentionBackend):
         if plan["variant"] != "sched":
             return None
         self._schedule_key = None
-        self._schedule = build_decode_schedule(kvl, query.shape[1], kc.shape[1], query.shape[2], block_size,
-                                               kc.shape[0], bt.shape[1], query.dtype, schedule=self._schedule,
+        self._schedule = build_decode_schedule(kvl, bt, query.shape[1], kc.shape[1], query.shape[2], block_size,
+                                               kc.shape[0], query.dtype, schedule=self._schedule,
                                                after_write=after, strict=False)
         self._schedule_key = key
         self._schedule_built_now = True

@@ -26,10 +26,10 @@ int stream_warps_per_cta(int head_dim);
 int stream_smem_bytes(int head_dim, int num_seqs);
 SchedLayout sched_layout(int num_seqs, int num_kv_heads, int head_groups, int G, int max_blocks,
                          int block_size, int head_dim, int ctas);
-cudaError_t launch_decode_schedule(const DecodeArgs& a, const SchedLayout& l, void* ws, int ctas, bool wait_at_end,
-                                   cudaStream_t stream);
+cudaError_t launch_decode_schedule(const DecodeArgs& a, int head_dim, const SchedLayout& l, void* ws,
+                                   bool wait_at_end, cudaStream_t stream);
 cudaError_t launch_decode_sched(const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a, int dtype,
-                                int head_dim, const SchedLayout& l, void* ws, int ctas, cudaStream_t stream);
+                                int head_dim, const SchedLayout& l, void* ws, cudaStream_t stream);
 
 // cuTensorMapEncodeTiled from the driver (nullptr when the driver lacks it);
 // shared by the decode (pool maps) and the gather (output maps).
@@ -49,7 +49,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 namespace {
 
-constexpr int kAbiVersion = 3;
+constexpr int kAbiVersion = 4;
 // Longest context the auto plan serves with one CTA per (sequence, KV head);
 // beyond it the flash-decoding split is used.
 constexpr int64_t kUnsplitMaxTokens = 8192;
@@ -132,7 +132,7 @@ int make_plan(int num_seqs, int num_heads, int num_kv_heads, int head_dim, int b
   const int hg16 = (G + kMmaHeadGroup - 1) / kMmaHeadGroup;
   SchedLayout sl = sched_layout(num_seqs, num_kv_heads, hg16, G, max_blocks, block_size, head_dim,
                                 sm_count_current());
-  const bool sched_ok = mma_ok && sl.max_chunks < ((int64_t)1 << 30);
+  const bool sched_ok = mma_ok && sl.ok;
   int v = variant;
   // AUTO: the stream kernel where it applies (measured fastest at configs 2-4),
   // else the scheduled kernel (any batch size), else CUDA cores
@@ -427,14 +427,13 @@ int mvb_paged_decode(const void* query, int64_t q_stride_seq, int64_t q_stride_h
     if (!pool_tensor_map(key_cache, rows, head_dim, dtype, &tmk) ||
         !pool_tensor_map(value_cache, rows, head_dim, dtype, &tmv))
       return MVB_ERR_TENSOR_MAP;
-    const int ctas = sm_count_current();
     if (!sched_ready) {
       // build the schedule first; the decode then waits for it before reading anything
-      e = launch_decode_schedule(a, pl.sched, workspace, ctas, after_write, s);
+      e = launch_decode_schedule(a, head_dim, pl.sched, workspace, after_write, s);
       if (e != cudaSuccess) return MVB_ERR_CUDA;
       a.early_inputs = 0;
     }
-    e = launch_decode_sched(tmk, tmv, a, dtype, head_dim, pl.sched, workspace, ctas, s);
+    e = launch_decode_sched(tmk, tmv, a, dtype, head_dim, pl.sched, workspace, s);
     return e == cudaSuccess ? MVB_OK : MVB_ERR_CUDA;
   }
   if (pl.variant == MVB_DECODE_STREAM) {
@@ -466,11 +465,11 @@ int mvb_paged_decode(const void* query, int64_t q_stride_seq, int64_t q_stride_h
   return MVB_OK;
 }
 
-int mvb_paged_decode_schedule(const int32_t* kv_len, int32_t num_seqs, int32_t num_heads,
-                              int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
-                              int32_t num_blocks, int32_t max_blocks_per_seq, int32_t dtype,
-                              int32_t flags, void* workspace, int64_t workspace_bytes,
-                              int32_t* error_flags, void* stream) {
+int mvb_paged_decode_schedule(const int32_t* kv_len, const int64_t* block_table, int64_t block_table_stride,
+                              int32_t num_seqs, int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+                              int32_t block_size, int32_t num_blocks, int32_t max_blocks_per_seq, int32_t dtype,
+                              int32_t flags, void* workspace, int64_t workspace_bytes, int32_t* error_flags,
+                              void* stream) {
   mvb::NvtxRange nvtx_range("mvb_paged_decode_schedule");
   Plan pl;
   const int st = make_plan(num_seqs, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
@@ -478,11 +477,14 @@ int mvb_paged_decode_schedule(const int32_t* kv_len, int32_t num_seqs, int32_t n
   if (st != MVB_OK) return st;
   if ((flags & ~MVB_DECODE_AFTER_WRITE) != 0) return MVB_ERR_INVALID_ARG;
   if (num_seqs == 0) return MVB_OK;
-  if (!kv_len || !error_flags) return MVB_ERR_INVALID_ARG;
+  if (!kv_len || !block_table || !error_flags) return MVB_ERR_INVALID_ARG;
+  if (max_blocks_per_seq > 0 && block_table_stride < max_blocks_per_seq) return MVB_ERR_INVALID_ARG;
   if (workspace == nullptr || workspace_bytes < pl.ws_bytes || !aligned_to(workspace, 256))
     return MVB_ERR_WORKSPACE;
   DecodeArgs a = {};
   a.kv_len = kv_len;
+  a.bt = block_table;
+  a.bt_s0 = block_table_stride;
   a.num_seqs = num_seqs;
   a.num_heads = num_heads;
   a.num_kv_heads = num_kv_heads;
@@ -492,7 +494,7 @@ int mvb_paged_decode_schedule(const int32_t* kv_len, int32_t num_seqs, int32_t n
   a.max_blocks = max_blocks_per_seq;
   a.num_blocks = num_blocks;
   a.err = error_flags;
-  const cudaError_t e = launch_decode_schedule(a, pl.sched, workspace, sm_count_current(),
+  const cudaError_t e = launch_decode_schedule(a, head_dim, pl.sched, workspace,
                                                (flags & MVB_DECODE_AFTER_WRITE) != 0,
                                                static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? MVB_OK : MVB_ERR_CUDA;

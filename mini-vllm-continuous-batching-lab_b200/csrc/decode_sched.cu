@@ -2,88 +2,95 @@
 //
 // Two kernels.
 //
-// decode_schedule_kernel (once per model step: kv_len and the block tables are
-// the same for every layer of a step) cuts every unit — (sequence, KV head,
-// head group of <= 16 query heads) — into pieces of at most `piece` 16-token
-// tiles, split evenly (piece sizes of one unit differ by at most one tile),
-// and lists the pieces ("chunks") longest first: units are bucketed by piece
-// size, buckets in decreasing order, and the pieces of one unit are adjacent.
-// `piece` is chosen from the step's total tile count so that there are about
-// two chunks per CTA of the decode grid or more (4..32 tiles).
+// decode_schedule_kernel runs once per model step (kv_len and the block tables
+// are the same for every layer of a step).  The decode's work is the stream of
+// 16-token K/V tiles of every unit — (sequence, KV head, head group of <= 16
+// query heads) — in sequence order.  The schedule cuts that stream into one
+// contiguous range per CTA of the decode grid (one CTA per SM; the lengths
+// differ by at most one tile) and writes, for each CTA:
+//   * its pieces: the part of each unit its range covers.  A unit cut by a
+//     range boundary has one piece in every CTA it spans.  The piece cut by the
+//     range's end is processed first, the piece cut by its start second and the
+//     whole units longest first, so the partial states of cut units are stored
+//     early and merged while the CTAs stream their longest whole units;
+//   * the pool row of each of its tiles, in processing order: the block-table
+//     lookups of every layer of the step, done once;
+//   * a 256-byte record at a fixed place: where its pieces and rows are, its
+//     first two pieces and the first rows of every consumer warp, so that a
+//     decode CTA issues its first loads after one read.
+// Sequences with kv_len < 1 or a block table too short for kv_len are left out
+// of the stream and listed apart; the decode writes zeros to their rows.
 //
-// decode_sched_kernel runs one CTA per SM over that list.  Each CTA takes its
-// first chunk by index (blockIdx.x) and every further one from a global
-// counter, so SMs that stream faster take more chunks and the last chunks
-// handed out are the smallest: no per-warp static range, no random tail.
-// Warp roles inside the CTA:
-//   * fetcher (warp 0): takes the next chunk index, loads its descriptor, the
-//     block ids of its tiles (validated, turned into pool rows) and the query
-//     rows of its head group, and publishes them in one of 4 chunk slots.  It
-//     is software-pipelined: while chunk k's block ids and query rows load,
-//     chunk k+1's descriptor and the index after it are in flight;
-//   * issuers (warps 1 .. NI): walk the published chunks and issue two 2-D TMA
-//     tile loads (K and V, 16 rows x D, 128-byte swizzle) per tile into a
-//     STAGES-deep ring (one full / one empty mbarrier per stage), in batches of
-//     8 tiles, one per lane, the batches alternating between the issuer warps:
-//     the bulk copies of one warp are accepted one after another (~60 ns each),
-//     so a single issuing warp would cap the CTA near 8 tiles per microsecond;
-//   * consumers (the next NC warps): tile j of the CTA's tile sequence goes to
-//     consumer j % NC, which runs attend_tile (mma.sync m16n8k16, online
-//     softmax, fp32 accumulate) and at the chunk end hands its state to the
-//     merger.  Every stage thus has one consumer, which waits on its phases in
-//     order (a parity wait is sound only while its waiter is at most one phase
-//     away; consumers sharing stages drifted further apart than the ring).  A
-//     chunk's tiles start on a multiple of NC of the sequence — the places
-//     skipped are virtual tiles that pass through the ring without a load — so
-//     tile i of a chunk always goes to consumer i % NC and the result does not
-//     depend on timing;
-//   * mergers (the last NM warps; chunk k is merger k % NM's): merge the NC
-//     consumer states of the chunk.  A chunk
-//     that holds a whole unit is normalised and written to `out`; a piece of a
-//     longer unit writes its partial state (O, m, l per head row) and counts
-//     itself in on the unit's arrival counter, and the last piece to arrive
-//     merges all pieces in piece order (deterministic) and writes the unit.
-// The consumers never wait for global memory, so the ring keeps streaming
-// while the merger works.
+// decode_sched_kernel: one CTA per SM, NC consumer warps and one merger warp.
+//   * consumer c takes tiles c, c + NC, c + 2 NC, ... of its CTA's range.  It
+//     issues the TMA loads of its own tiles (K and V, 16 rows x D, 128-byte
+//     swizzle, 2-D tensor maps) S tiles ahead into its own S-stage ring and runs
+//     attend_tile (mma.sync m16n8k16, online softmax, fp32 accumulate).  When its
+//     next tile lies in a later piece it hands its state for the piece to the
+//     merger, through one of NB shared-memory buffers, and switches to the next
+//     piece's query fragments, loaded one piece ahead.  Warps that issue their
+//     own copies stream like the stream kernel's; a separate issuing warp caps
+//     a CTA near 8 tiles per microsecond (the copies one warp issues are
+//     accepted one after another, ~60 ns each);
+//   * the merger combines the consumer states of each piece in consumer order.
+//     A whole unit is normalised and written to `out`.  A cut piece is stored
+//     as a partial state (O, m, l per head row) and counted in on the unit's
+//     arrival counter; the last of the unit's pieces to arrive merges all of
+//     them in CTA order and writes the unit.
+// Which consumer and which CTA take which tile is fixed by the schedule, so the
+// result does not depend on timing.
 //
 // Every wait is bounded (DecodeArgs::wait_limit); a wait that runs out sets
-// MVB_DEV_TIMEOUT and a CTA-wide abort flag that every other wait polls, the
-// issuer then waits (bounded) for its loads in flight, and every role leaves.
-// The work counters are then left dirty: the schedule must be rebuilt (the
-// schedule kernel resets every counter it hands to the decode).
+// MVB_DEV_TIMEOUT and a CTA-wide abort flag that every other wait polls; each
+// consumer then waits (bounded) for its own loads in flight and every warp
+// leaves.  An arrival counter may then be left dirty: the schedule must be
+// rebuilt (the schedule kernel zeroes every counter).
 #include "mma_tile.cuh"
 
 namespace mvb {
 
-constexpr int kSchedMaxPiece = 32;  // tiles per chunk at most: one block id per fetcher lane
-constexpr int kSchedMinPiece = 4;
-constexpr int kSchedSlots = 4;      // chunk slots between the fetcher and the other roles
-constexpr int kSchedIssueLanes = 8;  // tiles the issuer warp issues at once, one per lane
-constexpr int kSchedBuildThreads = 1024;
+constexpr int kSchedBuildThreads = 512;
+constexpr int kSchedMaxSeqs = 16384;  // sequences the schedule kernel's prefix arrays hold
+constexpr int kSchedMaxCtas = kSchedBuildThreads;
+constexpr int kSchedRecRows = 44;     // first rows a CTA record carries (NC * S of the decode)
+constexpr int kSchedSortMax = 256;    // a CTA's whole pieces are sorted longest first up to this many pieces
 
-// Workspace header (256 bytes at the start of the workspace).
+// Workspace header (256 bytes).
 struct SchedHeader {
-  int n_chunks;
-  int piece;        // tiles per chunk at most, as chosen
-  int next;         // chunk hand-out counter (zero at rest)
-  int done;         // CTAs whose fetcher saw the end of the list (zero at rest)
-  int total_tiles;  // tiles of all units
-  int pad[59];
+  int total_tiles;  // tiles of all units of good sequences
+  int ctas;         // CTAs with work: min(grid, total_tiles)
+  int n_bad;        // sequences left out (kv_len < 1, block table too short)
+  int bad_bits;     // their error bits, OR-ed
+  int pad[60];
 };
 static_assert(sizeof(SchedHeader) == 256, "header is 256 bytes");
 
-// Chunk descriptor: two int4
-//   {sequence, unit of the sequence (kvh * head_groups + hg), first tile, tiles}
-//   {first chunk of the unit, pieces of the unit, kv_len, bad sequence flag}
-// A bad sequence (kv_len < 1 or a block table too short) has one chunk of zero
-// tiles per unit: its output rows are written as zeros.
+// Piece descriptor: two int4
+//   {sequence, unit of the sequence (kvh * head_groups + hg), first tile of the
+//    piece in the unit, tiles}
+//   {position of its first tile in the CTA's processing order, kv_len,
+//    first CTA of a cut unit (-1: the piece is the whole unit),
+//    (CTAs the cut unit spans << 1) | (1 when it starts at that CTA's range start)}
+// Per-CTA record (256 bytes): {first piece, pieces, first tile position of the
+// range, tiles}, the first two pieces, and the pool row of tile c + NC * i of
+// the range at rows0[c * S + i] (-1 past the range).
+struct SchedRec {
+  int4 h;
+  int4 p[2][2];
+  int rows0[kSchedRecRows];
+};
+static_assert(sizeof(SchedRec) == 256, "record is 256 bytes");
+
 struct SchedArgs {
-  SchedHeader* hdr;
-  const int4* desc;  // [max_chunks][2]
-  int* ucnt;         // [max_chunks] arrival counters, indexed by a unit's first chunk
-  float* part;       // [max_chunks][mg][D + 4] partial O (D), m, l
-  int max_chunks;
-  int mg;            // partial rows per chunk: min(16, G)
+  const SchedHeader* hdr;
+  const SchedRec* rec;  // [grid]
+  const int4* desc;     // [max_pieces][2]
+  const int* rows;      // [max_tiles] pool rows by tile position
+  const int* bad;       // [num_seqs] sequences left out, in order
+  int* ucnt;            // [grid] arrival counters of cut units, by first CTA
+  float* part;          // [2 * grid][mg][D + 4] partial states: O (D), m, l
+  int mg;               // query heads per unit: min(16, G)
+  int nb;               // merge buffers (1 or 2)
 };
 
 // ---------------------------------------------------------------------------
@@ -96,95 +103,245 @@ __device__ __forceinline__ int sched_seq_error(int ctx, int block_size, int max_
   return 0;
 }
 
-// One CTA.  wait_at_end: the previous kernel in the stream may still be running
-// and writes none of this kernel's inputs (the KV write); the kernel computes
-// first and waits for it only before exiting, so that a dependent of this
-// kernel that waits for it also waits for that previous kernel.
+// Last i in [0, n) with v[i] <= x (v non-decreasing, v[0] <= x).
+__device__ __forceinline__ int sched_last_le(const int* v, int n, int x) {
+  int lo = 0, hi = n;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (v[mid] <= x)
+      lo = mid;
+    else
+      hi = mid;
+  }
+  return lo;
+}
+
+// One CTA per CTA of the decode grid; each scans kv_len itself (a few KB from
+// L2) and writes its own record, pieces and rows.  wait_at_end: the previous
+// kernel in the stream may still be running and writes none of this kernel's
+// inputs (the KV write); the kernel computes first and waits for it only
+// before exiting, so that a dependent of this kernel that waits for it also
+// waits for that previous kernel.
 __global__ void __launch_bounds__(kSchedBuildThreads)
-decode_schedule_kernel(const int* __restrict__ kv_len, int num_seqs, int units_per_seq, int block_size,
-                       int max_blocks, int ctas, SchedHeader* hdr, int4* desc, int* ucnt, int max_chunks,
-                       int* err, int wait_at_end) {
-  __shared__ int s_hist[kSchedMaxPiece + 1];
-  __shared__ int s_base[kSchedMaxPiece + 1];
-  __shared__ long long s_red[kSchedBuildThreads / 32];
-  __shared__ int s_piece, s_overflow;
+decode_schedule_kernel(const int* __restrict__ kv_len, const int64_t* __restrict__ bt, int64_t bt_s0,
+                       int num_seqs, int num_kv_heads, int head_groups, int block_size, int max_blocks,
+                       int num_blocks, int nc, int stages, SchedHeader* hdr, SchedRec* rec, int4* desc,
+                       int* rows, int* bad, int* ucnt, int* err, int wait_at_end) {
+  extern __shared__ int sched_smem[];
+  int* pseq = sched_smem;                 // [num_seqs + 1] first tile position of the sequence's units
+  int* gseq = sched_smem + num_seqs + 1;  // [num_seqs + 1] good sequences before it
+  constexpr int NT = kSchedBuildThreads, NWP = NT / 32;
+  __shared__ int s_red[3][NWP];
+  __shared__ int s_cnt[NWP];
+  __shared__ int s_len[kSchedSortMax];
   if (!wait_at_end) grid_dependency_wait();
   grid_launch_dependents();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid <= kSchedMaxPiece) s_hist[tid] = 0;
+  const int ups = num_kv_heads * head_groups;
+  const int c = blockIdx.x;
 
-  // total tiles of all units
-  long long tiles = 0;
-  for (int s = tid; s < num_seqs; s += blockDim.x) {
-    const int ctx = __ldg(kv_len + s);
-    if (!sched_seq_error(ctx, block_size, max_blocks)) tiles += (ctx + kTile - 1) / kTile;
+  // ---- tiles of each sequence (all its units), exclusive prefixes ----
+  const int per = (num_seqs + NT - 1) / NT;
+  const int i0 = min(num_seqs, tid * per), i1 = min(num_seqs, i0 + per);
+  int my_t = 0, my_g = 0, my_bits = 0;
+  for (int i = i0; i < i1; ++i) {
+    const int ctx = __ldg(kv_len + i);
+    const int e = sched_seq_error(ctx, block_size, max_blocks);
+    const int t = e ? 0 : (ctx + kTile - 1) / kTile * ups;
+    pseq[i] = t;
+    gseq[i] = e ? 0 : 1;
+    my_t += t;
+    my_g += e ? 0 : 1;
+    my_bits |= e;
+  }
+  int it = my_t, ig = my_g, ob = my_bits;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int vt = __shfl_up_sync(0xffffffffu, it, o), vg = __shfl_up_sync(0xffffffffu, ig, o);
+    if (lane >= o) {
+      it += vt;
+      ig += vg;
+    }
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) tiles += __shfl_xor_sync(0xffffffffu, tiles, o);
-  if (lane == 0) s_red[warp] = tiles;
-  __syncthreads();
-  if (tid == 0) {
-    long long t = 0;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += s_red[w];
-    t *= units_per_seq;
-    long long pc = (t + 2LL * ctas - 1) / (2LL * ctas);
-    if (pc < kSchedMinPiece) pc = kSchedMinPiece;
-    if (pc > kSchedMaxPiece) pc = kSchedMaxPiece;
-    s_piece = (int)pc;
-    hdr->piece = (int)pc;
-    hdr->total_tiles = (int)(t < 0x7fffffffLL ? t : 0x7fffffffLL);
+  for (int o = 16; o > 0; o >>= 1) ob |= __shfl_xor_sync(0xffffffffu, ob, o);
+  if (lane == 31) {
+    s_red[0][warp] = it;
+    s_red[1][warp] = ig;
   }
+  if (lane == 0) s_red[2][warp] = ob;
   __syncthreads();
-  const int piece = s_piece;
-
-  // histogram of chunks by piece size (bucket 0: bad sequences)
-  for (int s = tid; s < num_seqs; s += blockDim.x) {
-    const int ctx = __ldg(kv_len + s);
-    const bool bad = sched_seq_error(ctx, block_size, max_blocks) != 0;
-    const int nt = bad ? 0 : (ctx + kTile - 1) / kTile;
-    const int p = bad ? 1 : (nt + piece - 1) / piece;
-    const int ps = bad ? 0 : (nt + p - 1) / p;
-    atomicAdd(&s_hist[ps], p * units_per_seq);
-  }
-  __syncthreads();
-  if (tid == 0) {
-    int run = 0;
-    for (int b = kSchedMaxPiece; b >= 0; --b) {
-      s_base[b] = run;
-      run += s_hist[b];
+  int base_t = 0, base_g = 0, T = 0, NG = 0, bits = 0;
+  for (int w = 0; w < NWP; ++w) {
+    if (w < warp) {
+      base_t += s_red[0][w];
+      base_g += s_red[1][w];
     }
-    s_overflow = run > max_chunks;
-    if (s_overflow) {  // cannot happen with the host's bound; refuse rather than overrun
-      atomicOr(err, MVB_DEV_SCHEDULE);
-      run = 0;
-    }
-    hdr->n_chunks = run;
-    hdr->next = 0;
-    hdr->done = 0;
+    T += s_red[0][w];
+    NG += s_red[1][w];
+    bits |= s_red[2][w];
+  }
+  int run_t = base_t + it - my_t, run_g = base_g + ig - my_g;
+  for (int i = i0; i < i1; ++i) {
+    const int t = pseq[i], g = gseq[i];
+    pseq[i] = run_t;
+    gseq[i] = run_g;
+    run_t += t;
+    run_g += g;
+  }
+  if (tid == 0) {
+    pseq[num_seqs] = T;
+    gseq[num_seqs] = NG;
   }
   __syncthreads();
-  const bool overflow = s_overflow != 0;
 
-  // descriptors; within a bucket the order is arbitrary (it only affects which
-  // CTA takes a chunk, never the arithmetic of any output)
-  for (int s = tid; s < num_seqs; s += blockDim.x) {
-    const int ctx = __ldg(kv_len + s);
-    const int bad = sched_seq_error(ctx, block_size, max_blocks);
-    if (bad) atomicOr(err, bad);
-    if (overflow) continue;
-    const int nt = bad ? 0 : (ctx + kTile - 1) / kTile;
-    const int p = bad ? 1 : (nt + piece - 1) / piece;
-    const int ps = bad ? 0 : (nt + p - 1) / p;
-    const int c0 = atomicAdd(&s_base[ps], p * units_per_seq);
-    for (int k = 0; k < units_per_seq; ++k) {
-      const int first = c0 + k * p;
-      ucnt[first] = 0;
-      for (int i = 0; i < p; ++i) {
-        const int b0 = (int)((int64_t)i * nt / p), b1 = (int)((int64_t)(i + 1) * nt / p);
-        desc[2 * (first + i)] = make_int4(s, k, b0, b1 - b0);
-        desc[2 * (first + i) + 1] = make_int4(first, p, ctx, bad ? 1 : 0);
+  const int Ce = T < (int)gridDim.x ? T : (int)gridDim.x;
+  if (c == 0) {
+    for (int i = tid; i < num_seqs; i += NT)
+      if (gseq[i + 1] == gseq[i]) bad[i - gseq[i]] = i;
+    if (tid == 0) {
+      hdr->total_tiles = T;
+      hdr->ctas = Ce;
+      hdr->n_bad = num_seqs - NG;
+      hdr->bad_bits = bits;
+      if (bits) atomicOr(err, bits);
+    }
+  }
+  if (tid == 0) ucnt[c] = 0;
+  if (c >= Ce) {
+    if (tid == 0) rec[c].h = make_int4(0, 0, 0, 0);
+    if (wait_at_end) grid_dependency_wait();
+    return;
+  }
+
+  auto R = [&](int x) { return (int)((int64_t)x * T / Ce); };
+  // CTA whose range holds tile position x: the largest c with R(c) <= x
+  auto cta_of = [&](int x) { return (int)(((int64_t)(x + 1) * Ce + T - 1) / T) - 1; };
+  // the unit holding tile position x < T: sequence, unit of it, its tiles, its first position
+  auto locate = [&](int x, int& s, int& k, int& t, int& p) {
+    s = sched_last_le(pseq, num_seqs, x);  // pseq[s] <= x < pseq[s + 1]: s has tiles
+    t = (pseq[s + 1] - pseq[s]) / ups;
+    k = (x - pseq[s]) / t;
+    p = pseq[s] + k * t;
+  };
+  auto good_unit = [&](int s, int k) { return gseq[s] * ups + k; };
+
+  // pieces of the CTAs before this one (c < Ce <= NT: one range per thread)
+  int cnt = 0;
+  if (tid < c) {
+    int s0, k0, t0, p0, s1, k1, t1, p1;
+    locate(R(tid), s0, k0, t0, p0);
+    locate(R(tid + 1) - 1, s1, k1, t1, p1);
+    cnt = good_unit(s1, k1) - good_unit(s0, k0) + 1;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+  if (lane == 0) s_cnt[warp] = cnt;
+  __syncthreads();
+  int pbase = 0;
+  for (int w = 0; w < NWP; ++w) pbase += s_cnt[w];
+
+  const int r0 = R(c), r1 = R(c + 1), n = r1 - r0;
+  int sa, ka, ta, pa, sb, kb, tb, pb;
+  locate(r0, sa, ka, ta, pa);
+  locate(r1 - 1, sb, kb, tb, pb);
+  const int gua = good_unit(sa, ka);
+  const int np = good_unit(sb, kb) - gua + 1;
+  // Processing order: the piece cut by the range's end first (when there are
+  // two pieces or more it starts inside the range), the piece cut by its start
+  // second, then the whole units longest first (ties in unit order; in unit
+  // order when there are more than kSchedSortMax pieces).
+  const bool cut_s = pa < r0, cut_e = pb + tb > r1;
+  const int len0 = min(pa + ta, r1) - r0, len_l = r1 - max(pb, r0);
+  const int n_head = np == 1 ? 1 : (cut_e ? 1 : 0) + (cut_s ? 1 : 0);
+  const int head_len = np == 1 ? len0 : (cut_e ? len_l : 0) + (cut_s ? len0 : 0);
+  const bool sorted = np <= kSchedSortMax;
+  auto unit_piece = [&](int i, int& s, int& k, int& P, int& ps, int& pe) {
+    const int g = gua + i, gs = g / ups;
+    s = sched_last_le(gseq, num_seqs, gs);  // the good sequence number gs
+    k = g - gs * ups;
+    const int t = (pseq[s + 1] - pseq[s]) / ups;
+    P = pseq[s] + k * t;
+    ps = max(P, r0);
+    pe = min(P + t, r1);
+  };
+  if (sorted) {
+    for (int i = tid; i < np; i += NT) {
+      int s, k, P, ps, pe;
+      unit_piece(i, s, k, P, ps, pe);
+      s_len[i] = pe - ps;
+    }
+    __syncthreads();
+  }
+  auto is_head = [&](int i) { return np == 1 || (i == np - 1 && cut_e) || (i == 0 && cut_s); };
+  if (tid == 0) rec[c].h = make_int4(pbase, np, r0, n);
+  for (int i = tid; i < np; i += NT) {
+    int s, k, P, ps, pe;
+    unit_piece(i, s, k, P, ps, pe);
+    const int len = pe - ps;
+    int pos, v0;
+    if (np == 1 || (i == np - 1 && cut_e)) {
+      pos = 0;
+      v0 = 0;
+    } else if (i == 0 && cut_s) {
+      pos = cut_e ? 1 : 0;
+      v0 = cut_e ? len_l : 0;
+    } else if (sorted) {
+      int rank = 0, before = 0;
+      for (int j = 0; j < np; ++j) {
+        if (j == i || is_head(j)) continue;
+        const int lj = s_len[j];
+        if (lj > len || (lj == len && j < i)) {
+          ++rank;
+          before += lj;
+        }
       }
+      pos = n_head + rank;
+      v0 = head_len + before;
+    } else {
+      pos = i - (cut_s ? 1 : 0) + n_head;
+      v0 = head_len + ps - (r0 + (cut_s ? len0 : 0));
     }
+    int c0 = -1, w = 0;
+    const int t = (pseq[s + 1] - pseq[s]) / ups;
+    if (P < r0 || P + t > r1) {
+      c0 = cta_of(P);
+      const int c1 = cta_of(P + t - 1);
+      w = ((c1 - c0 + 1) << 1) | (P == R(c0) ? 1 : 0);
+    }
+    const int4 d0 = make_int4(s, k, ps - P, len);
+    const int4 d1 = make_int4(v0, __ldg(kv_len + s), c0, w);
+    desc[2 * (pbase + pos)] = d0;
+    desc[2 * (pbase + pos) + 1] = d1;
+    if (pos < 2) {
+      rec[c].p[pos][0] = d0;
+      rec[c].p[pos][1] = d1;
+    }
+  }
+  __syncthreads();  // this CTA's descriptors are visible to all its threads
+
+  // pool rows, one warp per piece
+  for (int pos = warp; pos < np; pos += NWP) {
+    const int4 d0 = __ldcg(desc + 2 * (pbase + pos)), d1 = __ldcg(desc + 2 * (pbase + pos) + 1);
+    const int s = d0.x, kvh = d0.y / head_groups, t0 = d0.z, len = d0.w, v0 = d1.x;
+    for (int i = lane; i < len; i += 32) {
+      const int tok = (t0 + i) * kTile;
+      const int bi = tok / block_size;
+      const int64_t b = __ldg(bt + (int64_t)s * bt_s0 + bi);
+      int row = -1;
+      if (b >= 0 && b < num_blocks)
+        row = ((int)b * num_kv_heads + kvh) * block_size + (tok - bi * block_size);
+      else
+        atomicOr(err, MVB_DEV_BLOCK_ID);
+      const int j = v0 + i;
+      rows[r0 + j] = row;
+      const int ii = j / nc;
+      if (ii < stages) rec[c].rows0[(j - ii * nc) * stages + ii] = row;
+    }
+  }
+  for (int e = tid; e < nc * stages; e += NT) {
+    const int cc = e / stages, ii = e - cc * stages;
+    if (cc + nc * ii >= n) rec[c].rows0[e] = -1;
   }
   if (wait_at_end) grid_dependency_wait();
 }
@@ -192,81 +349,49 @@ decode_schedule_kernel(const int* __restrict__ kv_len, int num_seqs, int units_p
 // ---------------------------------------------------------------------------
 // decode
 // ---------------------------------------------------------------------------
-// Per head dim: ring stages, consumer warps, merge buffers between the
-// consumers and the mergers, issuer warps (the bulk copies one warp issues are
-// accepted one after another, ~60 ns each, so a single warp caps a CTA near 8
-// tiles per microsecond) and merger warps (under full streaming load each L2
-// round trip of a merge — partial stores and fence, the arrival atomic, the
-// other pieces' partials — takes 1-2 us, so one merger warp falls behind the
-// ~7 split pieces a CTA streams at config 2).  The ring holds 128 KB in flight
-// per SM; shared memory (ring + slots + NB buffers of NC states) sets NB.
-// (Overridable at build time for tuning sweeps.)
-#ifndef MVB_SCHED64_STAGES
-#define MVB_SCHED64_STAGES 32
-#endif
+// Per head dim: consumer warps and ring stages per consumer.  The CTA keeps
+// NC * S tiles in flight (176 KB at D 64, 192 KB at D 128); the decode is bound
+// by the bytes in flight (40 stages of 4 KB stream ~12 % slower than 44).  The
+// registers a thread may use follow from the warps one SM sub-partition holds:
+// 12 warps (3 per sub-partition) get 168, enough at D 64; D 128 needs ~250, so
+// 6 consumers and the merger (2 per sub-partition).  Overridable at build time
+// for tuning sweeps.
 #ifndef MVB_SCHED64_NC
-#define MVB_SCHED64_NC 8
+#define MVB_SCHED64_NC 11
 #endif
-#ifndef MVB_SCHED64_NB
-#define MVB_SCHED64_NB 2
-#endif
-#ifndef MVB_SCHED64_NM
-#define MVB_SCHED64_NM 2
-#endif
-#ifndef MVB_SCHED64_NI
-#define MVB_SCHED64_NI 2
-#endif
-#ifndef MVB_SCHED128_STAGES
-#define MVB_SCHED128_STAGES 16
+#ifndef MVB_SCHED64_STAGES
+#define MVB_SCHED64_STAGES 4
 #endif
 #ifndef MVB_SCHED128_NC
-#define MVB_SCHED128_NC 4
+#define MVB_SCHED128_NC 6
 #endif
-#ifndef MVB_SCHED128_NB
-#define MVB_SCHED128_NB 2
-#endif
-#ifndef MVB_SCHED128_NM
-#define MVB_SCHED128_NM 2
-#endif
-#ifndef MVB_SCHED128_NI
-#define MVB_SCHED128_NI 2
+#ifndef MVB_SCHED128_STAGES
+#define MVB_SCHED128_STAGES 4
 #endif
 template <int D> struct SchedConfig;
 template <> struct SchedConfig<64> {
-  static constexpr int STAGES = MVB_SCHED64_STAGES, NC = MVB_SCHED64_NC, NB = MVB_SCHED64_NB, NI = MVB_SCHED64_NI,
-                       NM = MVB_SCHED64_NM;
+  static constexpr int NC = MVB_SCHED64_NC, S = MVB_SCHED64_STAGES;
 };
 template <> struct SchedConfig<128> {
-  static constexpr int STAGES = MVB_SCHED128_STAGES, NC = MVB_SCHED128_NC, NB = MVB_SCHED128_NB,
-                       NI = MVB_SCHED128_NI, NM = MVB_SCHED128_NM;
+  static constexpr int NC = MVB_SCHED128_NC, S = MVB_SCHED128_STAGES;
 };
 
+// Shared memory: rings [NC][S] stages, NB merge buffers [NC][mg][D + 4] floats,
+// barriers (NC * S tile-full, NB merge-full, NB merge-empty), per-stage bad-row
+// flags, the abort flag (16 bytes), the merger's descriptor ring (4 x 32 bytes).
 template <int D> struct SchedSmem {
-  using Geo = MmaGeom<D>;
-  static constexpr int STAGES = SchedConfig<D>::STAGES, NC = SchedConfig<D>::NC, NB = SchedConfig<D>::NB;
-  static constexpr int NI = SchedConfig<D>::NI, NM = SchedConfig<D>::NM;
-  static_assert(STAGES % NC == 0, "each stage belongs to one consumer");
-  static_assert(STAGES % (NI * kSchedIssueLanes) == 0, "each stage belongs to one issuer");
-  static_assert(NB % NM == 0, "each merge buffer belongs to one merger");
-  static constexpr int THREADS = (1 + NI + NC + NM) * 32;  // fetcher, issuers, consumers, mergers
-  static constexpr int QP = D + 8;  // query row pitch (elements): conflict-free fragment loads
-  static constexpr int SLOT_BYTES = 32 + 4 * kSchedMaxPiece + 16 * QP * 2;
-  // merge buffer: header (2 x int4), (m, l) [consumers][16], O [consumers][16][D]
-  static constexpr int MB_ML = 32;
-  static constexpr int MB_O = MB_ML + NC * 16 * 8;
-  static constexpr int MB_BYTES = MB_O + NC * 16 * D * 4;
-  static constexpr int RING = 0;
-  static constexpr int SLOTS = RING + STAGES * Geo::STAGE_BYTES;
-  static constexpr int MERGE = SLOTS + kSchedSlots * SLOT_BYTES;
-  static constexpr int BARS = MERGE + NB * MB_BYTES;
-  static constexpr int NBARS = 2 * STAGES + 2 * kSchedSlots + 2 * NB;
-  static constexpr int STAGE_BAD = BARS + NBARS * 8;
-  static constexpr int MISC = STAGE_BAD + STAGES * 4;
-  static constexpr int BYTES = MISC + 16;
-  static_assert(SLOTS % 16 == 0 && MERGE % 16 == 0 && MB_BYTES % 16 == 0 && BARS % 8 == 0, "alignment");
+  static constexpr int NC = SchedConfig<D>::NC, S = SchedConfig<D>::S;
+  static_assert(NC * S <= kSchedRecRows, "the record carries every consumer's first rows");
+  static_assert(NC * S % 4 == 0, "barriers and flags keep the descriptor ring 16-byte aligned");
+  static constexpr int THREADS = (NC + 1) * 32;
+  static constexpr int RING = NC * S * MmaGeom<D>::STAGE_BYTES;
+  static __host__ __device__ constexpr int merge_bytes(int mg) { return NC * mg * (D + 4) * 4; }
+  static __host__ __device__ constexpr int bytes(int mg, int nb) {
+    return RING + nb * merge_bytes(mg) + (NC * S + 2 * nb) * 8 + NC * S * 4 + 16 + 128;
+  }
 };
 
-// Bounded wait that also gives up when another role has aborted the CTA.
+// Bounded wait that also gives up when another warp has aborted the CTA.
 __device__ __forceinline__ bool sched_wait(uint32_t bar, uint32_t parity, int limit, volatile int* abort_flag,
                                            int* err) {
   for (int i = 0; i < limit; ++i) {
@@ -287,12 +412,81 @@ __device__ __forceinline__ bool sched_wait_warp(uint32_t bar, uint32_t parity, i
 
 __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 
+// 16-byte global -> shared copy through L2 (cp.async), in the thread's current group.
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_async_wait_group() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // One arrival for a whole warp: __syncwarp orders every lane's shared-memory
-// accesses before lane 0's arrive (release), as one arrival per lane would,
-// at a thirty-second of the barrier traffic.
+// accesses before lane 0's arrive (release).
 __device__ __forceinline__ void warp_arrive(uint32_t bar, int lane) {
   __syncwarp();
   if (lane == 0) mbar_arrive(bar);
+}
+
+// (M, L, O[cq .. cq + D/4)) of head row r from the consumer states of one
+// merge buffer ([NC][mg][D + 4] floats: O, m, l): consumer cc holds tiles of the
+// piece when some i < len has (first + i) % NC == cc; one without tiles, or
+// whose tiles all had bad block ids (m = -inf, O = 0), weighs 0.  Branch-free,
+// so that every consumer's loads are in flight together.  `row_ok`: r is a
+// head row of the unit (else the result is zeros and nothing is read).
+template <int D, int NC>
+__device__ __forceinline__ void merge_row(const float* mb, int mg, int r, int cq, int first, int len, bool row_ok,
+                                          float& M, float& L, float (&O)[D / 4]) {
+  constexpr int CQ = D / 4, PR = D + 4;
+  M = -INFINITY;
+  L = 0.f;
+#pragma unroll
+  for (int i = 0; i < CQ; ++i) O[i] = 0.f;
+  auto holds = [&](int cc) {
+    int x = cc - first;
+    x += x < 0 ? NC : 0;
+    return row_ok && (len >= NC || x < len);
+  };
+#pragma unroll
+  for (int cc = 0; cc < NC; ++cc)
+    if (holds(cc)) M = fmaxf(M, mb[(cc * mg + r) * PR + D]);
+  const float mref = M == -INFINITY ? 0.f : M;  // no readable token: zeros
+#pragma unroll
+  for (int cc = 0; cc < NC; ++cc) {
+    const bool in = holds(cc);
+    const float2 ml = in ? *reinterpret_cast<const float2*>(mb + (cc * mg + r) * PR + D) : make_float2(-INFINITY, 0.f);
+    const float w = fast_exp2(ml.x - mref);  // 0 for m = -inf
+    L = fmaf(ml.y, w, L);
+    const float4* src = reinterpret_cast<const float4*>(mb + (cc * mg + r) * PR + cq);
+#pragma unroll
+    for (int i = 0; i < CQ / 4; ++i) {
+      const float4 v = in ? src[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+      O[4 * i] = fmaf(v.x, w, O[4 * i]);
+      O[4 * i + 1] = fmaf(v.y, w, O[4 * i + 1]);
+      O[4 * i + 2] = fmaf(v.z, w, O[4 * i + 2]);
+      O[4 * i + 3] = fmaf(v.w, w, O[4 * i + 3]);
+    }
+  }
+}
+
+// n = D / 4 normalised values of one output row, x[i] * inv, to p: two 16-byte
+// stores when p is 16-byte aligned, else element by element.
+template <typename T, int N>
+__device__ __forceinline__ void store_row(T* p, const float (&x)[N], float inv) {
+  if ((reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+#pragma unroll
+    for (int v = 0; v < N / 8; ++v) {
+      uint4 w;
+      w.x = Mma16816<T>::pack(x[8 * v] * inv, x[8 * v + 1] * inv);
+      w.y = Mma16816<T>::pack(x[8 * v + 2] * inv, x[8 * v + 3] * inv);
+      w.z = Mma16816<T>::pack(x[8 * v + 4] * inv, x[8 * v + 5] * inv);
+      w.w = Mma16816<T>::pack(x[8 * v + 6] * inv, x[8 * v + 7] * inv);
+      reinterpret_cast<uint4*>(p)[v] = w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) p[i] = from_f32<T>(x[i] * inv);
+  }
 }
 
 template <typename T, int D>
@@ -301,442 +495,397 @@ decode_sched_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_consta
                     const DecodeArgs a, const SchedArgs sa) {
   using Geo = MmaGeom<D>;
   using L = SchedSmem<D>;
-  constexpr int KC = D / 16, NO = D / 8, QP = L::QP, PR = D + 4, NB = L::NB, NC = L::NC, STAGES = L::STAGES;
-  constexpr int NI = L::NI, NM = L::NM;
+  constexpr int NC = L::NC, S = L::S, KC = D / 16, NO = D / 8, PR = D + 4;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem =
       reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* ring = smem + L::RING;
-  uint8_t* slots = smem + L::SLOTS;
-  uint8_t* merge = smem + L::MERGE;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BARS);
-  uint64_t* full = bars;                   // [STAGES] tile landed
-  uint64_t* empty = bars + STAGES;         // [STAGES] tile consumed
-  uint64_t* cfull = bars + 2 * STAGES;     // [slots] chunk published
-  uint64_t* cempty = cfull + kSchedSlots;  // [slots] chunk read by the issuer and the consumers
-  uint64_t* mfull = cempty + kSchedSlots;  // [NB] consumer states written
-  uint64_t* mempty = mfull + NB;           // [NB] states read by the merger
-  volatile int* stage_bad = reinterpret_cast<volatile int*>(smem + L::STAGE_BAD);
-  volatile int* misc = reinterpret_cast<volatile int*>(smem + L::MISC);  // [0] abort flag
+  const int NB = sa.nb, mg = sa.mg;
+  uint8_t* ring = smem;
+  float* merge = reinterpret_cast<float*>(smem + L::RING);  // [NB][NC][mg][PR]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::RING + NB * L::merge_bytes(mg));  // [NC][S]
+  uint64_t* mfull = full + NC * S;  // [NB] consumer states written
+  uint64_t* mempty = mfull + NB;    // [NB] states read by the merger
+  volatile int* stage_bad = reinterpret_cast<volatile int*>(mempty + NB);  // [NC][S]
+  volatile int* abort_flag = stage_bad + NC * S;
+  int4* dring = reinterpret_cast<int4*>(const_cast<int*>(abort_flag) + 4);  // [4][2] merger's descriptor ring
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(smem_u32(full + s), 1);
-      mbar_init(smem_u32(empty + s), 1);  // the consuming warp
-    }
-    for (int c = 0; c < kSchedSlots; ++c) {
-      mbar_init(smem_u32(cfull + c), 1);        // the fetcher warp
-      mbar_init(smem_u32(cempty + c), NI + NC);  // the issuer and consumer warps
-    }
+    for (int i = 0; i < NC * S; ++i) mbar_init(smem_u32(full + i), 1);
     for (int b = 0; b < NB; ++b) {
       mbar_init(smem_u32(mfull + b), NC);  // the consumer warps
       mbar_init(smem_u32(mempty + b), 1);  // the merger warp
     }
-    misc[0] = 0;
+    *abort_flag = 0;
     fence_mbar_init();
   }
   __syncthreads();  // the only CTA-wide barrier
   grid_launch_dependents();
-  volatile int* abort_flag = misc;
   const int limit = a.wait_limit;
-
-  auto slot_desc = [&](int slot) { return reinterpret_cast<int4*>(slots + slot * L::SLOT_BYTES); };
-  auto slot_rows = [&](int slot) { return reinterpret_cast<int*>(slots + slot * L::SLOT_BYTES + 32); };
-  auto slot_q = [&](int slot) {
-    return reinterpret_cast<T*>(slots + slot * L::SLOT_BYTES + 32 + 4 * kSchedMaxPiece);
-  };
-  auto mb_hdr = [&](int b) { return reinterpret_cast<int4*>(merge + b * L::MB_BYTES); };
-  auto mb_ml = [&](int b) { return reinterpret_cast<float2*>(merge + b * L::MB_BYTES + L::MB_ML); };
-  auto mb_o = [&](int b) { return reinterpret_cast<float*>(merge + b * L::MB_BYTES + L::MB_O); };
-
-  if (warp == 0) {
-    // ================================= fetcher =================================
-    if (!a.early_inputs) grid_dependency_wait();
-    bool waited = a.early_inputs == 0;
-    const int4 stop = make_int4(0, 0, 0, -1);
-    int idx = blockIdx.x;  // the first chunk by index; its descriptor is read before the chunk
-                           // count (blockIdx.x < gridDim.x <= max_chunks: in bounds either way)
-    int4 d0 = __ldcg(sa.desc + 2 * idx), d1 = __ldcg(sa.desc + 2 * idx + 1);
-    const int n_chunks = __ldcg(&sa.hdr->n_chunks);
-    bool have = idx < n_chunks;
-    if (!have) {
-      d0 = stop;
-      d1 = make_int4(0, 0, 0, 0);
-    }
-    int idx_n = -1;  // the next chunk (from the second iteration on)
-    bool aborted = false;
-    for (int k = 0;; ++k) {
-      const int slot = k % kSchedSlots;
-      const int seq = d0.x, uk = d0.y, begin = d0.z, n = d0.w;
-      const int kvh = uk / a.head_groups, hg = uk - kvh * a.head_groups;
-      const int h0 = kvh * a.G + hg * 16, nh = min(16, a.G - hg * 16);
-      // block id -> pool row of tile `lane` of the chunk
-      int row = -1;
-      if (lane < n) {
-        const int tok = (begin + lane) * kTile;
-        const int bi = tok / a.block_size;
-        const int64_t b = __ldg(a.bt + (int64_t)seq * a.bt_s0 + bi);
-        if (b >= 0 && b < a.num_blocks)
-          row = ((int)b * a.num_kv_heads + kvh) * a.block_size + (tok - bi * a.block_size);
-        else
-          atomicOr(a.err, MVB_DEV_BLOCK_ID);
-      }
-      // query rows of the head group, 16 x D, zero past nh (4-byte words)
-      constexpr int QW = 16 * D / 2 / 32;  // words per lane
-      uint32_t qw[QW];
-      const T* qbase = static_cast<const T*>(a.q) + (int64_t)seq * a.q_s0 + (int64_t)h0 * a.q_s1;
-#pragma unroll
-      for (int v = 0; v < QW; ++v) {
-        const int e = lane + 32 * v, r = e / (D / 2), c = e - r * (D / 2);
-        qw[v] = (n > 0 && r < nh) ? ld_u32(qbase + (int64_t)r * a.q_s1 + 2 * c) : 0u;
-      }
-      if (!waited) {  // the hand-out counter is reset by the previous decode
-        grid_dependency_wait();
-        waited = true;
-      }
-      // In flight during the publication below: on the first chunk the index of
-      // the second; afterwards the next descriptor and the index after it.
-      bool have_n = false;
-      int4 n0 = stop, n1 = make_int4(0, 0, 0, 0);
-      int t_nn = n_chunks;
-      if (k == 0) {
-        if (have && lane == 0) t_nn = (int)gridDim.x + atomicAdd(&sa.hdr->next, 1);
-      } else {
-        have_n = idx_n < n_chunks;
-        if (have_n) {
-          n0 = __ldcg(sa.desc + 2 * idx_n);
-          n1 = __ldcg(sa.desc + 2 * idx_n + 1);
-          if (lane == 0) t_nn = (int)gridDim.x + atomicAdd(&sa.hdr->next, 1);
-        }
-      }
-      if (k >= kSchedSlots &&
-          !sched_wait_warp(smem_u32(cempty + slot), (uint32_t)((k / kSchedSlots - 1) & 1), limit, abort_flag,
-                           a.err)) {
-        aborted = true;
-        break;
-      }
-      if (lane == 0) {
-        slot_desc(slot)[0] = d0;
-        slot_desc(slot)[1] = make_int4(d1.x, d1.y, d1.z, idx);  // .w: the chunk's own index
-      }
-      slot_rows(slot)[lane] = row;
-      uint32_t* qs = reinterpret_cast<uint32_t*>(slot_q(slot));
-#pragma unroll
-      for (int v = 0; v < QW; ++v) {
-        const int e = lane + 32 * v, r = e / (D / 2), c = e - r * (D / 2);
-        qs[r * (QP / 2) + c] = qw[v];
-      }
-      warp_arrive(smem_u32(cfull + slot), lane);
-      if (!have) break;  // the end marker is published
-      if (k == 0) {  // the second chunk's descriptor, and the third's index: the pipeline from here on
-        idx = __shfl_sync(0xffffffffu, t_nn, 0);
-        have = idx < n_chunks;
-        d0 = have ? __ldcg(sa.desc + 2 * idx) : stop;
-        d1 = have ? __ldcg(sa.desc + 2 * idx + 1) : make_int4(0, 0, 0, 0);
-        int t = n_chunks;
-        if (have && lane == 0) t = (int)gridDim.x + atomicAdd(&sa.hdr->next, 1);
-        idx_n = __shfl_sync(0xffffffffu, t, 0);
-      } else {
-        idx = idx_n;
-        have = have_n;
-        d0 = n0;
-        d1 = n1;
-        idx_n = __shfl_sync(0xffffffffu, t_nn, 0);
-      }
-    }
-    if (!aborted && lane == 0) {
-      // the last CTA to reach the end of the list resets the counters
-      const int prev = atomicAdd(&sa.hdr->done, 1);
-      if (prev == (int)gridDim.x - 1) {
-        atomicExch(&sa.hdr->next, 0);
-        atomicExch(&sa.hdr->done, 0);
-      }
-    }
-    return;
+  // Without early_inputs the schedule or any input may come from the previous
+  // kernel: wait for it first.  With it (the schedule is older than the
+  // previous kernel, the KV write, which writes only the cache) everything but
+  // the cache is read at once, and the first cache load waits.
+  if (!a.early_inputs) grid_dependency_wait();
+  const SchedRec* rc = sa.rec + blockIdx.x;
+  const int4 h = __ldcg(&rc->h);
+  // A consumer's first rows and the first two pieces share the header's round
+  // trip (requested before anything waits for the header).
+  int row0 = -1;
+  int4 p00 = make_int4(0, 0, 0, 0), p01 = p00, p10 = p00, p11 = p00;
+  if (warp < NC) {
+    if (lane < S) row0 = __ldcg(&rc->rows0[warp * S + lane]);
+    p00 = __ldcg(&rc->p[0][0]);
+    p01 = __ldcg(&rc->p[0][1]);
+    p10 = __ldcg(&rc->p[1][0]);
+    p11 = __ldcg(&rc->p[1][1]);
   }
+  const int pbase = h.x, np = h.y, r0 = h.z, n = h.w;
+  auto piece = [&](int p, int4& d0, int4& d1) {
+    if (p < 2) {
+      d0 = __ldcg(&rc->p[p][0]);
+      d1 = __ldcg(&rc->p[p][1]);
+    } else {
+      d0 = __ldcg(sa.desc + 2 * (pbase + p));
+      d1 = __ldcg(sa.desc + 2 * (pbase + p) + 1);
+    }
+  };
+  auto heads = [&](int uk, int& h0, int& nh) {
+    const int kvh = uk / a.head_groups, hg = uk - kvh * a.head_groups;
+    h0 = kvh * a.G + hg * 16;
+    nh = min(16, a.G - hg * 16);
+  };
 
-  if (warp <= NI) {
-    // ================================= issuers =================================
-    // The tile sequence in batches of kSchedIssueLanes: batch j / kSchedIssueLanes
-    // is issuer warp (j / kSchedIssueLanes) % NI's, one tile per lane.  Each lane
-    // waits for its stage's previous tile to be consumed, then arms the stage's
-    // barrier and issues the K and V loads.
-    const int w = warp - 1;
-    grid_dependency_wait();  // the cache is complete from here on
-    if (w == 0 && lane == 0) {
+  if (warp < NC) {
+    // ================================ consumers ================================
+    const int c = warp;
+    const int g0 = lane >> 2, qd = lane & 3;
+    const int nq = n > c ? (n - 1 - c) / NC + 1 : 0;  // this consumer's tiles: c + NC * q
+    if (nq == 0 && np == 0) return;
+    // pool rows: the first S from the record (row0), then batches of 32 (rb: rcur's batch)
+    auto load_rows = [&](int batch) {
+      const int q = batch * 32 + lane;
+      return q < nq ? __ldcg(sa.rows + r0 + c + NC * q) : -1;
+    };
+    int rb = 0;
+    int rcur = load_rows(0), rnext = load_rows(1);
+
+    // current piece (cd), next (nd) with its query fragments (qn), the one after (fd)
+    int4 cd0 = make_int4(0, 0, 0, 0), cd1 = cd0, nd0 = cd0, nd1 = cd0, fd0 = cd0, fd1 = cd0;
+    uint32_t qa[KC][4], qn[KC][4];
+    auto load_q = [&](const int4& d0, uint32_t(&dst)[KC][4]) {
+      int h0, nh;
+      heads(d0.y, h0, nh);
+      load_q_frags<T, D>(a, d0.x, h0, nh, dst);
+    };
+    if (np > 0) {
+      cd0 = p00;
+      cd1 = p01;
+      load_q(cd0, qa);
+    }
+    if (np > 1) {
+      nd0 = p10;
+      nd1 = p11;
+      load_q(nd0, qn);
+    }
+    if (np > 2) piece(2, fd0, fd1);
+
+    if (a.early_inputs) grid_dependency_wait();  // the cache is complete from here on
+    if (c == 0 && lane == 0) {
       prefetch_tensormap(&tmk);
       prefetch_tensormap(&tmv);
     }
     const uint64_t pol = l2_policy_evict_first();
-    int j_base = 0, j_last = -1;  // the CTA's tile sequence; the end of this issuer's last batch
-    for (int k = 0;; ++k) {
-      const int slot = k % kSchedSlots;
-      if (!sched_wait_warp(smem_u32(cfull + slot), (uint32_t)((k / kSchedSlots) & 1), limit, abort_flag, a.err))
-        break;
-      const int n = slot_desc(slot)[0].w;
-      if (n < 0) break;
-      const int* rows = slot_rows(slot);
-      const int j_start = (j_base + NC - 1) / NC * NC, j_end = j_start + n;  // before j_start: virtual tiles
-      bool ok = true;
-      for (int j0 = j_base / kSchedIssueLanes * kSchedIssueLanes; j0 < j_end; j0 += kSchedIssueLanes) {
-        if ((j0 / kSchedIssueLanes) % NI != w) continue;
-        const int j = j0 + lane, st = j % STAGES;
-        const bool mine = lane < kSchedIssueLanes && j >= j_base && j < j_end;
-        bool got = true;
-        if (mine && j >= STAGES)
-          got = sched_wait(smem_u32(empty + st), (uint32_t)((j / STAGES - 1) & 1), limit, abort_flag, a.err);
-        if (!__all_sync(0xffffffffu, got)) {
-          ok = false;
+    uint8_t* myring = ring + c * S * Geo::STAGE_BYTES;
+    uint64_t* myfull = full + c * S;
+    volatile int* mybad = stage_bad + c * S;
+    const int W = (int)blockIdx.x * NC + c;
+    // lane 0: start the loads of this consumer's tile q into its stage
+    auto issue = [&](int q, int row) {
+      const int st = q % S;
+      mybad[st] = row < 0;
+      if (W == a.hold_warp && q == a.hold_tile) return;  // test hook: the stage never completes
+      const uint32_t bar = smem_u32(myfull + st);
+      if (row < 0) {
+        atomicOr(a.err, MVB_DEV_BLOCK_ID);
+        mbar_arrive(bar);
+        return;
+      }
+      mbar_arrive_expect_tx(bar, Geo::STAGE_BYTES);
+      const uint32_t dk = smem_u32(myring + st * Geo::STAGE_BYTES);
+#pragma unroll
+      for (int p = 0; p < Geo::SUB; ++p) {
+        tma_load_2d(dk + p * Geo::PANEL_BYTES, &tmk, p * 64, row, bar, pol);
+        tma_load_2d(dk + Geo::TILE_BYTES + p * Geo::PANEL_BYTES, &tmv, p * 64, row, bar, pol);
+      }
+    };
+    {
+      const int n0 = nq < S ? nq : S;
+      for (int q = 0; q < n0; ++q) {
+        const int row = __shfl_sync(0xffffffffu, row0, q);
+        if (lane == 0) issue(q, row);
+      }
+    }
+
+    float o[NO][4];
+#pragma unroll
+    for (int nn = 0; nn < NO; ++nn) o[nn][0] = o[nn][1] = o[nn][2] = o[nn][3] = 0.f;
+    float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+    // Hand this consumer's state for piece p to the merger (had: it holds tiles
+    // of p); false when the CTA aborted.
+    auto handoff = [&](int p, bool had) -> bool {
+      const int b = NB == 1 ? 0 : (p & 1), use = NB == 1 ? p : (p >> 1);
+      if (use > 0 &&
+          !sched_wait_warp(smem_u32(mempty + b), (uint32_t)((use - 1) & 1), limit, abort_flag, a.err))
+        return false;
+      if (had) {
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 1);
+          lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 2);
+        }
+        int h0, nh;
+        heads(cd0.y, h0, nh);
+        float* mo = merge + (int64_t)(b * NC + c) * mg * PR;
+#pragma unroll
+        for (int nn = 0; nn < NO; ++nn) {
+          const int d = nn * 8 + 2 * qd;
+          if (g0 < nh) *reinterpret_cast<float2*>(mo + g0 * PR + d) = make_float2(o[nn][0], o[nn][1]);
+          if (g0 + 8 < nh) *reinterpret_cast<float2*>(mo + (g0 + 8) * PR + d) = make_float2(o[nn][2], o[nn][3]);
+        }
+        if (qd == 0) {
+          if (g0 < nh) *reinterpret_cast<float2*>(mo + g0 * PR + D) = make_float2(mrow[0], lrow[0]);
+          if (g0 + 8 < nh) *reinterpret_cast<float2*>(mo + (g0 + 8) * PR + D) = make_float2(mrow[1], lrow[1]);
+        }
+      }
+      warp_arrive(smem_u32(mfull + b), lane);
+#pragma unroll
+      for (int nn = 0; nn < NO; ++nn) o[nn][0] = o[nn][1] = o[nn][2] = o[nn][3] = 0.f;
+      mrow[0] = mrow[1] = -INFINITY;
+      lrow[0] = lrow[1] = 0.f;
+      return true;
+    };
+
+    int p = 0;
+    int vend = np > 0 ? cd1.x + cd0.w : 0;  // end of the current piece's positions
+    bool had = false, failed = false;
+    int q = 0;
+    for (;; ++q) {
+      const int j = q < nq ? c + NC * q : n;  // n, past the range: hand over every remaining piece
+      while (p < np && j >= vend) {  // warp-uniform: the tile lies in a later piece
+        if (!handoff(p, had)) {
+          failed = true;
           break;
         }
-        if (mine && !((int)blockIdx.x == a.hold_warp && j == a.hold_tile)) {  // test hook: never completes
-          const int row = j < j_start ? -1 : rows[j - j_start];
-          stage_bad[st] = row < 0;
-          const uint32_t fb = smem_u32(full + st);
-          if (row < 0) {
-            mbar_arrive(fb);
-          } else {
-            mbar_arrive_expect_tx(fb, Geo::STAGE_BYTES);
-            const uint32_t dk = smem_u32(ring + st * Geo::STAGE_BYTES);
+        had = false;
+        if (++p >= np) break;
+        cd0 = nd0;
+        cd1 = nd1;
 #pragma unroll
-            for (int p = 0; p < Geo::SUB; ++p) {
-              tma_load_2d(dk + p * Geo::PANEL_BYTES, &tmk, p * 64, row, fb, pol);
-              tma_load_2d(dk + Geo::TILE_BYTES + p * Geo::PANEL_BYTES, &tmv, p * 64, row, fb, pol);
-            }
-          }
-        }
-        j_last = min(j0 + kSchedIssueLanes, j_end) - 1;
+        for (int kc = 0; kc < KC; ++kc)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) qa[kc][e] = qn[kc][e];
+        vend = cd1.x + cd0.w;
+        nd0 = fd0;
+        nd1 = fd1;
+        if (p + 1 < np) load_q(nd0, qn);
+        if (p + 2 < np) piece(p + 2, fd0, fd1);
       }
-      if (!ok) break;
-      j_base = j_end;
-      warp_arrive(smem_u32(cempty + slot), lane);
+      if (failed || q >= nq) break;
+      const int st = q % S;
+      if (!sched_wait_warp(smem_u32(myfull + st), (uint32_t)((q / S) & 1), limit, abort_flag, a.err)) {
+        failed = true;
+        break;
+      }
+      if (!mybad[st]) {
+        const int t = cd0.z + (j - cd1.x);  // tile of the unit
+        const int valid = min(kTile, cd1.y - t * kTile);
+        const uint32_t kb = smem_u32(myring + st * Geo::STAGE_BYTES);
+        attend_tile<T, D>(kb, kb + Geo::TILE_BYTES, valid, a.scale_log2, qa, o, mrow, lrow);
+      }
+      had = true;
+      __syncwarp();
+      const int qi = q + S;
+      if (qi < nq) {
+        if ((qi >> 5) != rb) {
+          rcur = rnext;
+          ++rb;
+          rnext = load_rows(rb + 1);
+        }
+        const int row = __shfl_sync(0xffffffffu, rcur, qi & 31);
+        if (lane == 0) {
+          fence_proxy_async_smem();  // V rows zeroed through the generic proxy before the next copy
+          issue(qi, row);
+        }
+      }
     }
-    // Wait (bounded, without the abort shortcut) for this issuer's loads still in
-    // flight, the latest use of each of its stages, so no copy lands after the
-    // CTA has left.
-    for (int i = lane; i < STAGES; i += 32) {
-      const int jj = j_last - i;
-      if (jj < 0 || (jj / kSchedIssueLanes) % NI != w || ((int)blockIdx.x == a.hold_warp && jj == a.hold_tile))
-        continue;
-      mbar_wait_bounded(smem_u32(full + jj % STAGES), (uint32_t)((jj / STAGES) & 1), limit);
+    if (!failed) return;
+    // Aborted: wait (bounded, without the abort shortcut) for this consumer's
+    // copies still in flight, so that none lands after the CTA has left.
+    const int issued = nq < q + S ? nq : q + S;
+    for (int jj = q; jj < issued; ++jj) {
+      if (W == a.hold_warp && jj == a.hold_tile) continue;
+      mbar_wait_bounded(smem_u32(myfull + jj % S), (uint32_t)((jj / S) & 1), limit);
     }
     return;
   }
 
-  if (warp < 1 + NI + NC) {
-    // ================================ consumers ================================
-    const int c = warp - 1 - NI;
-    const int g0 = lane >> 2, qd = lane & 3;
-    int j_base = 0;
-    for (int k = 0;; ++k) {
-      const int slot = k % kSchedSlots;
-      if (!sched_wait_warp(smem_u32(cfull + slot), (uint32_t)((k / kSchedSlots) & 1), limit, abort_flag, a.err))
-        return;
-      const int4 d0 = slot_desc(slot)[0], d1 = slot_desc(slot)[1];
-      const int n = d0.w;
-      const int begin = d0.z, ctx = d1.z;
-      uint32_t qa[KC][4];
-      if (n > 0) {
-        const uint32_t* qs = reinterpret_cast<const uint32_t*>(slot_q(slot));
-#pragma unroll
-        for (int kc = 0; kc < KC; ++kc) {
-          const int w = kc * 8 + qd;  // word column of element kc * 16 + 2 qd
-          qa[kc][0] = qs[g0 * (QP / 2) + w];
-          qa[kc][1] = qs[(g0 + 8) * (QP / 2) + w];
-          qa[kc][2] = qs[g0 * (QP / 2) + w + 4];
-          qa[kc][3] = qs[(g0 + 8) * (QP / 2) + w + 4];
-        }
-      }
-      if (n >= 0) warp_arrive(smem_u32(cempty + slot), lane);  // descriptor and query are in registers
-
-      float o[NO][4];
-#pragma unroll
-      for (int nn = 0; nn < NO; ++nn) o[nn][0] = o[nn][1] = o[nn][2] = o[nn][3] = 0.f;
-      float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
-      // tile j of the sequence is this consumer's when j % NC == c; the chunk's
-      // tiles start at j_start (a multiple of NC; before it, virtual tiles)
-      const int j_start = (j_base + NC - 1) / NC * NC;
-      const int j_end = n >= 0 ? j_start + n : j_base;  // the end marker has no tiles, virtual or real
-      for (int jj = j_base + (c - j_base % NC + NC) % NC; jj < j_end; jj += NC) {
-        const int st = jj % STAGES;
-        if (!sched_wait_warp(smem_u32(full + st), (uint32_t)((jj / STAGES) & 1), limit, abort_flag, a.err))
-          return;
-        if (!stage_bad[st]) {
-          const int i = jj - j_start;
-          const int valid = min(kTile, ctx - (begin + i) * kTile);
-          const uint32_t kb = smem_u32(ring + st * Geo::STAGE_BYTES);
-          attend_tile<T, D>(kb, kb + Geo::TILE_BYTES, valid, a.scale_log2, qa, o, mrow, lrow);
-          if (valid < kTile) fence_proxy_async_smem();  // V rows zeroed through the generic proxy
-        }
-        warp_arrive(smem_u32(empty + st), lane);
-      }
-      j_base = j_end;
-
-      // ---- hand this consumer's state to the chunk's merger; at the end, the
-      // end marker to every merger (chunks k .. k + NM - 1) ----
-      for (int e = 0; e < (n < 0 ? NM : 1); ++e) {
-        const int kk = k + e, b = kk % NB;
-        if (kk >= NB &&
-            !sched_wait_warp(smem_u32(mempty + b), (uint32_t)((kk / NB - 1) & 1), limit, abort_flag, a.err))
-          return;
-        if (n >= 0) {
-#pragma unroll
-          for (int r = 0; r < 2; ++r) {
-            lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 1);
-            lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 2);
-          }
-          const int nh = min(16, a.G - (d0.y % a.head_groups) * 16);
-          float* mo = mb_o(b) + c * 16 * D;
-#pragma unroll
-          for (int nn = 0; nn < NO; ++nn) {
-            const int d = nn * 8 + 2 * qd;
-            if (g0 < nh) *reinterpret_cast<float2*>(mo + g0 * D + d) = make_float2(o[nn][0], o[nn][1]);
-            if (g0 + 8 < nh) *reinterpret_cast<float2*>(mo + (g0 + 8) * D + d) = make_float2(o[nn][2], o[nn][3]);
-          }
-          if (qd == 0) {
-            float2* mml = mb_ml(b) + c * 16;
-            if (g0 < nh) mml[g0] = make_float2(mrow[0], lrow[0]);
-            if (g0 + 8 < nh) mml[g0 + 8] = make_float2(mrow[1], lrow[1]);
-          }
-        }
-        if (c == 0 && lane == 0) {
-          mb_hdr(b)[0] = d0;
-          mb_hdr(b)[1] = d1;
-        }
-        warp_arrive(smem_u32(mfull + b), lane);
-      }
-      if (n < 0) return;
-    }
-  }
-
-  // ================================== mergers =================================
-  // Merger m takes chunks k with k % NM == m, through its own buffers
-  // b = k % NB (b % NM == m).  Lane l takes head row r = l / 4 (+ 8 on a second
-  // pass for more than 8 heads) and column quarter l % 4 (CQ = D / 4 columns).
+  // ================================== merger ==================================
+  // Lane l takes head row l / 4 (+ 8 for more than 8 heads) and column quarter
+  // l % 4 (CQ = D / 4 columns).
   {
     constexpr int CQ = D / 4;
-    const int m = warp - (1 + NI + NC);
     const int rq = lane >> 2, cq = (lane & 3) * CQ;
     T* const outp = static_cast<T*>(a.out);
-    for (int k = m;; k += NM) {
-      const int b = k % NB;
-      if (!sched_wait_warp(smem_u32(mfull + b), (uint32_t)((k / NB) & 1), limit, abort_flag, a.err)) return;
-      const int4 d0 = mb_hdr(b)[0], d1 = mb_hdr(b)[1];
-      if (d0.w < 0) return;  // end marker
-      const int seq = d0.x, uk = d0.y;
-      const int first = d1.x, p = d1.y, me = d1.w;
-      const int kvh = uk / a.head_groups, hg = uk - kvh * a.head_groups;
-      const int h0 = kvh * a.G + hg * 16, nh = min(16, a.G - hg * 16);
-      // the NC consumer states of each row -> (M, L, O) of the chunk
-      float Mr[2], Lr[2], Or[2][CQ];
+    grid_dependency_wait();  // the previous decode's counters, outputs and partial states
+    const int n_bad = __ldcg(&sa.hdr->n_bad);
+    if (blockIdx.x == 0 && lane == 0) {
+      const int bb = __ldcg(&sa.hdr->bad_bits);
+      if (bb) atomicOr(a.err, bb);
+    }
+    for (int i = blockIdx.x; i < n_bad; i += gridDim.x) {  // rows of the sequences left out: zeros
+      T* o = outp + (int64_t)__ldcg(sa.bad + i) * a.o_s0;
+      for (int e = lane; e < a.num_heads * D; e += 32) o[(int64_t)(e / D) * a.o_s1 + e % D] = from_f32<T>(0.f);
+    }
+    // Slot of CTA `cta`'s partial state of the cut unit of descriptor d1.
+    auto cut_slot = [&](const int4& d1, int cta) {
+      const int c0 = d1.z;
+      return cta == c0 ? 2 * c0 + ((d1.w & 1) ? 0 : 1) : 2 * cta;
+    };
+    // Cut pieces (at most two, the CTA's first two) whose partial states are
+    // stored: count them in on their units' counters, both in flight at once,
+    // and merge the units they arrive last at, in CTA order (deterministic).
+    // Each step is an L2 round trip (~2 us under a full DRAM stream): it runs
+    // behind the first whole piece's merge, so the buffers keep draining.
+    int npend = 0;
+    int4 pa0 = make_int4(0, 0, 0, 0), pa1 = pa0, pb0 = pa0, pb1 = pa0;
+    auto finish_cuts = [&]() {
+      if (npend == 0) return;
+      fence_acq_rel_gpu();  // this lane's partial stores are visible GPU-wide before the arrivals
+      __syncwarp();
+      int arr = 0;
+      if (lane == 0) arr = atomicAdd(sa.ucnt + pa1.z, 1);
+      if (lane == 1 && npend > 1) arr = atomicAdd(sa.ucnt + pb1.z, 1);
+      const int arr_a = __shfl_sync(0xffffffffu, arr, 0), arr_b = __shfl_sync(0xffffffffu, arr, 1);
+      const bool last_a = arr_a == (pa1.w >> 1) - 1, last_b = npend > 1 && arr_b == (pb1.w >> 1) - 1;
+      npend = 0;
+      if (!last_a && !last_b) return;
+      fence_acq_rel_gpu();  // acquire side: the other CTAs' partials
+#pragma unroll 1
+      for (int k = 0; k < 2; ++k) {
+        if (!(k == 0 ? last_a : last_b)) continue;
+        const int4 d0 = k == 0 ? pa0 : pb0, d1 = k == 0 ? pa1 : pb1;
+        const int seq = d0.x, c0 = d1.z, ncon = d1.w >> 1;
+        int h0, nh;
+        heads(d0.y, h0, nh);
 #pragma unroll
-      for (int pass = 0; pass < 2; ++pass) {
-        const int r = rq + 8 * pass;
-        Mr[pass] = -INFINITY;
-        Lr[pass] = 0.f;
+        for (int pass = 0; pass < 2; ++pass) {
+          const int r = rq + 8 * pass;
+          if (r >= nh) continue;  // lane-divergent: no warp collectives below
+          float M = -INFINITY, Lsum = 0.f, acc[CQ];
 #pragma unroll
-        for (int i = 0; i < CQ; ++i) Or[pass][i] = 0.f;
-        if (r >= nh) continue;
-        float2 ml[NC];
+          for (int i = 0; i < CQ; ++i) acc[i] = 0.f;
+          for (int i0 = 0; i0 < ncon; i0 += 4) {
+            float2 ml[4];
+            float4 ov[4][CQ / 4];
 #pragma unroll
-        for (int s = 0; s < NC; ++s) {
-          ml[s] = mb_ml(b)[s * 16 + r];
-          Mr[pass] = fmaxf(Mr[pass], ml[s].x);
-        }
-        if (Mr[pass] == -INFINITY) continue;  // no token (a bad sequence): zeros
+            for (int t = 0; t < 4; ++t) {
+              const int i = i0 + t < ncon ? i0 + t : ncon - 1;
+              const float* pp = sa.part + ((int64_t)cut_slot(d1, c0 + i) * mg + r) * PR;
+              ml[t] = __ldcg(reinterpret_cast<const float2*>(pp + D));
 #pragma unroll
-        for (int s = 0; s < NC; ++s) {
-          const float w = fast_exp2(ml[s].x - Mr[pass]);
-          Lr[pass] = fmaf(ml[s].y, w, Lr[pass]);
-          const float4* src = reinterpret_cast<const float4*>(mb_o(b) + (s * 16 + r) * D + cq);
+              for (int v = 0; v < CQ / 4; ++v) ov[t][v] = __ldcg(reinterpret_cast<const float4*>(pp + cq) + v);
+            }
 #pragma unroll
-          for (int i = 0; i < CQ / 4; ++i) {
-            const float4 v = src[i];
-            Or[pass][4 * i] = fmaf(v.x, w, Or[pass][4 * i]);
-            Or[pass][4 * i + 1] = fmaf(v.y, w, Or[pass][4 * i + 1]);
-            Or[pass][4 * i + 2] = fmaf(v.z, w, Or[pass][4 * i + 2]);
-            Or[pass][4 * i + 3] = fmaf(v.w, w, Or[pass][4 * i + 3]);
+            for (int t = 0; t < 4; ++t) {
+              if (i0 + t >= ncon || ml[t].x == -INFINITY) continue;
+              const float mn = fmaxf(M, ml[t].x);
+              const float sa_ = fast_exp2(M - mn), sb = fast_exp2(ml[t].x - mn);
+              Lsum = Lsum * sa_ + ml[t].y * sb;
+#pragma unroll
+              for (int v = 0; v < CQ / 4; ++v) {
+                acc[4 * v] = acc[4 * v] * sa_ + ov[t][v].x * sb;
+                acc[4 * v + 1] = acc[4 * v + 1] * sa_ + ov[t][v].y * sb;
+                acc[4 * v + 2] = acc[4 * v + 2] * sa_ + ov[t][v].z * sb;
+                acc[4 * v + 3] = acc[4 * v + 3] * sa_ + ov[t][v].w * sb;
+              }
+              M = mn;
+            }
           }
+          store_row(outp + (int64_t)seq * a.o_s0 + (int64_t)(h0 + r) * a.o_s1 + cq, acc,
+                    Lsum > 0.f ? 1.f / Lsum : 0.f);
         }
+        __syncwarp();
+        if (lane == 0) sa.ucnt[c0] = 0;  // zero at rest for the next decode of this schedule
       }
+    };
+    // Piece descriptors reach the merger through a 4-slot shared-memory ring,
+    // copied 4 pieces ahead with cp.async (lanes 0 and 1, one group per piece):
+    // a load into registers would stall the warp at its first use (~1-2 us from
+    // L2 under a full DRAM stream), and one call site of the merge keeps the
+    // merger's code small (it runs a few times per kernel, from a cold
+    // instruction cache).
+    auto fetch = [&](int p) {
+      if (p < np && lane < 2) {
+        const int4* src = p < 2 ? &rc->p[p][lane] : sa.desc + 2 * (pbase + p) + lane;
+        cp_async_16(smem_u32(dring + 2 * (p & 3) + lane), src);
+      }
+      cp_async_commit();
+    };
+#pragma unroll 1
+    for (int p = 0; p < 4; ++p) fetch(p);
+#pragma unroll 1
+    for (int p = 0; p < np; ++p) {
+      cp_async_wait_group<3>();  // piece p's group has landed
+      __syncwarp();
+      const int4 d0 = dring[2 * (p & 3)], d1 = dring[2 * (p & 3) + 1];
+      __syncwarp();  // every lane has read the slot before it is refilled
+      fetch(p + 4);
+      const int b = NB == 1 ? 0 : (p & 1), use = NB == 1 ? p : (p >> 1);
+      if (!sched_wait_warp(smem_u32(mfull + b), (uint32_t)(use & 1), limit, abort_flag, a.err)) return;
+      int h0, nh;
+      heads(d0.y, h0, nh);
+      const float* mb = merge + (int64_t)b * NC * mg * PR;
+      const int first = d1.x % NC;
+      float M0, L0, O0[CQ], M1 = 0.f, L1 = 0.f, O1[CQ];
+      merge_row<D, NC>(mb, mg, rq, cq, first, d0.w, rq < nh, M0, L0, O0);
+      if (nh > 8) merge_row<D, NC>(mb, mg, rq + 8, cq, first, d0.w, rq + 8 < nh, M1, L1, O1);
       warp_arrive(smem_u32(mempty + b), lane);  // the states are in registers: the buffer is free
-
-      if (p == 1) {
+      if (d1.z < 0) {  // the whole unit
+        T* po = outp + (int64_t)d0.x * a.o_s0 + (int64_t)h0 * a.o_s1 + cq;
+        if (rq < nh) store_row(po + (int64_t)rq * a.o_s1, O0, L0 > 0.f ? 1.f / L0 : 0.f);
+        if (rq + 8 < nh) store_row(po + (int64_t)(rq + 8) * a.o_s1, O1, L1 > 0.f ? 1.f / L1 : 0.f);
+      } else {
+        // a piece of a cut unit: store its partial state now; the arrival
+        // waits for finish_cuts
+        const int self = cut_slot(d1, (int)blockIdx.x);
 #pragma unroll
         for (int pass = 0; pass < 2; ++pass) {
           const int r = rq + 8 * pass;
           if (r >= nh) continue;
-          const float inv = Lr[pass] > 0.f ? 1.f / Lr[pass] : 0.f;
-          T* po = outp + (int64_t)seq * a.o_s0 + (int64_t)(h0 + r) * a.o_s1 + cq;
+          float* pp = sa.part + ((int64_t)self * mg + r) * PR;
+          const float* src = pass == 0 ? O0 : O1;
+          float4* dst = reinterpret_cast<float4*>(pp + cq);
 #pragma unroll
-          for (int i = 0; i < CQ; ++i) po[i] = from_f32<T>(Or[pass][i] * inv);
+          for (int i = 0; i < CQ / 4; ++i)
+            dst[i] = make_float4(src[4 * i], src[4 * i + 1], src[4 * i + 2], src[4 * i + 3]);
+          if ((lane & 3) == 0)
+            *reinterpret_cast<float2*>(pp + D) = pass == 0 ? make_float2(M0, L0) : make_float2(M1, L1);
         }
-        continue;
-      }
-      // a piece of a split unit: store the partial, count in; the last piece merges
-#pragma unroll
-      for (int pass = 0; pass < 2; ++pass) {
-        const int r = rq + 8 * pass;
-        if (r >= nh) continue;
-        float* pp = sa.part + ((int64_t)me * sa.mg + r) * PR;
-        float4* dst = reinterpret_cast<float4*>(pp + cq);
-#pragma unroll
-        for (int i = 0; i < CQ / 4; ++i)
-          dst[i] = make_float4(Or[pass][4 * i], Or[pass][4 * i + 1], Or[pass][4 * i + 2], Or[pass][4 * i + 3]);
-        if ((lane & 3) == 0) *reinterpret_cast<float2*>(pp + D) = make_float2(Mr[pass], Lr[pass]);
-      }
-      fence_acq_rel_gpu();  // this lane's partial is visible GPU-wide before the arrival
-      __syncwarp();
-      int arrived = 0;
-      if (lane == 0) arrived = atomicAdd(sa.ucnt + first, 1);
-      arrived = __shfl_sync(0xffffffffu, arrived, 0);
-      if (arrived != p - 1) continue;
-      fence_acq_rel_gpu();  // acquire side: the other pieces' partials
-      // online merge of the pieces in piece order (deterministic), 4 at a time
-#pragma unroll
-      for (int pass = 0; pass < 2; ++pass) {
-        const int r = rq + 8 * pass;
-        if (r >= nh) continue;  // lane-divergent: no warp collectives below
-        float M = -INFINITY, Lsum = 0.f, acc[CQ];
-#pragma unroll
-        for (int i = 0; i < CQ; ++i) acc[i] = 0.f;
-        for (int i0 = 0; i0 < p; i0 += 4) {
-          float2 ml[4];
-          float4 ov[4][CQ / 4];
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const int i = i0 + t < p ? i0 + t : p - 1;
-            const float* pp = sa.part + ((int64_t)(first + i) * sa.mg + r) * PR;
-            ml[t] = __ldcg(reinterpret_cast<const float2*>(pp + D));
-#pragma unroll
-            for (int v = 0; v < CQ / 4; ++v) ov[t][v] = __ldcg(reinterpret_cast<const float4*>(pp + cq) + v);
-          }
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            if (i0 + t >= p) break;
-            const float mn = fmaxf(M, ml[t].x);
-            const float sa_ = fast_exp2(M - mn), sb = fast_exp2(ml[t].x - mn);
-            Lsum = Lsum * sa_ + ml[t].y * sb;
-#pragma unroll
-            for (int v = 0; v < CQ / 4; ++v) {
-              acc[4 * v] = acc[4 * v] * sa_ + ov[t][v].x * sb;
-              acc[4 * v + 1] = acc[4 * v + 1] * sa_ + ov[t][v].y * sb;
-              acc[4 * v + 2] = acc[4 * v + 2] * sa_ + ov[t][v].z * sb;
-              acc[4 * v + 3] = acc[4 * v + 3] * sa_ + ov[t][v].w * sb;
-            }
-            M = mn;
-          }
+        if (npend == 0) {
+          pa0 = d0;
+          pa1 = d1;
+        } else {
+          pb0 = d0;
+          pb1 = d1;
         }
-        const float inv = 1.f / Lsum;
-        T* po = outp + (int64_t)seq * a.o_s0 + (int64_t)(h0 + r) * a.o_s1 + cq;
-#pragma unroll
-        for (int i = 0; i < CQ; ++i) po[i] = from_f32<T>(acc[i] * inv);
+        ++npend;
       }
-      __syncwarp();
-      if (lane == 0) sa.ucnt[first] = 0;  // zero at rest for the next decode of this schedule
+      if (p == 2) finish_cuts();  // behind the first whole piece
     }
+    cp_async_wait_group<0>();
+    finish_cuts();  // fewer than three pieces
   }
 }
 
@@ -744,69 +893,94 @@ decode_sched_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_consta
 // host side
 // ---------------------------------------------------------------------------
 
+int sched_max_smem_per_block() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 232448;
+  if (cache[dev] == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess || v <= 0)
+      v = 232448;
+    cache[dev] = v;
+  }
+  return cache[dev];
+}
+
+static int sched_smem_for(int head_dim, int mg, int nb) {
+  return 1024 + (head_dim == 64 ? SchedSmem<64>::bytes(mg, nb) : SchedSmem<128>::bytes(mg, nb));
+}
+
 SchedLayout sched_layout(int num_seqs, int num_kv_heads, int head_groups, int G, int max_blocks,
                          int block_size, int head_dim, int ctas) {
   SchedLayout l = {};
   const int64_t units = (int64_t)num_seqs * num_kv_heads * head_groups;
-  const int64_t max_tiles = ((int64_t)max_blocks * block_size + kTile - 1) / kTile;
-  const int64_t per_unit = (max_tiles + kSchedMaxPiece - 1) / kSchedMaxPiece;
-  // sum over units of ceil(tiles / piece) <= total / piece + units, and the
-  // schedule's choice of piece keeps total / piece <= max(units * per_unit, 2 * ctas)
-  int64_t mc = units * per_unit;
-  if (mc < 2LL * ctas) mc = 2LL * ctas;
-  mc += units;
-  if (mc < 1) mc = 1;
-  l.max_chunks = mc;
+  const int64_t unit_tiles = ((int64_t)max_blocks * block_size + kTile - 1) / kTile;
+  l.ctas = ctas;
   l.mg = G < 16 ? G : 16;
+  l.max_tiles = units * unit_tiles;
+  l.max_pieces = units + ctas;
+  const int cap = sched_max_smem_per_block();
+  l.nb = sched_smem_for(head_dim, l.mg, 2) <= cap ? 2 : sched_smem_for(head_dim, l.mg, 1) <= cap ? 1 : 0;
+  l.ok = l.nb > 0 && num_seqs <= kSchedMaxSeqs && ctas >= 1 && ctas <= kSchedMaxCtas &&
+         l.max_tiles < ((int64_t)1 << 31) - 1;
   auto up = [](int64_t v) { return (v + 255) / 256 * 256; };
-  l.off_desc = 256;
-  l.off_ucnt = l.off_desc + up(mc * 32);
-  l.off_part = l.off_ucnt + up(mc * 4);
-  l.bytes = l.off_part + up(mc * l.mg * (head_dim + 4) * 4);
+  l.off_rec = 256;
+  l.off_desc = l.off_rec + up((int64_t)ctas * 256);
+  l.off_rows = l.off_desc + up(l.max_pieces * 32);
+  l.off_bad = l.off_rows + up(l.max_tiles * 4);
+  l.off_ucnt = l.off_bad + up((int64_t)num_seqs * 4);
+  l.off_part = l.off_ucnt + up((int64_t)ctas * 4);
+  l.bytes = l.off_part + up((int64_t)2 * ctas * l.mg * (head_dim + 4) * 4);
   return l;
 }
 
-int sched_smem_bytes(int head_dim) {
-  return 1024 + (head_dim == 64 ? SchedSmem<64>::BYTES : SchedSmem<128>::BYTES);
-}
+int sched_smem_bytes(int head_dim, int mg, int nb) { return sched_smem_for(head_dim, mg, nb); }
 
-cudaError_t launch_decode_schedule(const DecodeArgs& a, const SchedLayout& l, void* ws, int ctas, bool wait_at_end,
-                                   cudaStream_t stream) {
+cudaError_t launch_decode_schedule(const DecodeArgs& a, int head_dim, const SchedLayout& l, void* ws,
+                                   bool wait_at_end, cudaStream_t stream) {
   char* w = static_cast<char*>(ws);
   auto kern = decode_schedule_kernel;
-  cudaError_t e = ensure_kernel_attrs(kern, 0);
+  const int smem = 2 * (a.num_seqs + 1) * 4;
+  cudaError_t e = ensure_kernel_attrs(kern, smem);
   if (e != cudaSuccess) return e;
-  return launch_pdl(kern, dim3(1), dim3(kSchedBuildThreads), 0, stream, a.kv_len, a.num_seqs,
-                    a.num_kv_heads * a.head_groups, a.block_size, a.max_blocks, ctas,
-                    reinterpret_cast<SchedHeader*>(w), reinterpret_cast<int4*>(w + l.off_desc),
-                    reinterpret_cast<int*>(w + l.off_ucnt), (int)l.max_chunks, a.err, wait_at_end ? 1 : 0);
+  const int nc = head_dim == 64 ? SchedConfig<64>::NC : SchedConfig<128>::NC;
+  const int st = head_dim == 64 ? SchedConfig<64>::S : SchedConfig<128>::S;
+  return launch_pdl(kern, dim3(l.ctas), dim3(kSchedBuildThreads), smem, stream, a.kv_len, a.bt, a.bt_s0,
+                    a.num_seqs, a.num_kv_heads, a.head_groups, a.block_size, a.max_blocks, a.num_blocks, nc, st,
+                    reinterpret_cast<SchedHeader*>(w), reinterpret_cast<SchedRec*>(w + l.off_rec),
+                    reinterpret_cast<int4*>(w + l.off_desc), reinterpret_cast<int*>(w + l.off_rows),
+                    reinterpret_cast<int*>(w + l.off_bad), reinterpret_cast<int*>(w + l.off_ucnt), a.err,
+                    wait_at_end ? 1 : 0);
 }
 
 template <typename T, int D>
 cudaError_t launch_sched_t(const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a,
-                           const SchedLayout& l, void* ws, int ctas, cudaStream_t stream) {
+                           const SchedLayout& l, void* ws, cudaStream_t stream) {
   auto kern = decode_sched_kernel<T, D>;
-  const int smem = 1024 + SchedSmem<D>::BYTES;
+  const int smem = sched_smem_for(D, l.mg, l.nb);
   cudaError_t e = ensure_kernel_attrs(kern, smem);
   if (e != cudaSuccess) return e;
   char* w = static_cast<char*>(ws);
   SchedArgs sa;
-  sa.hdr = reinterpret_cast<SchedHeader*>(w);
+  sa.hdr = reinterpret_cast<const SchedHeader*>(w);
+  sa.rec = reinterpret_cast<const SchedRec*>(w + l.off_rec);
   sa.desc = reinterpret_cast<const int4*>(w + l.off_desc);
+  sa.rows = reinterpret_cast<const int*>(w + l.off_rows);
+  sa.bad = reinterpret_cast<const int*>(w + l.off_bad);
   sa.ucnt = reinterpret_cast<int*>(w + l.off_ucnt);
   sa.part = reinterpret_cast<float*>(w + l.off_part);
-  sa.max_chunks = (int)l.max_chunks;
   sa.mg = l.mg;
-  return launch_pdl(kern, dim3(ctas), dim3(SchedSmem<D>::THREADS), smem, stream, tmk, tmv, a, sa);
+  sa.nb = l.nb;
+  return launch_pdl(kern, dim3(l.ctas), dim3(SchedSmem<D>::THREADS), smem, stream, tmk, tmv, a, sa);
 }
 
 cudaError_t launch_decode_sched(const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a, int dtype,
-                                int head_dim, const SchedLayout& l, void* ws, int ctas, cudaStream_t stream) {
+                                int head_dim, const SchedLayout& l, void* ws, cudaStream_t stream) {
   if (dtype == MVB_DTYPE_BF16)
-    return head_dim == 64 ? launch_sched_t<__nv_bfloat16, 64>(tmk, tmv, a, l, ws, ctas, stream)
-                          : launch_sched_t<__nv_bfloat16, 128>(tmk, tmv, a, l, ws, ctas, stream);
-  return head_dim == 64 ? launch_sched_t<__half, 64>(tmk, tmv, a, l, ws, ctas, stream)
-                        : launch_sched_t<__half, 128>(tmk, tmv, a, l, ws, ctas, stream);
+    return head_dim == 64 ? launch_sched_t<__nv_bfloat16, 64>(tmk, tmv, a, l, ws, stream)
+                          : launch_sched_t<__nv_bfloat16, 128>(tmk, tmv, a, l, ws, stream);
+  return head_dim == 64 ? launch_sched_t<__half, 64>(tmk, tmv, a, l, ws, stream)
+                        : launch_sched_t<__half, 128>(tmk, tmv, a, l, ws, stream);
 }
 
 }  // namespace mvb

@@ -51,20 +51,25 @@ struct DecodeArgs {
   int early_inputs;  // read query / block table / kv_len before the grid-dependency wait
   // Test hook of the bounded waits: the load of local tile `hold_tile` of
   // stream warp `hold_warp` (stream kernel), or of tile number `hold_tile` of
-  // CTA `hold_warp` (scheduled kernel), is never issued, so the wait on it runs
-  // out after `wait_limit` try-waits and reports MVB_DEV_TIMEOUT.
+  // consumer warp `hold_warp` (CTA * consumers + consumer; scheduled kernel), is
+  // never issued, so the wait on it runs out after `wait_limit` try-waits and
+  // reports MVB_DEV_TIMEOUT.
   // Production calls: hold_warp = -1, wait_limit = kWaitSpinLimit.
   int hold_warp, hold_tile;
   int wait_limit;
 };
 
 // Workspace layout of the scheduled decode (MVB_DECODE_SCHED): a 256-byte
-// header, the chunk descriptors, the per-unit arrival counters and the partial
-// states, each 256-byte aligned.
+// header, one 256-byte record per CTA, the piece descriptors, the pool rows of
+// every tile, the list of sequences left out, the arrival counters of cut units
+// and their partial states, each 256-byte aligned.
 struct SchedLayout {
-  int64_t max_chunks;  // upper bound on the chunks any schedule of this shape lists
-  int mg;              // partial-state rows per chunk (query heads per unit)
-  int64_t off_desc, off_ucnt, off_part, bytes;
+  int ctas;  // decode grid: one CTA per SM
+  int mg;    // partial-state rows per piece: min(16, G)
+  int nb;    // merge buffers between the consumer warps and the merger (0: no fit)
+  bool ok;   // the shape fits the variant
+  int64_t max_tiles, max_pieces;
+  int64_t off_rec, off_desc, off_rows, off_bad, off_ucnt, off_part, bytes;
 };
 
 // ---------------------------------------------------------------------------

@@ -1,14 +1,16 @@
-"""The scheduled persistent decode (variant "sched", the default) and its
-per-step schedule (GPU).
+"""The scheduled persistent decode (variant "sched") and its per-step
+schedule (GPU).
 
-The schedule kernel lists every (sequence, KV head, head group) unit cut into
-pieces of at most `piece` 16-token tiles, longest first; the decode kernel's
-CTAs take pieces from a counter and the last piece of a split unit merges it.
-These tests check the schedule itself against a CPU restatement (as sets: the
-order inside a bucket is arbitrary by design), the decode against the oracle
-over batch sizes from 1 to 5000 and units thousands of tiles long, the reuse
-of one schedule by several layers, the write-then-decode overlap, the
-backend's once-per-step build, concurrent streams, and bad sequences.
+The schedule kernel cuts the tile stream of every (sequence, KV head, head
+group) unit into one range per SM, lists each range's pieces (the ones cut by
+its ends first) and resolves the pool row of every tile; the decode kernel
+streams each range with self-issuing consumer warps, and the last piece of a
+unit cut by a range boundary merges it.  These tests check the device schedule
+entry by entry against its CPU restatement (tests/sched_model.py), the decode
+against the oracle over batch sizes from 1 to 5000 and units spanning many
+SMs, the reuse of one schedule by several layers, the write-then-decode
+overlap, the backend's once-per-step build, concurrent streams, and bad
+sequences.
 """
 
 from __future__ import annotations
@@ -19,12 +21,14 @@ import torch
 
 import mini_vllm_b200 as M
 import oracle
+import sched_model as SM
 from conftest import torch_to_np
 from mini_vllm_b200 import workloads as W
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
-MAX_PIECE, MIN_PIECE = 32, 4
+NC = {64: 11, 128: 6}     # consumer warps per CTA
+STAGES = {64: 4, 128: 4}  # ring stages per consumer
 
 
 def close(gpu: torch.Tensor, ref: np.ndarray, msg: str = ""):
@@ -43,32 +47,54 @@ def ref_decode(spec, t, kc=None, vc=None):
     return ref
 
 
-def restated_pieces(ctx, units_per_seq, block_size, max_blocks, ctas):
-    """CPU restatement of the schedule kernel's cut: {(seq, unit): [(first
-    tile, tiles), ...]} and the piece length chosen."""
-    def bad(c):
-        return c < 1 or -(-c // block_size) > max_blocks
-    total = sum(-(-c // 16) for c in ctx if not bad(c)) * units_per_seq
-    piece = min(MAX_PIECE, max(MIN_PIECE, -(-total // (2 * ctas)) if total else MIN_PIECE))
-    out = {}
-    for s, c in enumerate(ctx):
-        nt = 0 if bad(c) else -(-c // 16)
-        p = 1 if bad(c) else -(-nt // piece)
-        for k in range(units_per_seq):
-            out[(s, k)] = [(i * nt // p, (i + 1) * nt // p - i * nt // p) for i in range(p)]
-    return out, piece
+def _ctas():
+    return torch.cuda.get_device_properties(0).multi_processor_count
 
 
-def read_schedule(sched):
-    ws = sched.workspace
-    hdr = ws[:256].view(torch.int32).cpu().numpy()
-    n = int(hdr[0])
-    desc = ws[256:256 + 32 * n].view(torch.int32).cpu().numpy().reshape(n, 8)
-    return hdr, desc
+def read_schedule(sched, spec, h, kh, d):
+    """The device schedule: header, records, pieces, rows, left-out list and
+    arrival counters, cut out of the workspace at sched_layout's offsets."""
+    hg = -(-(h // kh) // 16)
+    lay = SM.sched_layout(spec.num_seqs, kh, hg, spec.max_blocks, 16, _ctas(), G=h // kh, head_dim=d)
+    ws = sched.workspace.cpu()
+    i32 = lambda a, b: ws[a:b].view(torch.int32).numpy()
+    hdr = i32(0, 256)
+    T, ce, n_bad = int(hdr[0]), int(hdr[1]), int(hdr[2])
+    rec = i32(lay["off_rec"], lay["off_rec"] + 256 * _ctas()).reshape(_ctas(), 64)
+    npieces = int(rec[:, 1].sum())
+    desc = i32(lay["off_desc"], lay["off_desc"] + 32 * npieces).reshape(npieces, 8)
+    rows = i32(lay["off_rows"], lay["off_rows"] + 4 * T)
+    bad = i32(lay["off_bad"], lay["off_bad"] + 4 * n_bad)
+    ucnt = i32(lay["off_ucnt"], lay["off_ucnt"] + 4 * _ctas())
+    return {"hdr": hdr, "T": T, "ctas": ce, "rec": rec, "desc": desc, "rows": rows, "bad": bad, "ucnt": ucnt}
+
+
+def check_schedule(dev, spec, h, kh, d):
+    """The device schedule equals the CPU restatement entry by entry."""
+    hg = -(-(h // kh) // 16)
+    want = SM.schedule(spec.context_lens, spec.block_tables, kh, hg, 16, spec.num_blocks, _ctas(), NC[d], STAGES[d])
+    assert dev["T"] == want["T"] and dev["ctas"] == want["ctas"]
+    assert dev["bad"].tolist() == want["bad"]
+    assert (dev["ucnt"] == 0).all()  # arrival counters at rest
+    for c in range(_ctas()):
+        assert tuple(dev["rec"][c, :4]) == want["rec"][c], c
+        pbase, np_ = want["rec"][c][:2]
+        for pos in range(min(np_, 2)):  # the record's copy of its first two pieces
+            assert tuple(dev["rec"][c, 4 + 8 * pos:12 + 8 * pos]) == want["pieces"][pbase + pos][0] + \
+                want["pieces"][pbase + pos][1]
+        if np_:
+            assert dev["rec"][c, 20:20 + NC[d] * STAGES[d]].tolist() == want["rows0"][c], c
+    got_pieces = [tuple(map(int, r[:4])) + tuple(map(int, r[4:])) for r in dev["desc"]]
+    assert got_pieces == [a + b for a, b in want["pieces"]]
+    assert dev["rows"].tolist() == [want["rows"][i] for i in range(want["T"])]
+    SM.check_bounds(want, SM.sched_layout(spec.num_seqs, kh, hg, spec.max_blocks, 16, _ctas())["max_tiles"],
+                    SM.sched_layout(spec.num_seqs, kh, hg, spec.max_blocks, 16, _ctas())["max_pieces"], _ctas(),
+                    NC[d], STAGES[d])
+    return want
 
 
 @pytest.mark.parametrize("num_seqs,heads", [(256, (14, 2)), (7, (14, 2)), (96, (32, 8)), (3, (40, 2))])
-def test_schedule_lists_every_tile_once(num_seqs, heads):
+def test_schedule_matches_the_cpu_restatement(num_seqs, heads):
     h, kh = heads
     d = 128 if kh == 8 else 64
     ctx = W.context_lengths(2, seed=num_seqs, num_seqs=num_seqs)
@@ -76,69 +102,54 @@ def test_schedule_lists_every_tile_once(num_seqs, heads):
         ctx[:] = [1, 20000, 33]
     spec = W.build_spec("s", ctx, h, kh, d, 16, seed=1)
     t = W.torch_tensors(spec, torch.bfloat16, DEV)
-    sched = M.build_decode_schedule(t["kv_len"], h, kh, d, 16, spec.num_blocks, spec.max_blocks, torch.bfloat16)
+    sched = M.build_decode_schedule(t["kv_len"], t["block_tables"], h, kh, d, 16, spec.num_blocks, torch.bfloat16)
     torch.cuda.synchronize()
-    hdr, desc = read_schedule(sched)
-    hg = -(-(h // kh) // 16)
-    ctas = torch.cuda.get_device_properties(0).multi_processor_count
-    want, piece = restated_pieces([int(c) for c in ctx], kh * hg, 16, spec.max_blocks, ctas)
-    assert hdr[1] == piece and hdr[2] == 0 and hdr[3] == 0  # hand-out counters at rest
-    got = {}
-    sizes = []
-    for i, (s, k, b0, nt, first, p, c, _flag) in enumerate(desc.tolist()):
-        assert first <= i < first + p and c == ctx[s]
-        assert 0 <= nt <= MAX_PIECE
-        got.setdefault((s, k), []).append((b0, nt, i - first))
-        sizes.append(nt)
-    assert sorted(got) == sorted(want)
-    for key, pieces in got.items():
-        pieces.sort(key=lambda x: x[2])
-        assert [(b, n) for b, n, _ in pieces] == want[key], key
-    # longest first: the list's piece sizes never grow by more than the one
-    # tile an even split allows between pieces of one unit
-    assert all(b <= a + 1 for a, b in zip(sizes, sizes[1:]))
+    check_schedule(read_schedule(sched, spec, h, kh, d), spec, h, kh, d)
 
 
 def test_one_schedule_serves_every_layer():
     spec = W.make_spec(2, seed=40)
     t = W.torch_tensors(spec, torch.bfloat16, DEV, num_layers=3)
-    sched = M.build_decode_schedule(t["kv_len"], 14, 2, 64, 16, spec.num_blocks, spec.max_blocks, torch.bfloat16)
+    sched = M.build_decode_schedule(t["kv_len"], t["block_tables"], 14, 2, 64, 16, spec.num_blocks, torch.bfloat16)
     for layer in range(3):
         out = M.paged_decode_attention(t["query"], t["key_caches"][layer], t["value_caches"][layer],
                                        t["block_tables"], t["kv_len"], 16, schedule=sched)
         close(out, ref_decode(spec, t, t["key_caches"][layer], t["value_caches"][layer]), f"layer {layer}")
-        hdr, _ = read_schedule(sched)
-        assert hdr[2] == 0 and hdr[3] == 0  # the last CTA reset the counters
+        assert (read_schedule(sched, spec, 14, 2, 64)["ucnt"] == 0).all()  # the last arrivals reset them
 
 
 @pytest.mark.parametrize("num_seqs", [1, 2, 3, 8, 37, 148, 300, 1500, 5000])
 def test_batch_sizes(num_seqs):
-    """From one sequence (each unit cut into 4-tile pieces across the GPU) to
-    thousands (many pieces per CTA), twice in a row (the counters the first
-    call left at zero)."""
+    """From one sequence (its units cut across the whole GPU) to thousands
+    (many pieces per CTA), twice in a row (the counters the first call left at
+    zero)."""
     ctx = W.context_lengths(2, seed=num_seqs, num_seqs=num_seqs)
     if num_seqs <= 3:
         ctx[:] = [3000, 1, 77][:num_seqs]
     spec = W.build_spec("b", ctx, 14, 2, 64, 16, seed=num_seqs)
     t = W.torch_tensors(spec, torch.bfloat16, DEV)
     ref = ref_decode(spec, t)
+    outs = []
     for _ in range(2):
         out = M.paged_decode_attention(t["query"], t["key_caches"][0], t["value_caches"][0], t["block_tables"],
                                        t["kv_len"], 16, variant="sched")
         close(out, ref, f"n={num_seqs}")
+        outs.append(out)
+    assert torch.equal(outs[0], outs[1])  # fixed work split: the same bits every time
 
 
 @pytest.mark.parametrize("head_dim,heads,kv_heads", [(64, 14, 2), (128, 32, 8)])
-def test_long_units_many_pieces(head_dim, heads, kv_heads):
-    """Units thousands of tiles long: each is cut into more pieces than a warp
-    has lanes, merged in rounds of 32 by the last piece to arrive."""
+def test_long_units_many_ctas(head_dim, heads, kv_heads):
+    """Units thousands of tiles long: each spans many CTAs, and the last of
+    its pieces to arrive merges them (in rounds of 4 partial states)."""
     ctx = np.array([40000, 5, 30001, 17], np.int64)
     spec = W.build_spec("long", ctx, heads, kv_heads, head_dim, 16, seed=41)
     t = W.torch_tensors(spec, torch.bfloat16, DEV)
-    sched = M.build_decode_schedule(t["kv_len"], heads, kv_heads, head_dim, 16, spec.num_blocks, spec.max_blocks,
+    sched = M.build_decode_schedule(t["kv_len"], t["block_tables"], heads, kv_heads, head_dim, 16, spec.num_blocks,
                                     torch.bfloat16)
-    _, desc = read_schedule(sched)
-    assert desc[:, 5].max() > 32
+    dev = read_schedule(sched, spec, heads, kv_heads, head_dim)
+    want = check_schedule(dev, spec, heads, kv_heads, head_dim)
+    assert max(d1[3] >> 1 for _, d1 in want["pieces"]) > 4
     ref = ref_decode(spec, t)
     for _ in range(2):
         out = M.paged_decode_attention(t["query"], t["key_caches"][0], t["value_caches"][0], t["block_tables"],
@@ -167,7 +178,7 @@ def test_write_then_decode_with_a_schedule(num_seqs):
     The new tokens dominate attention (K = 4, V = 3), so a decode that read
     the cache before the write landed would be far off."""
     spec, t, ref = _write_then_decode_case(33, num_seqs)
-    sched = M.build_decode_schedule(t["kv_len"], 14, 2, 64, 16, spec.num_blocks, spec.max_blocks, torch.bfloat16)
+    sched = M.build_decode_schedule(t["kv_len"], t["block_tables"], 14, 2, 64, 16, spec.num_blocks, torch.bfloat16)
     outs = []
     for _ in range(3):
         kc, vc = t["key_caches"][0].clone(), t["value_caches"][0].clone()
@@ -182,14 +193,15 @@ def test_write_then_decode_with_a_schedule(num_seqs):
     # the inline form (schedule built inside the call, after the write) agrees bit for bit
     kc, vc = t["key_caches"][0].clone(), t["value_caches"][0].clone()
     M.paged_cache_write(t["new_key"], t["new_value"], kc, vc, t["slot_mapping"], 16)
-    o = M.paged_decode_attention(t["query"], kc, vc, t["block_tables"], t["kv_len"], 16, after_write=True)
+    o = M.paged_decode_attention(t["query"], kc, vc, t["block_tables"], t["kv_len"], 16, after_write=True,
+                                 variant="sched")
     assert torch.equal(o, outs[0])
 
 
 def test_backend_builds_the_schedule_once_per_step():
     spec, t, ref = _write_then_decode_case(34, 64)
     backend = M.AttentionBackendB200(M.ModelConfig(num_heads=14, num_kv_heads=2, head_dim=64), strict=True,
-                                     overlap_after_write=True)
+                                     overlap_after_write=True, decode_variant="sched")
     L = 3
     kcs = [t["key_caches"][0].clone() for _ in range(L)]
     vcs = [t["value_caches"][0].clone() for _ in range(L)]
@@ -229,7 +241,8 @@ def test_two_streams_at_once():
             with torch.cuda.stream(streams[i]):
                 t = ts[i]
                 outs[i].append(M.paged_decode_attention(t["query"], t["key_caches"][0], t["value_caches"][0],
-                                                        t["block_tables"], t["kv_len"], 16, strict=False))
+                                                        t["block_tables"], t["kv_len"], 16, strict=False,
+                                                        variant="sched"))
     torch.cuda.synchronize()
     M.check_device_errors()
     for i in range(2):
@@ -246,7 +259,7 @@ def test_bad_sequences_get_zero_rows_and_raise():
     kvl[1] = 0
     out = torch.full_like(t["query"], 5.0)
     M.paged_decode_attention(t["query"], t["key_caches"][0], t["value_caches"][0], t["block_tables"], kvl, 16,
-                             out=out, strict=False)
+                             out=out, strict=False, variant="sched")
     with pytest.raises(ValueError, match="kv_len"):
         M.check_device_errors()
     assert (out[1] == 0).all()

@@ -78,11 +78,14 @@ def test_plan_headline_config_uses_the_stream_kernel():
 def test_plan_scheduled_kernel_when_asked():
     p = _plan(variant="sched")
     assert p["variant"] == "sched" and p["num_partitions"] == 0
-    # header + per chunk: a 32-byte descriptor, an arrival counter and a partial
-    # state of 7 head rows x (64 + 4) floats, for the bound of
-    # max(512 units x 4 pieces, 2 x 148 CTAs) + 512 chunks
-    chunks = max(512 * 4, 2 * 148) + 512
-    assert p["workspace_bytes"] >= 256 + chunks * (32 + 4 + 7 * 68 * 4)
+    # header, a 256-byte record per CTA (148 SMs without a GPU), 512 units + 148
+    # pieces, 512 units x 128 tiles of rows, 256 left-out slots, 148 counters,
+    # and two partial states of 7 head rows x (64 + 4) floats per CTA
+    import sched_model
+
+    lay = sched_model.sched_layout(256, 2, 1, 128, 16, 148, G=7, head_dim=64)
+    assert p["workspace_bytes"] == lay["bytes"]
+    assert lay["bytes"] >= 256 + 148 * 256 + 660 * 32 + 65536 * 4 + 256 * 4 + 148 * 4 + 296 * 7 * 68 * 4
 
 
 def test_plan_stream_kernel_when_asked():
@@ -169,16 +172,21 @@ def test_decode_host_checks_without_gpu():
 def test_schedule_host_checks_without_gpu():
     lib = _native.lib()
 
-    def call(num_seqs, kv_len=None, ws=None, wsb=0, flags=0, dtype=_native.DTYPE_BF16, err=None):
-        return lib.mvb_paged_decode_schedule(kv_len, num_seqs, 14, 2, 64, 16, 100, 8, dtype, flags, ws, wsb,
-                                             err, None)
+    def call(num_seqs, kv_len=None, bt=None, bt_stride=8, ws=None, wsb=0, flags=0, dtype=_native.DTYPE_BF16,
+             err=None):
+        return lib.mvb_paged_decode_schedule(kv_len, bt, bt_stride, num_seqs, 14, 2, 64, 16, 100, 8, dtype, flags,
+                                             ws, wsb, err, None)
 
     assert call(0) == _native.OK  # empty batch: nothing launched
     assert call(1) == _native.ERR_INVALID_ARG  # null kv_len
+    assert call(1, kv_len=16, err=16) == _native.ERR_INVALID_ARG  # null block table
+    assert call(1, kv_len=16, bt=16, bt_stride=4, err=16) == _native.ERR_INVALID_ARG  # rows shorter than 8 blocks
     assert call(1, dtype=_native.DTYPE_F32) == _native.ERR_VARIANT  # the scheduled kernel is bf16 / f16 only
-    assert call(1, kv_len=16, err=16, flags=0x400) == _native.ERR_INVALID_ARG  # unknown flag
-    assert call(1, kv_len=16, err=16) == _native.ERR_WORKSPACE  # no workspace
-    assert call(1, kv_len=16, err=16, ws=256 * 7 + 16, wsb=1 << 30) == _native.ERR_WORKSPACE  # misaligned
+    assert call(1, kv_len=16, bt=16, err=16, flags=0x400) == _native.ERR_INVALID_ARG  # unknown flag
+    assert call(1, kv_len=16, bt=16, err=16) == _native.ERR_WORKSPACE  # no workspace
+    assert call(1, kv_len=16, bt=16, err=16, ws=256 * 7 + 16, wsb=1 << 30) == _native.ERR_WORKSPACE  # misaligned
+    # more sequences than the schedule kernel's prefix arrays hold: the plan refuses the variant
+    assert call(16385, kv_len=16, bt=16, err=16) == _native.ERR_VARIANT
 
 
 def test_direct_binding_loads_and_routes_cpu_tensors_to_the_full_path():
