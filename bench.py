@@ -75,9 +75,17 @@ def parse_args():
     p.add_argument("--partition-tokens", type=int, default=0)
     p.add_argument("--e2e-steps", type=int, default=1200)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-config4", action="store_true", help="skip the config-4 strong-scaling sub-object")
     p.add_argument("--seed", type=int, default=0)
-    p.add_argument("--op", choices=["step", "gather", "rope_write", "metadata"], default="step",
-                   help="step: the decode step (the headline); gather: the prefill prefix gather "
+    p.add_argument("--requests", type=int, default=256, help="--op engine: requests per replica")
+    p.add_argument("--op", choices=["step", "gather", "rope_write", "metadata", "sweep", "engine", "profile"],
+                   default="step",
+                   help="step: the decode step (the headline); sweep: decode time per launch of every "
+                        "kernel over batch x context (the plan's crossover table); engine: continuous-batching "
+                        "serving in the reference's own engine (config 5, bounded: --requests per replica; "
+                        "--impl reference runs the reference's GPU backend); profile: a few KV writes and "
+                        "decodes of --variant on --config over --layers pools, untimed (the case ncu captures); "
+                        "gather: the prefill prefix gather "
                         "(mvb_paged_gather) of every config-2 context; rope_write: the fused RoPE + "
                         "KV write (mvb_rope_kv_cache_write) of an 8192-token prefill chunk; metadata: "
                         "the per-step attention metadata of a config-2 decode step (StepMetadataBuilder)")
@@ -631,6 +639,10 @@ def ours(args, rank, world, local_rank):
                 "sample": f"the reference's own AttentionBackendRef.write_kv_cache + decode_attention "
                           f"(baseline/_ref, bf16 CPU tensors) on the full {spec.name} step, median of {rrep}"}
 
+    c4 = None
+    if args.config == 2 and not args.no_config4:
+        c4 = config4_strong(args, rank, world, dev, peak)
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value_gbs, 2), "unit": "GB/s", "n_gpus": world,
@@ -665,9 +677,123 @@ def ours(args, rank, world, local_rank):
                     "decode_tok_s": round(seqs_all / e2e_sec, 1)},
             "gpu_launches": K * per_layer + (-(-K // L) if scheduled else 0),
             "clocks": clocks.summary(),
+            "config4": c4,
         }
         print(json.dumps(line), flush=True)
     del g_full, g_rem, g_dec  # release graphs holding NCCL work before the group is destroyed
+
+
+def config4_strong(args, rank, world, dev, peak):
+    """BASELINE config 4 as strong scaling, for the same JSON line at every N:
+    the global batch of 1024 sequences (32 q / 8 KV heads, head_dim 128,
+    lognormal(7, 0.8) contexts in [16, 8192], block 16, bf16) sharded by
+    sequence with the token-balanced snake assignment; each rank decodes its
+    shard against its own pools, and the outputs are all-gathered in global
+    order (NCCL all_gather_into_tensor + index_copy_).  Timed per rank as CUDA
+    graphs of L back-to-back launches (decode alone, gather alone, decode then
+    gather), median of repeats, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    import mini_vllm_b200 as M
+    from mini_vllm_b200 import sharding
+    from mini_vllm_b200 import workloads as W
+
+    L = 2  # distinct pools (each shard's K/V is several GB at small N: no L2 reuse between launches)
+    ctx_all = W.context_lengths(4, seed=args.seed)
+    owned_all = sharding.snake_assignment(ctx_all, world)
+    owned = owned_all[rank]
+    c = W.CONFIGS[4]
+    spec = W.build_spec("config4-shard", ctx_all[owned], c["num_heads"], c["num_kv_heads"], c["head_dim"],
+                        c["block_size"], seed=args.seed + 101 * rank)
+    t = W.torch_tensors(spec, torch.bfloat16, dev, num_layers=L)
+    q, bt, kvl = t["query"], t["block_tables"], t["kv_len"]
+    kcs, vcs = t["key_caches"], t["value_caches"]
+    out = torch.empty_like(q)
+    gather = sharding.OutputGather(owned_all, spec.num_heads, spec.head_dim, torch.bfloat16, dev) if world > 1 else None
+    plan = M.decode_plan(spec.num_seqs, spec.num_heads, spec.num_kv_heads, spec.head_dim, 16, spec.num_blocks,
+                         spec.max_blocks, torch.bfloat16, "auto")
+
+    def decodes():
+        for layer in range(L):
+            M.paged_decode_attention(q, kcs[layer], vcs[layer], bt, kvl, 16, out=out, strict=False)
+
+    def gathers():
+        for _ in range(L):
+            if gather is not None:
+                gather(out)
+
+    def both():
+        for layer in range(L):
+            M.paged_decode_attention(q, kcs[layer], vcs[layer], bt, kvl, 16, out=out, strict=False)
+            if gather is not None:
+                gather(out)
+
+    decodes()
+    gathers()
+    torch.cuda.synchronize()
+    M.check_device_errors(dev)
+
+    def time_graph(fn):
+        s2 = torch.cuda.Stream(device=dev)
+        s2.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s2):
+            fn()
+        torch.cuda.current_stream(dev).wait_stream(s2)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        samples = []
+        for _ in range(20):
+            e0.record()
+            g.replay()
+            e1.record()
+            e1.synchronize()
+            samples.append(e0.elapsed_time(e1) / 1e3 / L)
+        del g
+        v = statistics.median(samples)
+        if world > 1:
+            tt = torch.tensor([v], device=dev, dtype=torch.float64)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            v = float(tt.item())
+        return v
+
+    dec_s = time_graph(decodes)
+    own_dec_s = dec_s
+    gat_s = time_graph(gathers) if world > 1 else 0.0
+    both_s = time_graph(both) if world > 1 else dec_s
+    # per-rank figures
+    by = spec.decode_bytes(2)
+    vals = torch.tensor([by, spec.num_seqs, spec.total_tokens], device=dev, dtype=torch.float64)
+    allv = [torch.zeros_like(vals) for _ in range(world)] if world > 1 else [vals]
+    if world > 1:
+        dist.all_gather(allv, vals)
+    toks = [float(v[2]) for v in allv]
+    res = {
+        "workload": "config4: global batch 1024, 32q/8kv/d128, ctx lognormal(7,0.8) in [16,8192], block 16, bf16, "
+                    "snake-sharded by sequence",
+        "scaling": "strong", "global_batch": int(ctx_all.size), "kernel": plan["variant"],
+        "decode_us_max_rank": round(dec_s * 1e6, 2), "gather_us": round(gat_s * 1e6, 2),
+        "decode_then_gather_us": round(both_s * 1e6, 2),
+        "decode_tok_s_no_gather": round(ctx_all.size / dec_s, 1),
+        "decode_tok_s_with_gather": round(ctx_all.size / both_s, 1),
+        "aggregate_GBps_no_gather": round(sum(float(v[0]) for v in allv) / dec_s / 1e9, 1),
+        "rank0_GBps": round(by / own_dec_s / 1e9, 1),
+        "rank0_frac": round(by / own_dec_s / 1e9 / peak, 4),
+        "tokens_per_rank_max_over_mean": round(max(toks) / (sum(toks) / len(toks)), 4),
+        "seqs_per_rank": [int(v[1]) for v in allv],
+        "timing": f"CUDA graphs of {L} launches, events, median of 20 replays, max over ranks",
+    }
+    del t, q, bt, kvl, kcs, vcs, out
+    torch.cuda.empty_cache()
+    return res
 
 
 def physical_gpu(local_rank: int) -> str:
@@ -910,6 +1036,228 @@ def rope_write_op(args):
     }), flush=True)
 
 
+def sweep_op(args):
+    """Secondary measurement: the decode kernels over batch x context, the
+    table behind the plan's kernel choice (make_plan in csrc/capi.cu).  Each
+    case is the Qwen2-0.5B attention shape (14 q / 2 KV heads, head_dim 64,
+    block 16, bf16) with every sequence at the same context length, timed as a
+    CUDA graph of L back-to-back decodes over L distinct pools (median over
+    repeats, per launch).  Kernels: "stream" (persistent stream-K + fixup),
+    "sched" (scheduled persistent, its per-step schedule built once outside the
+    timed graph), "mma" unsplit (one CTA per (sequence, KV head)), "mma" split
+    into 512-token partitions plus the reduction, "fma" (CUDA cores, the plan's
+    partitions), and "auto" (the plan's choice).  One JSON line per case."""
+    import torch
+
+    import mini_vllm_b200 as M
+    from mini_vllm_b200 import workloads as W
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    L = min(args.layers, 8)
+    batches = [1, 4, 8, 32, 64, 256]
+    contexts = [128, 1024, 8192]
+    for ctx in contexts:
+        for nb in batches:
+            spec = W.build_spec(f"sweep{nb}x{ctx}", np.full(nb, ctx, np.int64), 14, 2, 64, 16, seed=args.seed)
+            t = W.torch_tensors(spec, torch.bfloat16, dev, num_layers=L)
+            q, bt, kvl = t["query"], t["block_tables"], t["kv_len"]
+            kcs, vcs = t["key_caches"], t["value_caches"]
+            out = torch.empty_like(q)
+            sched = M.build_decode_schedule(kvl, bt, 14, 2, 64, 16, spec.num_blocks, torch.bfloat16)
+            kinds = [("stream", "stream", None, None), ("sched", "sched", None, sched),
+                     ("mma_unsplit", "mma", spec.max_blocks * 16, None), ("mma_split512", "mma", 512, None),
+                     ("fma", "fma", None, None), ("auto", "auto", None, None)]
+            res = {"batch": nb, "ctx": ctx}
+            for name, variant, pt, sc in kinds:
+                def launches():
+                    for layer in range(L):
+                        M.paged_decode_attention(q, kcs[layer], vcs[layer], bt, kvl, 16, out=out, variant=variant,
+                                                 partition_tokens=pt, strict=False, schedule=sc)
+                launches()
+                torch.cuda.synchronize()
+                M.check_device_errors(dev)
+                s2 = torch.cuda.Stream(device=dev)
+                s2.wait_stream(torch.cuda.current_stream(dev))
+                with torch.cuda.stream(s2):
+                    launches()
+                torch.cuda.current_stream(dev).wait_stream(s2)
+                torch.cuda.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    launches()
+                for _ in range(3):
+                    g.replay()
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                samples = []
+                for _ in range(30):
+                    e0.record()
+                    g.replay()
+                    e1.record()
+                    e1.synchronize()
+                    samples.append(e0.elapsed_time(e1) * 1e3 / L)
+                res[name + "_us"] = round(statistics.median(samples), 2)
+                del g
+            plan = M.decode_plan(nb, 14, 2, 64, 16, spec.num_blocks, spec.max_blocks, torch.bfloat16, "auto")
+            res["auto_plan"] = plan["variant"] + (f"/{plan['num_partitions']}p" if plan["num_partitions"] else "")
+            res["kv_MB"] = round(spec.kv_bytes(2) / 1e6, 3)
+            print(json.dumps(res), flush=True)
+            del t, q, bt, kvl, kcs, vcs, out, sched
+            torch.cuda.empty_cache()
+
+
+def profile_op(args):
+    """The case an ncu capture runs: for each of --layers pools, one KV write
+    and one decode of --variant (with --partition-tokens) on --config, twice
+    over, untimed; the scheduled kernel's schedule is built once first.
+    Captures pick the kernel with -k and skip the first round with -s."""
+    import torch
+
+    import mini_vllm_b200 as M
+    from mini_vllm_b200 import workloads as W
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    spec, _ = rank_spec(args.config, 0, 1, args.seed)
+    L = args.layers
+    t = W.torch_tensors(spec, torch.bfloat16, dev, num_layers=L)
+    q, nk, nv = t["query"], t["new_key"], t["new_value"]
+    bt, kvl, slots = t["block_tables"], t["kv_len"], t["slot_mapping"]
+    out = torch.empty_like(q)
+    pt = args.partition_tokens or None
+    plan = M.decode_plan(spec.num_seqs, spec.num_heads, spec.num_kv_heads, spec.head_dim, spec.block_size,
+                         spec.num_blocks, spec.max_blocks, torch.bfloat16, args.variant, pt)
+    sched = None
+    if plan["variant"] == "sched":
+        sched = M.build_decode_schedule(kvl, bt, spec.num_heads, spec.num_kv_heads, spec.head_dim,
+                                        spec.block_size, spec.num_blocks, torch.bfloat16)
+    for _ in range(2):
+        for layer in range(L):
+            M.paged_cache_write(nk, nv, t["key_caches"][layer], t["value_caches"][layer], slots, spec.block_size,
+                                strict=False, check_duplicates=False)
+            M.paged_decode_attention(q, t["key_caches"][layer], t["value_caches"][layer], bt, kvl, spec.block_size,
+                                     out=out, variant=args.variant, partition_tokens=pt, strict=False,
+                                     schedule=sched)
+    torch.cuda.synchronize()
+    M.check_device_errors(dev)
+    print(json.dumps({"op": "profile", "config": args.config, "plan": plan, "layers": L,
+                      "decode_bytes": spec.decode_bytes(2), "write_bytes": spec.write_bytes(2)}), flush=True)
+
+
+def engine_op(args):
+    """BASELINE config 5, bounded: continuous-batching serving in the
+    reference's own engine (LLMEngine -> EngineCore -> Scheduler / BlockManager
+    / ModelInputBuilder -> PagedExecutor -> QwenModelRunner, installed from
+    baseline/_ref), one replica per GPU, on a random-init Qwen2-0.5B (24
+    layers, hidden 896, 14/2 heads of 64, MLP 4864, vocab 151936, weights
+    N(0, 0.02), written to a temporary checkpoint).  Requests: --requests per
+    replica with prompt token ids uniform over the vocabulary, prompt lengths
+    U[32, 1024], max_tokens U[64, 512], Poisson arrivals at 64 req/s, greedy
+    sampling.  Our arm serves attention with AttentionBackendB200 (the "b200"
+    branch of AttentionBackend.create); --impl reference serves it with the
+    reference's own GPU backend ("triton", its default).  Metric: generated
+    tokens per second of wall time from the first arrival to the last
+    completion (aggregate over replicas), plus the per-step decode latency."""
+    import tempfile
+
+    import torch
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    from mini_vllm_b200 import reference_engine as RE
+
+    try:
+        RE.import_reference()
+    except ImportError as e:
+        if rank == 0:
+            print(json.dumps({"impl": args.impl, "op": "engine", "unavailable": str(e).splitlines()[0]}))
+        return
+    backend = "b200" if args.impl == "ours" else "triton"
+    RE.register_backend(overlap_after_write=True, strict=False)
+    from mini_vllm.config import Config
+    from mini_vllm.engine.engine import LLMEngine
+
+    ckpt = tempfile.mkdtemp(prefix=f"mvb_qwen2_{rank}_")
+    RE.write_random_checkpoint(ckpt, seed=1)
+    vocab = RE.QWEN2_0_5B["vocab_size"]
+    rng = np.random.default_rng(args.seed + 1000 * rank)
+    n = args.requests
+    plen = rng.integers(32, 1025, n)
+    maxt = rng.integers(64, 513, n)
+    arrive = np.cumsum(rng.exponential(1.0 / 64.0, n))
+    prompts = [RE.prompt_text(rng.integers(0, vocab, int(k))) for k in plen]
+    cfg = Config(executor_type="paged", attention_backend=backend, model_path=ckpt, device=f"cuda:{local_rank}",
+                 block_size=16, num_gpu_blocks=16384, max_num_seqs=128, max_num_batched_tokens=2048,
+                 max_num_prefill_tokens=2048, max_prefill_chunk_size=512, max_model_len=2048,
+                 max_queue_len=1 << 20, request_timeout_s=1e9, print_step_events=False,
+                 enable_prefix_caching=False)
+    eng = LLMEngine(cfg)
+    # warm-up: a few short requests through every path (prefill chunks, decode)
+    for i in range(4):
+        eng.add_request(prompts[i], max_new_tokens=8)
+    eng.run_until_done()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    steps, decode_steps, decode_s = 0, 0, 0.0
+    t0 = time.perf_counter()
+    nxt = 0
+    while True:
+        now = time.perf_counter() - t0
+        while nxt < n and arrive[nxt] <= now:
+            eng.add_request(prompts[nxt], max_new_tokens=int(maxt[nxt]))
+            nxt += 1
+        q = eng.queue
+        if q.num_waiting == 0 and q.num_running == 0:
+            if nxt >= n:
+                break
+            time.sleep(max(0.0, arrive[nxt] - now))
+            continue
+        ts = time.perf_counter()
+        res = eng.step()
+        steps += 1
+        if not res.scheduled_prefill_groups and res.scheduled_decode_groups:
+            decode_steps += 1
+            decode_s += time.perf_counter() - ts
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    outs = eng.get_outputs()
+    gen = int(sum(int(m) for m in maxt))  # greedy runs every request to max_tokens (no EOS in the id vocabulary)
+    stats = torch.tensor([gen, len(outs) - 4, steps], dtype=torch.float64, device=dev)  # minus the warm-up ones
+    wall_t = torch.tensor([wall], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(stats)
+        dist.all_reduce(wall_t, op=dist.ReduceOp.MAX)
+    if rank == 0:
+        tok_s = float(stats[0]) / float(wall_t[0])
+        line = {"metric": "config-5 engine decode tok/s (reference engine, random-init Qwen2-0.5B)",
+                "value": round(tok_s, 1), "unit": "tok/s", "n_gpus": world, "impl": args.impl,
+                "attention_backend": type(eng._executor._attention_backend).__name__,
+                "requests": int(stats[1]), "requests_per_replica": n, "generated_tokens": int(stats[0]),
+                "wall_s": round(float(wall_t[0]), 3), "engine_steps": int(stats[2]),
+                "rank0_decode_only_steps": decode_steps,
+                "rank0_decode_step_ms": round(1e3 * decode_s / max(1, decode_steps), 3),
+                "higher_is_better": True, "scaling": "weak", "data": "synthetic",
+                "config": {"workload": "config5: reference LLMEngine, random-init Qwen2-0.5B (24 layers), "
+                                       "prompts U[32,1024], max_tokens U[64,512], Poisson 64 req/s, greedy",
+                           "engine": {"block_size": 16, "num_gpu_blocks": 16384, "max_num_seqs": 128,
+                                      "max_num_batched_tokens": 2048, "max_prefill_chunk_size": 512},
+                           "parallelism": f"{world} replicas"}}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def metadata_op(args):
     """Secondary measurement: StepMetadataBuilder.build for one config-2 decode
     step (256 sequences, ctx U[128,2048], block 16: positions, slot mapping,
@@ -982,6 +1330,15 @@ def main():
         return
     if args.op == "rope_write":
         rope_write_op(args)
+        return
+    if args.op == "sweep":
+        sweep_op(args)
+        return
+    if args.op == "engine":
+        engine_op(args)
+        return
+    if args.op == "profile":
+        profile_op(args)
         return
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -62,7 +62,10 @@ extern "C" {
                                      (internal: the planned bound was wrong)   */
 
 /* ---- decode kernel variants --------------------------------------------- */
-#define MVB_DECODE_AUTO 0  /* STREAM when eligible, else SCHED, else FMA          */
+#define MVB_DECODE_AUTO 0  /* bf16/f16, BS%16==0: MMA unsplit for contexts <= 256
+                              tokens, MMA split-K when its 512-token partitions fill
+                              at most 2 CTAs per SM, else STREAM (<= 4096 sequences),
+                              else SCHED; FMA for everything else                   */
 #define MVB_DECODE_FMA  1  /* CUDA-core FP32 FMA kernel (any dtype, any BS)      */
 #define MVB_DECODE_MMA  2  /* TMA-staged tensor-core kernel, one CTA per (seq, KV head),
                               split-K + reduction for long contexts (bf16/f16, BS%16==0) */

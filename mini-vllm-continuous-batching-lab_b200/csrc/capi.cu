@@ -55,6 +55,8 @@ constexpr int kAbiVersion = 4;
 constexpr int64_t kUnsplitMaxTokens = 8192;
 // Split-K partition length of the auto plan (the north-star's 512 tokens).
 constexpr int kAutoPartitionTokens = 512;
+// AUTO: contexts up to this many tokens run one CTA per (sequence, KV head, head group), unsplit.
+constexpr int64_t kAutoShortTokens = 256;
 // Largest partition an MMA CTA accepts (bounds its block-id cache).
 constexpr int kMmaMaxPartitionTokens = 65536;
 constexpr int kMmaHeadGroup = 16;
@@ -134,9 +136,29 @@ int make_plan(int num_seqs, int num_heads, int num_kv_heads, int head_dim, int b
                                 sm_count_current());
   const bool sched_ok = mma_ok && sl.ok;
   int v = variant;
-  // AUTO: the stream kernel where it applies (measured fastest at configs 2-4),
-  // else the scheduled kernel (any batch size), else CUDA cores
-  if (v == MVB_DECODE_AUTO) v = stream_ok ? MVB_DECODE_STREAM : sched_ok ? MVB_DECODE_SCHED : MVB_DECODE_FMA;
+  // AUTO, from the batch x context sweep (bench.py --op sweep, 14/2/64 bf16):
+  //  * contexts of at most kAutoShortTokens: one CTA per (sequence, KV head,
+  //    head group), unsplit (5.6 us at 1-64 sequences of 128 tokens, where the
+  //    persistent kernels' fixed cost is 8-12 us);
+  //  * little work: 512-token split-K partitions of at most 2 CTAs per SM
+  //    (15.5 us for 1 x 8192 tokens against 58 us streamed through the
+  //    whole GPU);
+  //  * else the stream kernel where it applies (fastest at configs 2-4), the
+  //    scheduled kernel past its batch limit, CUDA cores for the rest.
+  int64_t auto_pt = 0;
+  if (v == MVB_DECODE_AUTO) {
+    const int64_t max_ctx_tok = (int64_t)max_blocks * block_size;
+    const int64_t split_ctas = (int64_t)num_seqs * khg16 * ((max_ctx_tok + kAutoPartitionTokens - 1) / kAutoPartitionTokens);
+    if (mma_ok && max_ctx_tok <= kAutoShortTokens) {
+      v = MVB_DECODE_MMA;
+      auto_pt = max_ctx_tok > 0 ? max_ctx_tok : 16;
+    } else if (mma_ok && split_ctas <= 2 * (int64_t)sm_count_current()) {
+      v = MVB_DECODE_MMA;
+      auto_pt = kAutoPartitionTokens;
+    } else {
+      v = stream_ok ? MVB_DECODE_STREAM : sched_ok ? MVB_DECODE_SCHED : MVB_DECODE_FMA;
+    }
+  }
   if (v != MVB_DECODE_FMA && v != MVB_DECODE_MMA && v != MVB_DECODE_STREAM && v != MVB_DECODE_SCHED)
     return MVB_ERR_VARIANT;
   if (v == MVB_DECODE_MMA && !mma_ok) return MVB_ERR_VARIANT;
@@ -192,6 +214,8 @@ int make_plan(int num_seqs, int num_heads, int num_kv_heads, int head_dim, int b
   int64_t pt;
   if (partition_tokens > 0) {
     pt = partition_tokens;
+  } else if (auto_pt > 0) {
+    pt = auto_pt;
   } else {
     const int64_t ctas = (int64_t)num_seqs * num_kv_heads * head_groups;
     if (max_ctx <= kUnsplitMaxTokens && ctas >= 2 * (int64_t)sm_count_current())

@@ -48,6 +48,9 @@ def stream_copy(dst: torch.Tensor, src: torch.Tensor, stream: torch.cuda.Stream,
         raise ValueError("stream_copy copies between host and device memory: exactly one tensor must be on the GPU")
     if not (dst.is_contiguous() and src.is_contiguous()):
         raise ValueError("stream_copy needs contiguous tensors")
+    dev = dst.device if dst.is_cuda else src.device
+    if stream.device != dev:
+        raise ValueError(f"stream_copy: the device tensor is on {dev} but the stream belongs to {stream.device}")
     nbytes = dst.numel() * dst.element_size()
     if nbytes != src.numel() * src.element_size():
         raise ValueError(f"stream_copy size mismatch: {nbytes} vs {src.numel() * src.element_size()} bytes")

@@ -15,7 +15,7 @@ keep the test short; weights ~ N(0, 0.02)) serves the same requests on two
 engines, one with the reference's torch backend ("reference") and one with
 "b200".  Chunked prefill (64-token chunks over prompts of up to 300 tokens)
 reads cached prefixes through the gather kernel, and every decode step runs
-the scheduled decode kernel.  Every step's logits must agree within
+the kernel the plan picks for its batch.  Every step's logits must agree within
 LOGIT_ATOL row by row (rows are sequences), and the greedy tokens must agree
 wherever the reference's top-2 margin exceeds twice that bound.  Where the
 margin is smaller (a near-tie: random weights make logits of ~8k tokens

@@ -75,6 +75,19 @@ def test_plan_headline_config_uses_the_stream_kernel():
     assert _plan()["variant"] == "stream"
 
 
+def test_plan_auto_crossover_from_the_sweep():
+    """AUTO follows the batch x context sweep: short contexts run one CTA per
+    (sequence, KV head) unsplit, little work runs 512-token split-K, the rest
+    streams (148 SMs without a GPU)."""
+    short = _plan(num_seqs=64, max_blocks_per_seq=8)  # 128 tokens
+    assert short["variant"] == "mma" and short["num_partitions"] == 1
+    little = _plan(num_seqs=1, max_blocks_per_seq=512)  # 1 x 8192 tokens: 2 x 16 partitions
+    assert little["variant"] == "mma" and little["partition_tokens"] == 512 and little["num_partitions"] == 16
+    assert _plan(num_seqs=8, max_blocks_per_seq=512)["variant"] == "mma"  # 256 CTAs <= 2 x 148
+    assert _plan(num_seqs=32, max_blocks_per_seq=512)["variant"] == "stream"  # 1024 CTAs
+    assert _plan(num_seqs=5000, max_blocks_per_seq=128)["variant"] == "sched"  # past the stream kernel's batch limit
+
+
 def test_plan_scheduled_kernel_when_asked():
     p = _plan(variant="sched")
     assert p["variant"] == "sched" and p["num_partitions"] == 0

@@ -55,3 +55,13 @@ def test_staging_errors():
         M.staging.stream_copy(torch.zeros(4, device=DEV), torch.zeros(4, device=DEV), side)
     with pytest.raises(ValueError, match="size"):
         M.staging.stream_copy(torch.zeros(4, device=DEV), torch.zeros(8).pin_memory(), side)
+
+
+def test_staging_rejects_a_stream_of_another_device():
+    """The device tensor and the stream must be on the same GPU (checked
+    before any CUDA call: the stream here only claims another device)."""
+    import types
+
+    other = types.SimpleNamespace(device=torch.device("cuda", DEV.index + 1), cuda_stream=0)
+    with pytest.raises(ValueError, match="stream belongs to"):
+        M.staging.stream_copy(torch.zeros(4, device=DEV), torch.zeros(4).pin_memory(), other)

@@ -64,14 +64,29 @@ def test_noalloc_matches_workspace_entry_point_twice(variant, partition_tokens, 
                                    t["kv_len"], spec.block_size, variant=name,
                                    partition_tokens=partition_tokens)
     err = torch.zeros(1, dtype=torch.int32, device=DEV)
-    for _ in range(2):  # the second call finds the first call's partials in the array
-        out = torch.full_like(ref, float("nan"))
-        st = _noalloc(t, spec, out, err, variant, partition_tokens)
-        assert st == _native.OK, _native.status_string(st)
-        torch.cuda.synchronize()
-        assert int(err.item()) == 0
-        _close(out, ref)
-        assert torch.equal(out, ref)  # same kernels, same partitions: the same bits
+    out = torch.full_like(ref, float("nan"))
+    st = _noalloc(t, spec, out, err, variant, partition_tokens)
+    assert st == _native.OK, _native.status_string(st)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    _close(out, ref)
+    assert torch.equal(out, ref)  # same kernels, same partitions: the same bits
+    # The second call finds the first call's partials in the array.  Other
+    # inputs with shorter contexts (fewer partitions per sequence) show that
+    # every partial it reads, it wrote first.
+    ctx2 = np.maximum(1, W.make_spec(2, seed=117, num_seqs=num_seqs).context_lens // 3)
+    spec2 = W.build_spec("short", ctx2, spec.num_heads, spec.num_kv_heads, spec.head_dim, spec.block_size,
+                         seed=117)
+    t2 = W.torch_tensors(spec2, torch.bfloat16, DEV)
+    ref2 = M.paged_decode_attention(t2["query"], t2["key_caches"][0], t2["value_caches"][0], t2["block_tables"],
+                                    t2["kv_len"], spec.block_size, variant=name, partition_tokens=partition_tokens)
+    out2 = torch.full_like(ref2, float("nan"))
+    st = _noalloc(t2, spec2, out2, err, variant, partition_tokens)
+    assert st == _native.OK, _native.status_string(st)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    _close(out2, ref2)
+    assert torch.equal(out2, ref2)
 
 
 def test_noalloc_rejects_shapes_beyond_its_array():
