@@ -109,6 +109,33 @@ int mvb_paged_gather(const void* key_cache, const void* value_cache, const int64
                      int32_t block_size, int32_t num_blocks, int32_t dtype, uint32_t* work_counter,
                      int32_t* error_flags, void* stream);
 
+/* Causal paged prefill attention of a batch of chunks, read in place from the
+ * paged pool on the tensor cores (bf16 / f16, head_dim 64 or 128, any power-of-
+ * two block_size).  Chunk i has query_len[i] query tokens at rows
+ * [sum_{j<i} query_len[j], ...) of `query` (and `out`), the block-table row
+ * seq_rows[i], and cached_len[i] tokens already in the cache before it; its
+ * token t attends cache positions [0, cached_len[i] + t].  Positions before
+ * cached_len[i] are read from the pool; the chunk's own positions from `key` /
+ * `value` ([total_q, KH, D] rows, strides in elements) when given, else from the
+ * pool (the reference's runner writes the chunk into the cache before
+ * attention).  seq_rows / cached_len / query_len are int64 device arrays
+ * (num_chunks <= 4096), so the call needs no host synchronisation; the chunks
+ * must hold at most total_q tokens (else MVB_DEV_BLOCK_ID and no output), and
+ * a chunk whose cache end exceeds max_blocks_per_seq * block_size gets zero
+ * rows and MVB_DEV_TABLE_SHORT.  Replaces AttentionBackendGPU.prefill_attention
+ * (mini_vllm/attention/paged_attention_gpu.py:577-661: per-sequence gather of
+ * the prefix, concatenation with the chunk, GQA repeat and torch SDPA with the
+ * offset causal mask). */
+int mvb_paged_prefill(const void* query, int64_t q_stride_tok, int64_t q_stride_head, const void* key,
+                      int64_t k_stride_tok, int64_t k_stride_head, const void* value, int64_t v_stride_tok,
+                      int64_t v_stride_head, const void* key_cache, const void* value_cache,
+                      const int64_t* block_table, int64_t block_table_rows, int64_t block_table_stride,
+                      int32_t max_blocks_per_seq, const int64_t* seq_rows, const int64_t* cached_len,
+                      const int64_t* query_len, int32_t num_chunks, int32_t total_q, void* out,
+                      int64_t out_stride_tok, int64_t out_stride_head, int32_t num_heads, int32_t num_kv_heads,
+                      int32_t head_dim, int32_t block_size, int32_t num_blocks, float scale, int32_t dtype,
+                      int32_t* error_flags, void* stream);
+
 /* Rotary position embedding of the step's query and key rows fused with the
  * paged KV-cache write of the rotated keys and the values: bit for bit the
  * reference's  q = rope(q, pos); k = rope(k, pos); write_kv_cache(k, v, slots)

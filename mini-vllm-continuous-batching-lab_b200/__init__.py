@@ -20,6 +20,7 @@ from .attention import (
     paged_cache_write,
     paged_decode_attention,
     paged_gather,
+    paged_prefill_attention,
     rope_cache_write,
     rope_tables,
     triton_cache_write,
@@ -53,6 +54,7 @@ __all__ = [
     "paged_cache_write",
     "paged_decode_attention",
     "paged_gather",
+    "paged_prefill_attention",
     "rope_cache_write",
     "rope_tables",
     "triton_cache_write",

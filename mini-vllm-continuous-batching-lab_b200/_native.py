@@ -83,6 +83,11 @@ SIGNATURES = {
         [_vp, _vp, _vp, _i64, _i64, _i32, _vp, _vp, _vp, _vp, _i32, _i64, _i32, _i32, _i32, _i32, _i32,
          _vp, _vp, _vp],
     ),
+    "mvb_paged_prefill": (
+        _i32,
+        [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _i64, _i32, _vp, _vp, _vp, _i32,
+         _i32, _vp, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _vp, _vp],
+    ),
     "mvb_rope_kv_cache_write": (
         _i32,
         [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _i64,

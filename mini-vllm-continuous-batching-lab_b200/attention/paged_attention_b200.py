@@ -663,6 +663,105 @@ def _host_ints(values) -> List[int]:
     return [int(v) for v in values]
 
 
+def paged_prefill_attention(
+    query: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    block_table: torch.Tensor,
+    seq_rows,
+    cached_len: torch.Tensor,
+    query_len: torch.Tensor,
+    block_size: int,
+    *,
+    key: Optional[torch.Tensor] = None,
+    value: Optional[torch.Tensor] = None,
+    scale: Optional[float] = None,
+    out: Optional[torch.Tensor] = None,
+    strict: bool = True,
+) -> torch.Tensor:
+    """Causal prefill attention of a batch of chunks read in place from the
+    paged pool (``mvb_paged_prefill``, one launch for the batch, no host
+    synchronisation).
+
+    Chunk ``i`` holds ``query_len[i]`` query tokens, one after another in
+    ``query`` ``[total_q, num_heads, head_dim]``; its sequence's block table is
+    ``block_table[seq_rows[i]]`` and ``cached_len[i]`` of its tokens are in the
+    cache before it.  Its token ``t`` attends positions
+    ``[0, cached_len[i] + t]``: the cached prefix from the pool, the chunk from
+    ``key`` / ``value`` (``[total_q, num_kv_heads, head_dim]``) when given, else
+    from the pool (written there first, as the reference's runner does).  The
+    same result as AttentionBackendGPU.prefill_attention
+    (paged_attention_gpu.py:577-661) without its per-sequence gather, concat,
+    GQA repeat and SDPA.  ``seq_rows`` / ``cached_len`` / ``query_len`` may be
+    lists or tensors (int64 on the device is the zero-copy form).
+    Returns ``[total_q, num_heads, head_dim]`` in the query's dtype.
+    """
+    _require(query.dim() == 3 and query.is_cuda, lambda: f"query must be a 3-D CUDA tensor, got {tuple(query.shape)}")
+    _require(key_cache.dim() == 4 and key_cache.shape == value_cache.shape,
+             lambda: f"key_cache {tuple(key_cache.shape)} / value_cache {tuple(value_cache.shape)} mismatch")
+    _require(query.dtype in (torch.bfloat16, torch.float16) and key_cache.dtype == query.dtype
+             and value_cache.dtype == query.dtype,
+             lambda: f"prefill needs bf16 or f16 query and caches of that dtype, got {query.dtype} / {key_cache.dtype}")
+    _require(key_cache.is_contiguous() and value_cache.is_contiguous(), "caches must be contiguous")
+    total_q, num_heads, head_dim = query.shape
+    num_blocks, num_kv_heads, bs, d2 = key_cache.shape
+    _require(bs == block_size and d2 == head_dim, lambda: f"cache {tuple(key_cache.shape)} does not match "
+                                                          f"block_size {block_size} / head_dim {head_dim}")
+    _require(num_heads % num_kv_heads == 0, lambda: f"{num_heads} query heads over {num_kv_heads} KV heads")
+    _require((key is None) == (value is None), "give both key and value, or neither")
+    dev = query.device
+    dev_idx = query.get_device()
+
+    def as_dev64(x):
+        if isinstance(x, torch.Tensor):
+            return x.to(device=dev, dtype=torch.int64).contiguous()
+        return torch.tensor(list(x), dtype=torch.int64).to(dev)
+
+    rows, cached, qlen = as_dev64(seq_rows), as_dev64(cached_len), as_dev64(query_len)
+    n = rows.numel()
+    _require(cached.numel() == n and qlen.numel() == n,
+             lambda: f"{n} sequences but {cached.numel()} cached lengths and {qlen.numel()} query lengths")
+    if out is None:
+        out = torch.empty_like(query)
+    else:
+        _require(out.shape == query.shape and out.dtype == query.dtype and out.get_device() == dev_idx
+                 and out.stride(2) == 1, "out must match query's shape, dtype and device, last dim contiguous")
+    if n == 0 or total_q == 0:
+        return out
+    if query.stride(2) != 1:
+        query = query.contiguous()
+    if key is not None:
+        _require(key.shape == (total_q, num_kv_heads, head_dim) and value.shape == key.shape,
+                 lambda: f"key / value must be [{total_q}, {num_kv_heads}, {head_dim}]")
+        if key.stride(2) != 1 or (key.stride(0) * key.element_size()) % 16 or (key.stride(1) * key.element_size()) % 16 \
+                or key.data_ptr() % 16:
+            key = key.contiguous()
+        if value.stride(2) != 1 or (value.stride(0) * value.element_size()) % 16 \
+                or (value.stride(1) * value.element_size()) % 16 or value.data_ptr() % 16:
+            value = value.contiguous()
+    if block_table.dtype != torch.int64 or block_table.get_device() != dev_idx or block_table.stride(1) != 1:
+        block_table = block_table.to(device=dev, dtype=torch.int64).contiguous()
+    state = _state(dev_idx)
+    scale = head_dim ** -0.5 if scale is None else float(scale)
+    status = _native.lib().mvb_paged_prefill(
+        query.data_ptr(), query.stride(0), query.stride(1),
+        key.data_ptr() if key is not None else None, key.stride(0) if key is not None else 0,
+        key.stride(1) if key is not None else 0,
+        value.data_ptr() if value is not None else None, value.stride(0) if value is not None else 0,
+        value.stride(1) if value is not None else 0,
+        key_cache.data_ptr(), value_cache.data_ptr(), block_table.data_ptr(), block_table.shape[0],
+        block_table.stride(0), block_table.shape[1], rows.data_ptr(), cached.data_ptr(), qlen.data_ptr(), n,
+        total_q, out.data_ptr(), out.stride(0), out.stride(1), num_heads, num_kv_heads, head_dim, block_size,
+        num_blocks, scale, _DTYPE_CODES[query.dtype], state.err_ptr, _stream_handle(dev_idx))
+    _host_status(status, "paged prefill")
+    if strict:
+        flags = _take_flags(state)
+        if flags:
+            _raise_flags(flags, {"max_blocks": block_table.shape[1], "block_size": block_size,
+                                 "num_blocks": num_blocks})
+    return out
+
+
 def paged_gather(
     key_cache: torch.Tensor,
     value_cache: torch.Tensor,
@@ -1033,15 +1132,37 @@ class AttentionBackendB200(AttentionBackend):
         chunk (mirror of AttentionBackendGPU.prefill_attention,
         paged_attention_gpu.py:577-661).
 
-        The cache is read by one ``paged_gather`` launch per group.  With the
-        chunk's ``key`` / ``value`` given, the gather reads the cached prefix and
-        the chunk is appended, as the Triton backend does; with ``None``, the
-        whole context is read from the cache (the new tokens are written before
+        One ``paged_prefill_attention`` launch for every prefill group of the
+        step: each query tile reads its cached prefix in place from the pool and
+        runs causal attention on the tensor cores, with no host synchronisation.
+        With the chunk's ``key`` / ``value`` given, the chunk's positions come from
+        them, as the Triton backend appends them; with ``None``, the whole
+        context is read from the cache (the new tokens are written before
         attention), as AttentionBackendRef does (paged_attention_ref.py:166-240).
-        The attention itself is torch SDPA with the offset causal mask.
         """
         if query.shape[0] == 0:
             return query
+        kc, vc = pool.key_caches[layer_idx], pool.value_caches[layer_idx]
+        groups = [g for g in attn_metadata.groups if g.attention_type in ("prefill_gpu", "prefill_ref")]
+        if not groups:
+            return query
+        if query.dtype not in (torch.bfloat16, torch.float16) or query.shape[2] not in (64, 128):
+            return self._prefill_general(layer_idx, query, key, value, attn_metadata, pool)
+        dev = query.device
+        rows = torch.cat([torch.as_tensor(g.seq_indices, dtype=torch.int64).to(dev) for g in groups])
+        cached = torch.cat([g.cached_len_before.to(device=dev, dtype=torch.int64).reshape(-1) for g in groups])
+        qlen = torch.cat([g.query_len.to(device=dev, dtype=torch.int64).reshape(-1) for g in groups])
+        with_chunk = key is not None and value is not None
+        return paged_prefill_attention(query, kc, vc, attn_metadata.prefill_block_tables, rows, cached, qlen,
+                                       pool.block_size, key=key if with_chunk else None,
+                                       value=value if with_chunk else None, strict=self.strict)
+
+
+    def _prefill_general(self, layer_idx, query, key, value, attn_metadata, pool) -> torch.Tensor:
+        """Prefill for shapes the paged prefill kernel does not take (fp32, head
+        dims other than 64 / 128): one paged_gather launch per group reads the
+        cached context, then torch SDPA per sequence with the offset causal mask
+        (the structure of paged_attention_gpu.py:577-661)."""
         num_heads, head_dim = query.shape[1], query.shape[2]
         reps = num_heads // pool.num_kv_heads
         scale = head_dim ** -0.5

@@ -24,7 +24,7 @@ OBJ_DIR = os.path.join(LIB_DIR, "obj")
 LIB_PATH = os.path.join(LIB_DIR, "libmvb200.so")
 
 SOURCES = ["kv_write.cu", "decode_fma.cu", "decode_mma.cu", "decode_stream.cu", "decode_sched.cu", "capi.cu",
-           "decode_noalloc.cu", "gather.cu", "rope_write.cu", "step_metadata.cu"]
+           "decode_noalloc.cu", "gather.cu", "rope_write.cu", "step_metadata.cu", "prefill_mma.cu"]
 HEADERS = ["mvb_common.cuh", "decode_common.cuh", "mma_tile.cuh"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

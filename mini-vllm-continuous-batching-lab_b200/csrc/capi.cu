@@ -24,6 +24,10 @@ cudaError_t launch_decode_stream(const CUtensorMap& tmk, const CUtensorMap& tmv,
                                  int sm_count, cudaStream_t stream);
 int stream_warps_per_cta(int head_dim);
 int stream_smem_bytes(int head_dim, int num_seqs);
+constexpr int kPrefillMaxSeqsHost = 4096;  // chunks per prefill launch (prefill_mma.cu)
+constexpr int kPrefillHeadsHost = 8;       // query heads per prefill CTA (prefill_mma.cu)
+cudaError_t launch_prefill(const PrefillArgs& a, int dtype, int head_dim, cudaStream_t stream);
+int prefill_smem_bytes(int head_dim, int n);
 SchedLayout sched_layout(int num_seqs, int num_kv_heads, int head_groups, int G, int max_blocks,
                          int block_size, int head_dim, int ctas);
 cudaError_t launch_decode_schedule(const DecodeArgs& a, int head_dim, const SchedLayout& l, void* ws,
@@ -521,6 +525,77 @@ int mvb_paged_decode_schedule(const int32_t* kv_len, const int64_t* block_table,
   const cudaError_t e = launch_decode_schedule(a, head_dim, pl.sched, workspace,
                                                (flags & MVB_DECODE_AFTER_WRITE) != 0,
                                                static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MVB_OK : MVB_ERR_CUDA;
+}
+
+int mvb_paged_prefill(const void* query, int64_t q_stride_tok, int64_t q_stride_head, const void* key,
+                      int64_t k_stride_tok, int64_t k_stride_head, const void* value, int64_t v_stride_tok,
+                      int64_t v_stride_head, const void* key_cache, const void* value_cache,
+                      const int64_t* block_table, int64_t block_table_rows, int64_t block_table_stride,
+                      int32_t max_blocks_per_seq, const int64_t* seq_rows, const int64_t* cached_len,
+                      const int64_t* query_len, int32_t num_chunks, int32_t total_q, void* out,
+                      int64_t out_stride_tok, int64_t out_stride_head, int32_t num_heads, int32_t num_kv_heads,
+                      int32_t head_dim, int32_t block_size, int32_t num_blocks, float scale, int32_t dtype,
+                      int32_t* error_flags, void* stream) {
+  mvb::NvtxRange nvtx_range("mvb_paged_prefill");
+  if (dtype != MVB_DTYPE_BF16 && dtype != MVB_DTYPE_F16) return MVB_ERR_DTYPE;
+  if (head_dim != 64 && head_dim != 128) return MVB_ERR_HEAD_DIM;
+  if (!is_pow2(block_size)) return MVB_ERR_BLOCK_SIZE;
+  if (num_chunks < 0 || total_q < 0 || num_heads <= 0 || num_kv_heads <= 0 || num_blocks <= 0 ||
+      max_blocks_per_seq < 0 || block_table_rows < 0)
+    return MVB_ERR_INVALID_ARG;
+  if (num_heads % num_kv_heads != 0) return MVB_ERR_HEADS;
+  if (num_chunks > mvb::kPrefillMaxSeqsHost) return MVB_ERR_INVALID_ARG;
+  if (num_chunks == 0 || total_q == 0) return MVB_OK;
+  if (!query || !key_cache || !value_cache || !block_table || !seq_rows || !cached_len || !query_len || !out ||
+      !error_flags)
+    return MVB_ERR_INVALID_ARG;
+  if ((key == nullptr) != (value == nullptr)) return MVB_ERR_INVALID_ARG;
+  if (max_blocks_per_seq > 0 && block_table_stride < max_blocks_per_seq) return MVB_ERR_INVALID_ARG;
+  const int64_t rows = (int64_t)num_blocks * num_kv_heads * block_size;
+  if (rows * head_dim >= ((int64_t)1 << 62)) return MVB_ERR_INVALID_ARG;
+  const int es = elem_size(dtype);
+  // 16-byte copies of pool and chunk rows, 4-byte query pairs, element output stores
+  if (!aligned_to(key_cache, 16) || !aligned_to(value_cache, 16)) return MVB_ERR_ALIGNMENT;
+  if (key != nullptr &&
+      (!aligned_to(key, 16) || !aligned_to(value, 16) || (k_stride_tok * es) % 16 || (k_stride_head * es) % 16 ||
+       (v_stride_tok * es) % 16 || (v_stride_head * es) % 16))
+    return MVB_ERR_ALIGNMENT;
+  if (!aligned_to(query, 4) || (q_stride_tok * es) % 4 || (q_stride_head * es) % 4) return MVB_ERR_ALIGNMENT;
+  if (!aligned_to(out, es)) return MVB_ERR_ALIGNMENT;
+  mvb::PrefillArgs a;
+  a.q = query;
+  a.q_s0 = q_stride_tok;
+  a.q_s1 = q_stride_head;
+  a.k = key;
+  a.k_s0 = k_stride_tok;
+  a.k_s1 = k_stride_head;
+  a.v = value;
+  a.v_s0 = v_stride_tok;
+  a.v_s1 = v_stride_head;
+  a.kc = key_cache;
+  a.vc = value_cache;
+  a.bt = block_table;
+  a.bt_rows = block_table_rows;
+  a.bt_s0 = block_table_stride;
+  a.max_blocks = max_blocks_per_seq;
+  a.seq_rows = seq_rows;
+  a.cached = cached_len;
+  a.qlen = query_len;
+  a.n = num_chunks;
+  a.total_q = total_q;
+  a.out = out;
+  a.o_s0 = out_stride_tok;
+  a.o_s1 = out_stride_head;
+  a.num_heads = num_heads;
+  a.num_kv_heads = num_kv_heads;
+  a.G = num_heads / num_kv_heads;
+  a.head_groups = (a.G + mvb::kPrefillHeadsHost - 1) / mvb::kPrefillHeadsHost;
+  a.block_size = block_size;
+  a.num_blocks = num_blocks;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.err = error_flags;
+  const cudaError_t e = launch_prefill(a, dtype, head_dim, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? MVB_OK : MVB_ERR_CUDA;
 }
 

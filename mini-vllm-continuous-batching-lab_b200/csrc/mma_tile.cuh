@@ -154,4 +154,93 @@ __device__ __forceinline__ void attend_tile(uint32_t kb, uint32_t vb, int valid,
   }
 }
 
+// attend_tile for rows with their own limits (causal prefill): row g0 of the
+// tile (this thread's c0 / c1 values) sees tokens t < valid0, row g0 + 8 tokens
+// t < valid1 (limits may be <= 0 or > 16).  The V rows are not zeroed: every
+// row the producer did not fill is zero-filled by its copies, and a real row a
+// limit masks gets weight 0.  Each row must see at least one token in the
+// first tile it is given (its running max is then finite).
+template <typename T, int D>
+__device__ __forceinline__ void attend_tile_rows(uint32_t kb, uint32_t vb, int valid0, int valid1,
+                                                 float scale_log2, const uint32_t (&qa)[D / 16][4],
+                                                 float (&o)[D / 8][4], float (&mrow)[2], float (&lrow)[2]) {
+  using MMA = Mma16816<T>;
+  constexpr int KC = D / 16, NO = D / 8;
+  const int lane = threadIdx.x & 31;
+  const int qd = lane & 3;
+  float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int kc = 0; kc < KC; ++kc) {
+    const int mi = lane >> 3;
+    const int r = (lane & 7) + ((mi >> 1) << 3);
+    const int ch = 2 * kc + (mi & 1);
+    uint32_t b0, b1, b2, b3;
+    ldsm_x4(kb + swz(r, ch), b0, b1, b2, b3);
+    MMA::run(s0, qa[kc], b0, b1);
+    MMA::run(s1, qa[kc], b2, b3);
+  }
+  float x[2][4] = {{s0[0], s0[1], s1[0], s1[1]}, {s0[2], s0[3], s1[2], s1[3]}};
+  const int tk0 = 2 * qd;
+  float p[2][4];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int lim = r == 0 ? valid0 : valid1;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int tk = tk0 + (k & 1) + ((k >> 1) << 3);
+      x[r][k] = tk < lim ? x[r][k] * scale_log2 : -INFINITY;
+      mx = fmaxf(mx, x[r][k]);
+    }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float mn = fmaxf(mrow[r], mx);
+    const float al = fast_exp2(mrow[r] - mn);
+    float sum = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      p[r][k] = fast_exp2(x[r][k] - mn);
+      sum += p[r][k];
+    }
+    lrow[r] = fmaf(lrow[r], al, sum);
+    mrow[r] = mn;
+#pragma unroll
+    for (int n = 0; n < NO; ++n) {
+      o[n][2 * r] *= al;
+      o[n][2 * r + 1] *= al;
+    }
+  }
+  uint32_t pa_hi[4], pa_lo[4];
+  {
+    float hi[2][4], lo[2][4];
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        hi[r][k] = MMA::round(p[r][k]);
+        lo[r][k] = p[r][k] - hi[r][k];
+      }
+    pa_hi[0] = MMA::pack(hi[0][0], hi[0][1]);
+    pa_hi[1] = MMA::pack(hi[1][0], hi[1][1]);
+    pa_hi[2] = MMA::pack(hi[0][2], hi[0][3]);
+    pa_hi[3] = MMA::pack(hi[1][2], hi[1][3]);
+    pa_lo[0] = MMA::pack(lo[0][0], lo[0][1]);
+    pa_lo[1] = MMA::pack(lo[1][0], lo[1][1]);
+    pa_lo[2] = MMA::pack(lo[0][2], lo[0][3]);
+    pa_lo[3] = MMA::pack(lo[1][2], lo[1][3]);
+  }
+#pragma unroll
+  for (int n = 0; n < NO; n += 2) {
+    const int mi = lane >> 3;
+    const int r = (lane & 7) + ((mi & 1) << 3);
+    const int ch = n + (mi >> 1);
+    uint32_t b0, b1, b2, b3;
+    ldsm_x4_trans(vb + swz(r, ch), b0, b1, b2, b3);
+    MMA::run(o[n], pa_hi, b0, b1);
+    MMA::run(o[n + 1], pa_hi, b2, b3);
+    MMA::run(o[n], pa_lo, b0, b1);
+    MMA::run(o[n + 1], pa_lo, b2, b3);
+  }
+}
+
 }  // namespace mvb

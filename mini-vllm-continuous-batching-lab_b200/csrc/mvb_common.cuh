@@ -59,6 +59,32 @@ struct DecodeArgs {
   int wait_limit;
 };
 
+// Arguments of the paged prefill kernel (prefill_mma.cu): the chunks' queries,
+// optionally their own K / V rows, the pool and the per-chunk metadata.
+struct PrefillArgs {
+  const void* q;
+  int64_t q_s0, q_s1;
+  const void* k;  // chunk rows [total_q, KH, D] (nullptr: the chunk is read from the pool)
+  int64_t k_s0, k_s1;
+  const void* v;
+  int64_t v_s0, v_s1;
+  const void* kc;  // pool [num_blocks, KH, BS, D]
+  const void* vc;
+  const int64_t* bt;
+  int64_t bt_rows, bt_s0;
+  int max_blocks;
+  const int64_t* seq_rows;  // [n] block-table row of chunk i
+  const int64_t* cached;    // [n] tokens already in the cache before chunk i
+  const int64_t* qlen;      // [n] tokens of chunk i
+  int n;
+  int total_q;
+  void* out;
+  int64_t o_s0, o_s1;
+  int num_heads, num_kv_heads, G, head_groups, block_size, num_blocks;
+  float scale_log2;
+  int* err;
+};
+
 // Workspace layout of the scheduled decode (MVB_DECODE_SCHED): a 256-byte
 // header, one 256-byte record per CTA, the piece descriptors, the pool rows of
 // every tile, the list of sequences left out, the arrival counters of cut units
