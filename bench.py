@@ -78,10 +78,12 @@ def parse_args():
     p.add_argument("--no-config4", action="store_true", help="skip the config-4 strong-scaling sub-object")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--requests", type=int, default=256, help="--op engine: requests per replica")
-    p.add_argument("--op", choices=["step", "gather", "rope_write", "metadata", "sweep", "engine", "profile"],
+    p.add_argument("--op", choices=["step", "gather", "rope_write", "metadata", "sweep", "engine", "profile",
+                                    "variants"],
                    default="step",
                    help="step: the decode step (the headline); sweep: decode time per launch of every "
-                        "kernel over batch x context (the plan's crossover table); engine: continuous-batching "
+                        "kernel over batch x context (the plan's crossover table); variants: decode time per "
+                        "launch of every kernel at configs 2, 3 and 4; engine: continuous-batching "
                         "serving in the reference's own engine (config 5, bounded: --requests per replica; "
                         "--impl reference runs the reference's GPU backend); profile: a few KV writes and "
                         "decodes of --variant on --config over --layers pools, untimed (the case ncu captures); "
@@ -1107,6 +1109,76 @@ def sweep_op(args):
             torch.cuda.empty_cache()
 
 
+def variants_op(args):
+    """Secondary measurement: decode time per launch of each kernel at the
+    benchmark configs — config 2 (256 x U[128,2048], 14/2/64), config 3 (32 x
+    32768, 14/2/64) and config 4 on one GPU (global batch 1024, 32/8/128,
+    lognormal contexts) — as CUDA graphs of back-to-back decodes over distinct
+    pools (more than L2 each), median of 20 replays.  Kernels: the stream
+    kernel (+ its fixup), the scheduled kernel (schedule built once per model
+    step, outside the graph), the one-CTA-per-(sequence, KV head) kernel with
+    the plan's split-K, the CUDA-core kernel (config 2 only), and AUTO.  One
+    JSON line per (config, kernel)."""
+    import torch
+
+    import mini_vllm_b200 as M
+    from mini_vllm_b200 import workloads as W
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peak, peak_kind = peaks()
+    for config, L, kinds in ((2, 24, ("stream", "sched", "mma", "fma", "auto")), (3, 4, ("stream", "sched", "mma", "auto")),
+                             (4, 2, ("stream", "sched", "mma", "auto"))):
+        spec, _ = rank_spec(config, 0, 1, args.seed)
+        t = W.torch_tensors(spec, torch.bfloat16, dev, num_layers=L)
+        q, bt, kvl = t["query"], t["block_tables"], t["kv_len"]
+        kcs, vcs = t["key_caches"], t["value_caches"]
+        out = torch.empty_like(q)
+        sched = M.build_decode_schedule(kvl, bt, spec.num_heads, spec.num_kv_heads, spec.head_dim, spec.block_size,
+                                        spec.num_blocks, torch.bfloat16)
+        by = spec.decode_bytes(2)
+        for variant in kinds:
+            sc = sched if variant == "sched" else None
+
+            def launches():
+                for layer in range(L):
+                    M.paged_decode_attention(q, kcs[layer], vcs[layer], bt, kvl, spec.block_size, out=out,
+                                             variant=variant, strict=False, schedule=sc)
+            launches()
+            torch.cuda.synchronize()
+            M.check_device_errors(dev)
+            s2 = torch.cuda.Stream(device=dev)
+            s2.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(s2):
+                launches()
+            torch.cuda.current_stream(dev).wait_stream(s2)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                launches()
+            for _ in range(3):
+                g.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            samples = []
+            for _ in range(20):
+                e0.record()
+                g.replay()
+                e1.record()
+                e1.synchronize()
+                samples.append(e0.elapsed_time(e1) * 1e3 / L)
+            us = statistics.median(samples)
+            plan = M.decode_plan(spec.num_seqs, spec.num_heads, spec.num_kv_heads, spec.head_dim, spec.block_size,
+                                 spec.num_blocks, spec.max_blocks, torch.bfloat16, variant)
+            print(json.dumps({"config": config, "kernel": variant, "plan": plan["variant"],
+                              "partitions": plan["num_partitions"], "us_per_launch": round(us, 2),
+                              "GBps": round(by / us / 1e3, 1), "frac": round(by / us / 1e3 / peak, 4),
+                              "peak": f"{peak} GB/s ({peak_kind})", "bytes_per_launch": by, "pools": L}), flush=True)
+            del g
+        del t, q, bt, kvl, kcs, vcs, out, sched
+        torch.cuda.empty_cache()
+
+
 def profile_op(args):
     """The case an ncu capture runs: for each of --layers pools, one KV write
     and one decode of --variant (with --partition-tokens) on --config, twice
@@ -1339,6 +1411,9 @@ def main():
         return
     if args.op == "profile":
         profile_op(args)
+        return
+    if args.op == "variants":
+        variants_op(args)
         return
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -38,6 +38,14 @@ def assert_close(gpu: torch.Tensor, ref: np.ndarray, dtype: str, msg: str = ""):
     assert np.isfinite(g).all(), f"non-finite output {msg}"
     err = np.abs(g - ref)
     bound = atol + rtol * np.abs(ref)
+    if msg.startswith("config"):
+        # the observed margins, for the record (pytest -s prints them): max abs,
+        # and max rel over outputs with |ref| >= 1e-2 (below, bf16 rounding of the
+        # output alone exceeds 1 % relative)
+        big = np.abs(ref) >= 1e-2
+        rel = (err[big] / np.abs(ref[big])).max() if big.any() else 0.0
+        print(f"PARITY {msg}: max_abs={err.max():.3e} max_rel(|ref|>=1e-2)={rel:.3e} "
+              f"max_err/bound={(err / bound).max():.3f}")
     worst = np.unravel_index(np.argmax(err - bound), err.shape)
     assert (err <= bound).all(), (
         f"{msg}: max excess at {worst}: gpu={g[worst]} ref={ref[worst]} "
