@@ -345,7 +345,7 @@ def ours(args, rank, world, local_rank):
     plan = M.decode_plan(spec.num_seqs, spec.num_heads, spec.num_kv_heads, spec.head_dim, spec.block_size,
                          spec.num_blocks, spec.max_blocks, torch.bfloat16, args.variant, pt,
                          kcs[0].data_ptr())
-    scheduled = plan["variant"] == "sched"
+    scheduled = plan["variant"] in ("sched", "stream")  # kernels with a per-step set-up
     sched = None
 
     def begin_model_step():
@@ -355,7 +355,7 @@ def ours(args, rank, world, local_rank):
         if scheduled:
             sched = M.build_decode_schedule(kvl, bt, spec.num_heads, spec.num_kv_heads, spec.head_dim,
                                             spec.block_size, spec.num_blocks, torch.bfloat16,
-                                            schedule=sched, strict=False)
+                                            schedule=sched, strict=False, variant=plan["variant"])
 
     def step(layer):
         M.paged_cache_write(nk, nv, kcs[layer], vcs[layer], slots, spec.block_size, strict=False,
@@ -1066,7 +1066,7 @@ def sweep_op(args):
             q, bt, kvl = t["query"], t["block_tables"], t["kv_len"]
             kcs, vcs = t["key_caches"], t["value_caches"]
             out = torch.empty_like(q)
-            sched = M.build_decode_schedule(kvl, bt, 14, 2, 64, 16, spec.num_blocks, torch.bfloat16)
+            sched = M.build_decode_schedule(kvl, bt, 14, 2, 64, 16, spec.num_blocks, torch.bfloat16, variant="sched")
             kinds = [("stream", "stream", None, None), ("sched", "sched", None, sched),
                      ("mma_unsplit", "mma", spec.max_blocks * 16, None), ("mma_split512", "mma", 512, None),
                      ("fma", "fma", None, None), ("auto", "auto", None, None)]
@@ -1115,7 +1115,9 @@ def variants_op(args):
     32768, 14/2/64) and config 4 on one GPU (global batch 1024, 32/8/128,
     lognormal contexts) — as CUDA graphs of back-to-back decodes over distinct
     pools (more than L2 each), median of 20 replays.  Kernels: the stream
-    kernel (+ its fixup), the scheduled kernel (schedule built once per model
+    kernel (+ its fixup) building its set-up in every launch ("stream") and
+    reading the per-step schedule built once outside the graph
+    ("stream+schedule"), the scheduled kernel (schedule built once per model
     step, outside the graph), the one-CTA-per-(sequence, KV head) kernel with
     the plan's split-K, the CUDA-core kernel (config 2 only), and AUTO.  One
     JSON line per (config, kernel)."""
@@ -1127,18 +1129,22 @@ def variants_op(args):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     peak, peak_kind = peaks()
-    for config, L, kinds in ((2, 24, ("stream", "sched", "mma", "fma", "auto")), (3, 4, ("stream", "sched", "mma", "auto")),
-                             (4, 2, ("stream", "sched", "mma", "auto"))):
+    for config, L, kinds in ((2, 24, ("stream", "stream+schedule", "sched", "mma", "fma", "auto")),
+                             (3, 4, ("stream", "stream+schedule", "sched", "mma", "auto")),
+                             (4, 2, ("stream", "stream+schedule", "sched", "mma", "auto"))):
         spec, _ = rank_spec(config, 0, 1, args.seed)
         t = W.torch_tensors(spec, torch.bfloat16, dev, num_layers=L)
         q, bt, kvl = t["query"], t["block_tables"], t["kv_len"]
         kcs, vcs = t["key_caches"], t["value_caches"]
         out = torch.empty_like(q)
         sched = M.build_decode_schedule(kvl, bt, spec.num_heads, spec.num_kv_heads, spec.head_dim, spec.block_size,
-                                        spec.num_blocks, torch.bfloat16)
+                                        spec.num_blocks, torch.bfloat16, variant="sched")
+        ssched = M.build_decode_schedule(kvl, bt, spec.num_heads, spec.num_kv_heads, spec.head_dim,
+                                         spec.block_size, spec.num_blocks, torch.bfloat16, variant="stream")
         by = spec.decode_bytes(2)
-        for variant in kinds:
-            sc = sched if variant == "sched" else None
+        for kind in kinds:
+            variant = "stream" if kind == "stream+schedule" else kind
+            sc = sched if kind == "sched" else ssched if kind == "stream+schedule" else None
 
             def launches():
                 for layer in range(L):
@@ -1170,12 +1176,12 @@ def variants_op(args):
             us = statistics.median(samples)
             plan = M.decode_plan(spec.num_seqs, spec.num_heads, spec.num_kv_heads, spec.head_dim, spec.block_size,
                                  spec.num_blocks, spec.max_blocks, torch.bfloat16, variant)
-            print(json.dumps({"config": config, "kernel": variant, "plan": plan["variant"],
+            print(json.dumps({"config": config, "kernel": kind, "plan": plan["variant"],
                               "partitions": plan["num_partitions"], "us_per_launch": round(us, 2),
                               "GBps": round(by / us / 1e3, 1), "frac": round(by / us / 1e3 / peak, 4),
                               "peak": f"{peak} GB/s ({peak_kind})", "bytes_per_launch": by, "pools": L}), flush=True)
             del g
-        del t, q, bt, kvl, kcs, vcs, out, sched
+        del t, q, bt, kvl, kcs, vcs, out, sched, ssched
         torch.cuda.empty_cache()
 
 
@@ -1201,9 +1207,9 @@ def profile_op(args):
     plan = M.decode_plan(spec.num_seqs, spec.num_heads, spec.num_kv_heads, spec.head_dim, spec.block_size,
                          spec.num_blocks, spec.max_blocks, torch.bfloat16, args.variant, pt)
     sched = None
-    if plan["variant"] == "sched":
+    if plan["variant"] in ("sched", "stream"):
         sched = M.build_decode_schedule(kvl, bt, spec.num_heads, spec.num_kv_heads, spec.head_dim,
-                                        spec.block_size, spec.num_blocks, torch.bfloat16)
+                                        spec.block_size, spec.num_blocks, torch.bfloat16, variant=plan["variant"])
     for _ in range(2):
         for layer in range(L):
             M.paged_cache_write(nk, nv, t["key_caches"][layer], t["value_caches"][layer], slots, spec.block_size,

@@ -213,8 +213,8 @@ int mvb_test_decode_wait_timeout(const void* query, int64_t q_stride_seq, int64_
  * must not be followed by a call with this flag. */
 #define MVB_DECODE_AFTER_WRITE 0x100
 
-/* Flag ORed into `variant` of mvb_paged_decode with MVB_DECODE_SCHED: the
- * workspace already holds the schedule of this batch, built by
+/* Flag ORed into `variant` of mvb_paged_decode (the stream and scheduled
+ * kernels): the workspace already holds the schedule of this batch, built by
  * mvb_paged_decode_schedule from the same kv_len and block-table contents and
  * shape arguments (kv_len and the block tables are the same for every layer of a model step,
  * so one schedule serves all of them).  Without the flag the call builds the
@@ -225,32 +225,39 @@ int mvb_test_decode_wait_timeout(const void* query, int64_t q_stride_seq, int64_
 #define MVB_DECODE_SCHEDULE_READY 0x200
 
 /*
- * Build the decode schedule of a batch (variant MVB_DECODE_SCHED) into
- * `workspace`: the stream of 16-token tiles of every (sequence, KV head, head
- * group) unit cut into one contiguous range per SM, each range's pieces (the
- * units it covers, the ones cut by its ends first) and the pool row of every
- * tile.  It reads kv_len (int32 [num_seqs]) and the block tables (int64,
- * row stride block_table_stride), both in device memory; the shape arguments
- * are those of the decodes that will use it, and workspace_bytes must be at
- * least the plan's (mvb_paged_decode_plan with variant MVB_DECODE_SCHED).  A
- * sequence whose kv_len is < 1 or needs more than max_blocks_per_seq blocks
- * sets MVB_DEV_KV_LEN / MVB_DEV_TABLE_SHORT and gets zero output rows from
- * every decode that uses the schedule; a block id outside [0, num_blocks)
- * sets MVB_DEV_BLOCK_ID and its tile is skipped.  `flags`:
- * MVB_DECODE_AFTER_WRITE when the kernel launched just before on `stream` is
- * the KV write (the schedule is then computed while the write runs).  No
- * reference counterpart: the Triton decode (paged_attention_gpu.py:252-321)
- * has no per-step set-up; this hoists the work every layer's decode would
- * repeat (the block-table walk) out of the per-layer calls.  A decode that
- * reported MVB_DEV_TIMEOUT may leave the schedule's counters dirty: build it
- * again before the next call.
+ * Build the per-step decode schedule of a batch into `workspace`, for the
+ * kernel the plan picks for `variant` (MVB_DECODE_AUTO and the shape
+ * arguments of the decodes that will use it).  kv_len and the block tables are
+ * the same for every layer of a model step, so one schedule serves all of them
+ * (mvb_paged_decode with MVB_DECODE_SCHEDULE_READY).
+ *   MVB_DECODE_STREAM: the stream kernel's set-up — the tile prefix of the
+ *     step, the pool row of every tile, and for every stream warp its tile range
+ *     with its first 32 rows — so each decode issues its first loads after one
+ *     read instead of deriving them from kv_len and the tables.
+ *   MVB_DECODE_SCHED: the scheduled kernel's per-SM tile ranges, their pieces
+ *     and pool rows.
+ *   any other kernel: nothing to build; returns MVB_OK.
+ * It reads kv_len (int32 [num_seqs]) and the block tables (int64, row stride
+ * block_table_stride), both in device memory; workspace_bytes must be at least
+ * the plan's (mvb_paged_decode_plan with the same arguments).  A sequence whose
+ * kv_len is < 1 or needs more than max_blocks_per_seq blocks sets
+ * MVB_DEV_KV_LEN / MVB_DEV_TABLE_SHORT and gets zero output rows from every
+ * decode that uses the schedule; a block id outside [0, num_blocks) sets
+ * MVB_DEV_BLOCK_ID and its tile is skipped.  `flags`: MVB_DECODE_AFTER_WRITE
+ * when the kernel launched just before on `stream` is the KV write (the
+ * schedule is then computed while the write runs).  No reference counterpart:
+ * the Triton decode (paged_attention_gpu.py:252-321) has no per-step set-up;
+ * this hoists the work every layer's decode would repeat (the kv_len prefix and
+ * the block-table walk) out of the per-layer calls.  A decode that reported
+ * MVB_DEV_TIMEOUT may leave a scheduled kernel's counters dirty: build it again
+ * before the next call.
  */
 int mvb_paged_decode_schedule(const int32_t* kv_len, const int64_t* block_table,
                               int64_t block_table_stride, int32_t num_seqs, int32_t num_heads,
                               int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
                               int32_t num_blocks, int32_t max_blocks_per_seq, int32_t dtype,
-                              int32_t flags, void* workspace, int64_t workspace_bytes,
-                              int32_t* error_flags, void* stream);
+                              int32_t variant, int32_t flags, void* workspace,
+                              int64_t workspace_bytes, int32_t* error_flags, void* stream);
 
 /* ABI version; bumped whenever a signature below changes. */
 int mvb_abi_version(void);

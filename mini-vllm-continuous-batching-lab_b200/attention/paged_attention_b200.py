@@ -437,10 +437,10 @@ def _decode_fast(query, key_cache, value_cache, block_table, kv_len_after, block
     state = _state(query.get_device())
     flags = _native.DECODE_AFTER_WRITE if after_write else 0
     ws = None
-    if schedule is not None:
-        if variant not in ("auto", "sched"):
+    if schedule is not None and schedule.variant is not None:
+        if variant not in ("auto", schedule.variant):
             return None
-        variant = "sched"  # a schedule is the scheduled kernel's
+        variant = schedule.variant  # the kernel the schedule was built for
         flags |= _native.DECODE_SCHEDULE_READY
         ws = schedule.workspace
     status, res = fast.decode(query, key_cache, value_cache, block_table, kv_len_after, block_size,
@@ -458,9 +458,10 @@ def _decode_fast(query, key_cache, value_cache, block_table, kv_len_after, block
 
 
 class DecodeSchedule:
-    """The per-step work list of the scheduled decode kernel (variant
-    ``"sched"``) and the device workspace it lives in: every SM's range of the
-    step's KV tiles, its pieces and the pool row of each tile.
+    """The per-step set-up of the decode kernel the plan picks (``variant``:
+    ``"stream"`` or ``"sched"``; ``None`` for kernels that need none) and the
+    device workspace it lives in: the step's tile ranges and the pool row of
+    each KV tile.
 
     kv_len and the block tables are the same for every layer of a model step,
     so one schedule, built once per step by ``build_decode_schedule``, serves
@@ -470,11 +471,12 @@ class DecodeSchedule:
     raised a device timeout (which may leave its counters dirty).
     """
 
-    __slots__ = ("workspace", "key")
+    __slots__ = ("workspace", "key", "variant")
 
-    def __init__(self, workspace: torch.Tensor, key: tuple) -> None:
+    def __init__(self, workspace: Optional[torch.Tensor], key: tuple, variant: Optional[str] = "sched") -> None:
         self.workspace = workspace
         self.key = key
+        self.variant = variant
 
 
 def build_decode_schedule(
@@ -490,9 +492,12 @@ def build_decode_schedule(
     schedule: Optional[DecodeSchedule] = None,
     after_write: bool = False,
     strict: bool = True,
+    variant: str = "auto",
 ) -> DecodeSchedule:
-    """Build the decode schedule of a batch (``mvb_paged_decode_schedule``, one
-    launch on the current stream) for decodes of the given shape, with
+    """Build the per-step decode schedule of a batch
+    (``mvb_paged_decode_schedule``, one launch on the current stream) for
+    decodes of the given shape with ``variant`` (the plan's kernel: the stream
+    and scheduled kernels have a per-step set-up, the others none), with
     ``block_tables`` ``[num_seqs, max_blocks_per_seq]`` (``-1`` padded).
     ``schedule`` reuses an earlier schedule's workspace when it is large
     enough.  ``after_write``: the kernel launched just before on the current
@@ -509,10 +514,14 @@ def build_decode_schedule(
     if block_tables.dtype != torch.int64 or block_tables.get_device() != dev_idx or block_tables.stride(1) != 1:
         block_tables = block_tables.to(device=kv_len_after.device, dtype=torch.int64).contiguous()
     max_blocks_per_seq = block_tables.shape[1]
+    _require(variant in _VARIANTS, lambda: f"variant must be one of {sorted(_VARIANTS)}, got {variant!r}")
     plan = _cached_plan(dev_idx, num_seqs, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
-                        max_blocks_per_seq, dtype, "sched", None, 16)
+                        max_blocks_per_seq, dtype, variant, None, 16)
     nbytes = plan["workspace_bytes"]
-    key = (dev_idx, num_seqs, num_heads, num_kv_heads, head_dim, block_size, num_blocks, max_blocks_per_seq, dtype)
+    key = (dev_idx, num_seqs, num_heads, num_kv_heads, head_dim, block_size, num_blocks, max_blocks_per_seq, dtype,
+           plan["variant"])
+    if plan["variant"] not in ("stream", "sched"):
+        return DecodeSchedule(None, key, None)  # the plan's kernel has no per-step set-up
     if schedule is not None and schedule.workspace.get_device() == dev_idx and schedule.workspace.numel() >= nbytes:
         ws = schedule.workspace
     else:
@@ -521,7 +530,7 @@ def build_decode_schedule(
     status = _native.lib().mvb_paged_decode_schedule(
         kv_len_after.data_ptr(), block_tables.data_ptr(), block_tables.stride(0), num_seqs, num_heads,
         num_kv_heads, head_dim, block_size, num_blocks,
-        max_blocks_per_seq, _DTYPE_CODES[dtype], _native.DECODE_AFTER_WRITE if after_write else 0,
+        max_blocks_per_seq, _DTYPE_CODES[dtype], _VARIANTS[variant], _native.DECODE_AFTER_WRITE if after_write else 0,
         ws.data_ptr(), ws.numel(), state.err_ptr, _stream_handle(dev_idx))
     _host_status(status, "paged decode schedule")
     if strict:
@@ -531,8 +540,9 @@ def build_decode_schedule(
                                  "block_size": block_size, "num_blocks": num_blocks})
     if schedule is not None and schedule.workspace is ws:
         schedule.key = key
+        schedule.variant = plan["variant"]
         return schedule
-    return DecodeSchedule(ws, key)
+    return DecodeSchedule(ws, key, plan["variant"])
 
 
 def paged_decode_attention(
@@ -577,8 +587,8 @@ def paged_decode_attention(
 
     Returns ``[total_decode, num_q_heads, head_dim]`` in the query's dtype.
     """
-    if schedule is not None and variant == "auto":
-        variant = "sched"
+    if schedule is not None and schedule.variant is not None and variant == "auto":
+        variant = schedule.variant
     res = _decode_fast(query, key_cache, value_cache, block_table, kv_len_after, block_size, scale, out,
                        variant, partition_tokens, strict, after_write, schedule)
     if res is not None:
@@ -625,8 +635,9 @@ def paged_decode_attention(
                         16 if key_cache.data_ptr() % 16 == 0 else 8)
     ws_bytes = plan["workspace_bytes"]
     flags = _native.DECODE_AFTER_WRITE if after_write else 0
-    if schedule is not None:
-        _require(plan["variant"] == "sched", lambda: f"schedule= needs the 'sched' kernel, the plan is {plan['variant']!r}")
+    if schedule is not None and schedule.variant is not None:
+        _require(plan["variant"] == schedule.variant,
+                 lambda: f"the schedule was built for the {schedule.variant!r} kernel, the plan is {plan['variant']!r}")
         _require(schedule.workspace.get_device() == dev_idx and schedule.workspace.numel() >= ws_bytes,
                  "the schedule was built for another device or a smaller shape")
         ws_ptr, ws_bytes = schedule.workspace.data_ptr(), schedule.workspace.numel()
@@ -1037,7 +1048,8 @@ class AttentionBackendB200(AttentionBackend):
         # early and writes the decode's inputs (plain torch kernels do not).
         self.overlap_after_write = overlap_after_write
         self._last_write: Optional[Tuple[int, int]] = None
-        # The decode schedule of the current step (variant "sched"): built at
+        # The decode schedule of the current step (variants "stream" and
+        # "sched"): built at
         # layer 0 of every step and whenever the metadata object, its
         # tensors or the shapes change; every other layer reuses it.
         self._schedule: Optional[DecodeSchedule] = None
@@ -1102,10 +1114,11 @@ class AttentionBackendB200(AttentionBackend):
     _schedule_built_now = False
 
     def _step_schedule(self, layer_idx, query, kc, bt, kvl, attn_metadata, block_size, after) -> Optional[DecodeSchedule]:
-        """The decode schedule of this step for the "sched" kernel, built when
-        needed (None when the decode runs another kernel)."""
+        """The decode schedule of this step for the "stream" or "sched"
+        kernel, built when needed (None when the decode runs another
+        kernel)."""
         self._schedule_built_now = False
-        if self.decode_variant not in ("auto", "sched") or not (query.is_cuda and kvl.is_cuda and bt.is_cuda):
+        if self.decode_variant not in ("auto", "sched", "stream") or not (query.is_cuda and kvl.is_cuda and bt.is_cuda):
             return None
         if query.dtype not in (torch.bfloat16, torch.float16) or block_size % 16 or kc.dtype != query.dtype:
             return None
@@ -1116,12 +1129,12 @@ class AttentionBackendB200(AttentionBackend):
         plan = _cached_plan(query.get_device(), query.shape[0], query.shape[1], kc.shape[1], query.shape[2],
                             block_size, kc.shape[0], bt.shape[1], query.dtype, self.decode_variant,
                             self.partition_tokens, 16 if kc.data_ptr() % 16 == 0 else 8)
-        if plan["variant"] != "sched":
+        if plan["variant"] not in ("sched", "stream"):
             return None
         self._schedule_key = None
         self._schedule = build_decode_schedule(kvl, bt, query.shape[1], kc.shape[1], query.shape[2], block_size,
                                                kc.shape[0], query.dtype, schedule=self._schedule,
-                                               after_write=after, strict=False)
+                                               after_write=after, strict=False, variant=plan["variant"])
         self._schedule_key = key
         self._schedule_built_now = True
         return self._schedule

@@ -21,7 +21,9 @@ cudaError_t launch_decode_mma(const CUtensorMap& tmk, const CUtensorMap& tmv, co
                               int dtype, int head_dim, int max_bids, cudaStream_t stream);
 cudaError_t launch_decode_stream(const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a,
                                  int dtype, int head_dim, int* scratch, float* part, int max_warps,
-                                 int sm_count, cudaStream_t stream);
+                                 int sm_count, const StreamSchedPtrs* sp, cudaStream_t stream);
+cudaError_t launch_decode_stream_schedule(const DecodeArgs& a, int dtype, int head_dim, int max_warps, int sm_count,
+                                          const StreamSchedPtrs& sp, bool wait_at_end, cudaStream_t stream);
 int stream_warps_per_cta(int head_dim);
 int stream_smem_bytes(int head_dim, int num_seqs);
 constexpr int kPrefillMaxSeqsHost = 4096;  // chunks per prefill launch (prefill_mma.cu)
@@ -53,7 +55,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 namespace {
 
-constexpr int kAbiVersion = 4;
+constexpr int kAbiVersion = 5;
 // Longest context the auto plan serves with one CTA per (sequence, KV head);
 // beyond it the flash-decoding split is used.
 constexpr int64_t kUnsplitMaxTokens = 8192;
@@ -111,8 +113,20 @@ struct Plan {
   int64_t off_m, off_l;  // workspace offsets of the m / l arrays
   int max_warps;         // stream variant: warps the partial-state slots cover
   int64_t off_part;      // stream variant: workspace offset of the partial slots
+  // stream variant: its per-step schedule after the per-launch part
+  int64_t off_shdr, off_spre, off_sctx, off_srows, off_srec;
   SchedLayout sched;     // sched variant: workspace layout
 };
+
+StreamSchedPtrs stream_sched_ptrs(const Plan& pl, char* ws) {
+  StreamSchedPtrs sp;
+  sp.hdr = ws + pl.off_shdr;
+  sp.pre = reinterpret_cast<const int*>(ws + pl.off_spre);
+  sp.ctx = reinterpret_cast<const int*>(ws + pl.off_sctx);
+  sp.rows = reinterpret_cast<const int*>(ws + pl.off_srows);
+  sp.rec = ws + pl.off_srec;
+  return sp;
+}
 
 int make_plan(int num_seqs, int num_heads, int num_kv_heads, int head_dim, int block_size,
               int num_blocks, int max_blocks, int dtype, int variant, int partition_tokens,
@@ -201,7 +215,14 @@ int make_plan(int num_seqs, int num_heads, int num_kv_heads, int head_dim, int b
     pl->max_warps = per_sm * sm_count_current() * nw;
     pl->off_m = pl->off_l = 0;
     pl->off_part = round_up((int64_t)per_sm * sm_count_current() * nw * 32, 256);
-    pl->ws_bytes = pl->off_part + (int64_t)pl->max_warps * 2 * 16 * (head_dim + 2) * 4;
+    // the per-step schedule (MVB_DECODE_SCHEDULE_READY): header, tile prefix,
+    // servable kv_len, one row per tile, one 144-byte record per warp
+    pl->off_shdr = round_up(pl->off_part + (int64_t)pl->max_warps * 2 * 16 * (head_dim + 2) * 4, 256);
+    pl->off_spre = pl->off_shdr + 256;
+    pl->off_sctx = round_up(pl->off_spre + ((int64_t)num_seqs + 1) * 4, 256);
+    pl->off_srows = round_up(pl->off_sctx + (int64_t)num_seqs * 4, 256);
+    pl->off_srec = round_up(pl->off_srows + (int64_t)num_seqs * khg16 * max_ctx_tiles * 4, 256);
+    pl->ws_bytes = pl->off_srec + (int64_t)pl->max_warps * 144;
     return MVB_OK;
   }
   pl->max_warps = 0;
@@ -470,9 +491,10 @@ int mvb_paged_decode(const void* query, int64_t q_stride_seq, int64_t q_stride_h
     if (!pool_tensor_map(key_cache, rows, head_dim, dtype, &tmk) ||
         !pool_tensor_map(value_cache, rows, head_dim, dtype, &tmv))
       return MVB_ERR_TENSOR_MAP;
+    StreamSchedPtrs sp = stream_sched_ptrs(pl, ws);
     e = launch_decode_stream(tmk, tmv, a, dtype, head_dim, reinterpret_cast<int*>(ws),
                              reinterpret_cast<float*>(ws + pl.off_part), pl.max_warps,
-                             sm_count_current(), s);
+                             sm_count_current(), sched_ready ? &sp : nullptr, s);
     return e == cudaSuccess ? MVB_OK : MVB_ERR_CUDA;
   }
   if (pl.variant == MVB_DECODE_MMA) {
@@ -496,15 +518,17 @@ int mvb_paged_decode(const void* query, int64_t q_stride_seq, int64_t q_stride_h
 int mvb_paged_decode_schedule(const int32_t* kv_len, const int64_t* block_table, int64_t block_table_stride,
                               int32_t num_seqs, int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
                               int32_t block_size, int32_t num_blocks, int32_t max_blocks_per_seq, int32_t dtype,
-                              int32_t flags, void* workspace, int64_t workspace_bytes, int32_t* error_flags,
-                              void* stream) {
+                              int32_t variant, int32_t flags, void* workspace, int64_t workspace_bytes,
+                              int32_t* error_flags, void* stream) {
   mvb::NvtxRange nvtx_range("mvb_paged_decode_schedule");
   Plan pl;
+  variant &= ~(MVB_DECODE_AFTER_WRITE | MVB_DECODE_SCHEDULE_READY);
   const int st = make_plan(num_seqs, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
-                           max_blocks_per_seq, dtype, MVB_DECODE_SCHED, 0, nullptr, &pl);
+                           max_blocks_per_seq, dtype, variant, 0, nullptr, &pl);
   if (st != MVB_OK) return st;
   if ((flags & ~MVB_DECODE_AFTER_WRITE) != 0) return MVB_ERR_INVALID_ARG;
   if (num_seqs == 0) return MVB_OK;
+  if (pl.variant != MVB_DECODE_SCHED && pl.variant != MVB_DECODE_STREAM) return MVB_OK;  // nothing per step
   if (!kv_len || !block_table || !error_flags) return MVB_ERR_INVALID_ARG;
   if (max_blocks_per_seq > 0 && block_table_stride < max_blocks_per_seq) return MVB_ERR_INVALID_ARG;
   if (workspace == nullptr || workspace_bytes < pl.ws_bytes || !aligned_to(workspace, 256))
@@ -522,9 +546,15 @@ int mvb_paged_decode_schedule(const int32_t* kv_len, const int64_t* block_table,
   a.max_blocks = max_blocks_per_seq;
   a.num_blocks = num_blocks;
   a.err = error_flags;
-  const cudaError_t e = launch_decode_schedule(a, head_dim, pl.sched, workspace,
-                                               (flags & MVB_DECODE_AFTER_WRITE) != 0,
-                                               static_cast<cudaStream_t>(stream));
+  const bool wait_at_end = (flags & MVB_DECODE_AFTER_WRITE) != 0;
+  cudaError_t e;
+  if (pl.variant == MVB_DECODE_SCHED) {
+    e = launch_decode_schedule(a, head_dim, pl.sched, workspace, wait_at_end, static_cast<cudaStream_t>(stream));
+  } else {
+    e = launch_decode_stream_schedule(a, dtype, head_dim, pl.max_warps, sm_count_current(),
+                                      stream_sched_ptrs(pl, static_cast<char*>(workspace)), wait_at_end,
+                                      static_cast<cudaStream_t>(stream));
+  }
   return e == cudaSuccess ? MVB_OK : MVB_ERR_CUDA;
 }
 

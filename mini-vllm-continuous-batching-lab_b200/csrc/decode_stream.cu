@@ -31,12 +31,34 @@ namespace mvb {
 
 constexpr int kStreamRowBatch = 128;  // tiles whose pool rows a warp resolves at once
 
+// Per-step schedule of the stream kernel (MVB_DECODE_SCHEDULE_READY): what
+// every layer of a model step would otherwise derive again from kv_len and the
+// block tables, built once by decode_stream_schedule_kernel.
+struct StreamSchedHeader {
+  int total_tiles;
+  int bits;       // MVB_DEV_* bits of the step's sequences and block ids
+  int num_warps;  // the stream grid the schedule was cut for
+  int pad[61];
+};
+static_assert(sizeof(StreamSchedHeader) == 256, "header is 256 bytes");
+struct StreamRec {  // one per stream warp: its tile range and the pool rows of its first 32 tiles
+  int4 h;           // {first tile, tiles, 0, 0}
+  int rows[32];     // -1 past the range or for a bad block id
+};
+static_assert(sizeof(StreamRec) == 144, "record is 144 bytes");
+
 struct StreamArgs {
   int4* desc;     // [num_warps][2] the cut unit each warp begins, for the fixup:
                   // {first tile, end tile, sequence, T_all}, {first head, heads, 0, 0};
                   // first tile = -1 when the warp begins no cut unit
   float* part;    // [num_warps][2][16][D + 2] partial states (m, l, O[D] per row)
   int num_warps;  // gridDim.x * NW
+  // the step's schedule (nullptr: the kernel derives its set-up from kv_len and the tables)
+  const StreamSchedHeader* shdr;
+  const int* spre;        // [Nd + 1] tile prefix per sequence (all its units)
+  const int* sctx;        // [Nd] servable kv_len (0 = left out)
+  const int* srows;       // [total_tiles] pool row of every tile, in stream order
+  const StreamRec* srec;  // [num_warps]
 };
 
 // Warp whose range [R(w), R(w+1)), R(w) = floor(w * T / Wtot), holds global
@@ -77,6 +99,35 @@ decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
   if (!a.early_inputs) grid_dependency_wait();
   grid_launch_dependents();    // the fixup kernel may be scheduled as CTAs retire
 
+  const bool from_schedule = sa.srec != nullptr;
+  int rec_row = -1;
+  if (from_schedule) {
+    // The step's schedule: the pool rows of this warp's first 32 tiles in one
+    // read, the tile prefix and servable kv_len for locating units
+    // (L2-resident: every layer of the step reads them).
+    rec_row = __ldcg(&(sa.srec + blockIdx.x * NW + warp)->rows[lane]);
+    for (int i = tid; i <= Nd; i += NW * 32) {
+      pre[i] = __ldcg(sa.spre + i);
+      if (i < Nd) ctxs[i] = __ldcg(sa.sctx + i);
+    }
+    __syncthreads();
+    if (__ldcg(&sa.shdr->num_warps) != sa.num_warps) {  // cut for another grid: refuse
+      if (tid == 0 && blockIdx.x == 0) atomicOr(a.err, MVB_DEV_SCHEDULE);
+      if (lane == 0) sa.desc[2 * (blockIdx.x * NW + warp)] = make_int4(-1, 0, 0, 0);
+      return;
+    }
+    if (blockIdx.x == 0) {  // rows of the sequences left out: zeros, and the step's error bits
+      if (tid == 0) {
+        const int bits = __ldcg(&sa.shdr->bits);
+        if (bits) atomicOr(a.err, bits);
+      }
+      for (int i = warp; i < Nd; i += NW) {
+        if (ctxs[i] != 0) continue;
+        T* out = static_cast<T*>(a.out) + (int64_t)i * a.o_s0;
+        for (int e = lane; e < a.num_heads * D; e += 32) out[(e / D) * a.o_s1 + e % D] = from_f32<T>(0.f);
+      }
+    }
+  } else {
   // ---- prologue: tiles per sequence (all its units) and their exclusive prefix ----
   {
     constexpr int NT = NW * 32;
@@ -116,6 +167,7 @@ decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
     }
     if (tid == 0) pre[Nd] = total;
     __syncthreads();
+  }
   }
 
   const int T_all = pre[Nd];
@@ -162,6 +214,14 @@ decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
   };
   // All lanes: resolve the pool rows of tiles [j0, j0 + kStreamRowBatch) of this range.
   auto fill_rows = [&](int j0, int i0 = 0) {
+    if (from_schedule) {
+      for (int i = i0 + lane; i < kStreamRowBatch; i += 32) {
+        const int j = j0 + i;
+        myrows[i] = j < n ? __ldcg(sa.srows + r0 + j) : -1;
+      }
+      __syncwarp();
+      return;
+    }
     for (int i = i0 + lane; i < kStreamRowBatch; i += 32) {
       const int j = j0 + i;
       int row = -1;
@@ -190,6 +250,7 @@ decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
     myok[st] = row >= 0;
     if (W == a.hold_warp && j == a.hold_tile) return;  // test hook: the stage never completes
     if (row < 0) {
+      if (from_schedule) atomicOr(a.err, MVB_DEV_BLOCK_ID);  // resolved by the schedule: flag it per call
       mbar_arrive(bar);
       return;
     }
@@ -204,7 +265,8 @@ decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
 
   // The first 32 block ids only: the first loads are issued before the rest of
   // the batch is resolved (below).
-  for (int j = lane; j < 32; j += 32) {
+  if (from_schedule) myrows[lane] = rec_row;
+  for (int j = lane; j < 32 && !from_schedule; j += 32) {
     int row = -1;
     if (j < n) {
       int s, k, t;
@@ -660,6 +722,118 @@ __global__ void __launch_bounds__(kFixupWarps * 32) decode_stream_fixup_cta_kern
   }  // q
 }
 
+
+// ---------------------------------------------------------------------------
+// per-step schedule of the stream kernel
+// ---------------------------------------------------------------------------
+constexpr int kStreamSchedThreads = 512;
+
+__device__ __forceinline__ int stream_sched_seq_error(int ctx, int block_size, int max_blocks) {
+  if (ctx < 1) return MVB_DEV_KV_LEN;
+  if (((int64_t)ctx + block_size - 1) / block_size > max_blocks) return MVB_DEV_TABLE_SHORT;
+  return 0;
+}
+
+// One launch of C CTAs per model step.  Every CTA scans kv_len into the tile
+// prefix (shared memory; tiles of a left-out sequence are 0), then resolves the
+// pool rows of its 1/C share of the tile stream and the records of its 1/C
+// share of the stream warps.  wait_at_end: as decode_schedule_kernel.
+__global__ void __launch_bounds__(kStreamSchedThreads)
+decode_stream_schedule_kernel(const int* __restrict__ kv_len, const int64_t* __restrict__ bt, int64_t bt_s0,
+                              int num_seqs, int num_kv_heads, int head_groups, int block_size, int max_blocks,
+                              int num_blocks, int num_warps, StreamSchedHeader* hdr, int* spre, int* sctx,
+                              int* srows, StreamRec* srec, int* err, int wait_at_end) {
+  extern __shared__ int spre_s[];  // [num_seqs + 1]
+  constexpr int NT = kStreamSchedThreads, NWP = NT / 32;
+  __shared__ int s_red[2][NWP];
+  if (!wait_at_end) grid_dependency_wait();
+  grid_launch_dependents();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int ups = num_kv_heads * head_groups;
+  const int per = (num_seqs + NT - 1) / NT;
+  const int i0 = min(num_seqs, tid * per), i1 = min(num_seqs, i0 + per);
+  int my_t = 0, my_bits = 0;
+  for (int i = i0; i < i1; ++i) {
+    const int ctx = __ldg(kv_len + i);
+    const int e = stream_sched_seq_error(ctx, block_size, max_blocks);
+    const int t = e ? 0 : (ctx + kTile - 1) / kTile * ups;
+    spre_s[i] = t;
+    my_t += t;
+    my_bits |= e;
+    if (blockIdx.x == 0) sctx[i] = e ? 0 : ctx;
+  }
+  int it = my_t, ob = my_bits;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, it, o);
+    if (lane >= o) it += v;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ob |= __shfl_xor_sync(0xffffffffu, ob, o);
+  if (lane == 31) s_red[0][warp] = it;
+  if (lane == 0) s_red[1][warp] = ob;
+  __syncthreads();
+  int base = 0, T = 0, bits = 0;
+  for (int w = 0; w < NWP; ++w) {
+    if (w < warp) base += s_red[0][w];
+    T += s_red[0][w];
+    bits |= s_red[1][w];
+  }
+  int run = base + it - my_t;
+  for (int i = i0; i < i1; ++i) {
+    const int t = spre_s[i];
+    spre_s[i] = run;
+    run += t;
+  }
+  if (tid == 0) spre_s[num_seqs] = T;
+  __syncthreads();
+  if (blockIdx.x == 0)
+    for (int i = tid; i <= num_seqs; i += NT) spre[i] = spre_s[i];
+  // pool row of stream tile g (-1 for a bad block id)
+  auto row_of = [&](int g, int& bad) -> int {
+    int lo = 0, hi = num_seqs;  // spre_s[lo] <= g < spre_s[hi]: lo has tiles
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (spre_s[mid] <= g)
+        lo = mid;
+      else
+        hi = mid;
+    }
+    const int ut = (spre_s[lo + 1] - spre_s[lo]) / ups;
+    const int off = g - spre_s[lo];
+    const int k = off / ut, t = off - k * ut;
+    const int kvh = k / head_groups;
+    const int tok = t * kTile;
+    const int bi = tok / block_size;
+    const int64_t b = __ldg(bt + (int64_t)lo * bt_s0 + bi);
+    if (b >= 0 && b < num_blocks) return ((int)b * num_kv_heads + kvh) * block_size + (tok - bi * block_size);
+    bad = MVB_DEV_BLOCK_ID;
+    return -1;
+  };
+  int my_bad = 0;
+  const int C = gridDim.x;
+  const int g0 = (int)((int64_t)blockIdx.x * T / C), g1 = (int)((int64_t)(blockIdx.x + 1) * T / C);
+  for (int g = g0 + tid; g < g1; g += NT) srows[g] = row_of(g, my_bad);
+  const int w0 = (int)((int64_t)blockIdx.x * num_warps / C), w1 = (int)((int64_t)(blockIdx.x + 1) * num_warps / C);
+  for (int e = tid; e < (w1 - w0) * 32; e += NT) {
+    const int W = w0 + e / 32, j = e % 32;
+    const int r0 = (int)((int64_t)W * T / num_warps), r1 = (int)((int64_t)(W + 1) * T / num_warps);
+    if (j == 0) srec[W].h = make_int4(r0, r1 - r0, 0, 0);
+    srec[W].rows[j] = r0 + j < r1 ? row_of(r0 + j, my_bad) : -1;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) my_bad |= __shfl_xor_sync(0xffffffffu, my_bad, o);
+  if (lane == 0 && (my_bad | (blockIdx.x == 0 && tid == 0 ? bits : 0))) atomicOr(err, my_bad | bits);
+  if (blockIdx.x == 0 && tid == 0) {
+    hdr->total_tiles = T;
+    hdr->num_warps = num_warps;
+    // every CTA's block-id errors are reported by the CTA itself; the header
+    // carries the sequence errors, OR-ed in again by each decode
+    hdr->bits = bits;
+  }
+  if (wait_at_end) grid_dependency_wait();
+}
+
 // ---------------------------------------------------------------------------
 // host launch
 // ---------------------------------------------------------------------------
@@ -696,18 +870,14 @@ int stream_smem_bytes(int head_dim, int num_seqs) {
          (2 * num_seqs + 1) * 4;
 }
 
+// CTAs of the stream grid: the CTAs the GPU holds at once, capped by the
+// warps the workspace covers.  The per-step schedule is cut for this grid.
 template <typename T, int D>
-cudaError_t launch_stream_t(const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a,
-                            int* scratch, float* part, int max_warps, int sm_count,
-                            cudaStream_t stream) {
+cudaError_t stream_ctas_t(int num_seqs, int max_warps, int sm_count, int* ctas_out) {
   constexpr int NW = StreamConfig<D>::NW, STAGES = StreamConfig<D>::STAGES;
   auto kern = decode_stream_kernel<T, D, NW, STAGES>;
-  const int smem = stream_smem_bytes(D, a.num_seqs);
+  const int smem = stream_smem_bytes(D, num_seqs);
   cudaError_t e = ensure_kernel_attrs(kern, smem);
-  if (e != cudaSuccess) return e;
-  e = ensure_kernel_attrs(decode_stream_fixup_kernel<T, D>, 0);
-  if (e != cudaSuccess) return e;
-  e = ensure_kernel_attrs(decode_stream_fixup_cta_kernel<T, D>, 0);
   if (e != cudaSuccess) return e;
   // Resident CTAs per SM, queried once per (device, shared-memory size): the
   // query costs microseconds of host time, and this runs once per layer-step.
@@ -734,10 +904,35 @@ cudaError_t launch_stream_t(const CUtensorMap& tmk, const CUtensorMap& tmv, cons
   int ctas = per_sm * sm_count;
   if (ctas * NW > max_warps) ctas = max_warps / NW;
   if (ctas < 1) return cudaErrorInvalidConfiguration;
-  StreamArgs sa;
+  *ctas_out = ctas;
+  return cudaSuccess;
+}
+
+template <typename T, int D>
+cudaError_t launch_stream_t(const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a,
+                            int* scratch, float* part, int max_warps, int sm_count, const StreamSchedPtrs* sp,
+                            cudaStream_t stream) {
+  constexpr int NW = StreamConfig<D>::NW, STAGES = StreamConfig<D>::STAGES;
+  auto kern = decode_stream_kernel<T, D, NW, STAGES>;
+  const int smem = stream_smem_bytes(D, a.num_seqs);
+  int ctas = 0;
+  cudaError_t e = stream_ctas_t<T, D>(a.num_seqs, max_warps, sm_count, &ctas);
+  if (e != cudaSuccess) return e;
+  e = ensure_kernel_attrs(decode_stream_fixup_kernel<T, D>, 0);
+  if (e != cudaSuccess) return e;
+  e = ensure_kernel_attrs(decode_stream_fixup_cta_kernel<T, D>, 0);
+  if (e != cudaSuccess) return e;
+  StreamArgs sa = {};
   sa.desc = reinterpret_cast<int4*>(scratch);
   sa.part = part;
   sa.num_warps = ctas * NW;
+  if (sp != nullptr) {
+    sa.shdr = static_cast<const StreamSchedHeader*>(sp->hdr);
+    sa.spre = sp->pre;
+    sa.sctx = sp->ctx;
+    sa.srows = sp->rows;
+    sa.srec = static_cast<const StreamRec*>(sp->rec);
+  }
   e = launch_pdl(kern, dim3(ctas), dim3(NW * 32), smem, stream, tmk, tmv, a, sa);
   if (e != cudaSuccess) return e;
   // Stream warps per unit = the pieces an average unit is cut into: few (many
@@ -753,14 +948,37 @@ cudaError_t launch_stream_t(const CUtensorMap& tmk, const CUtensorMap& tmv, cons
 
 cudaError_t launch_decode_stream(const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a,
                                  int dtype, int head_dim, int* scratch, float* part, int max_warps,
-                                 int sm_count, cudaStream_t stream) {
+                                 int sm_count, const StreamSchedPtrs* sp, cudaStream_t stream) {
   if (dtype == MVB_DTYPE_BF16)
     return head_dim == 64
-               ? launch_stream_t<__nv_bfloat16, 64>(tmk, tmv, a, scratch, part, max_warps, sm_count, stream)
-               : launch_stream_t<__nv_bfloat16, 128>(tmk, tmv, a, scratch, part, max_warps, sm_count, stream);
+               ? launch_stream_t<__nv_bfloat16, 64>(tmk, tmv, a, scratch, part, max_warps, sm_count, sp, stream)
+               : launch_stream_t<__nv_bfloat16, 128>(tmk, tmv, a, scratch, part, max_warps, sm_count, sp, stream);
   return head_dim == 64
-             ? launch_stream_t<__half, 64>(tmk, tmv, a, scratch, part, max_warps, sm_count, stream)
-             : launch_stream_t<__half, 128>(tmk, tmv, a, scratch, part, max_warps, sm_count, stream);
+             ? launch_stream_t<__half, 64>(tmk, tmv, a, scratch, part, max_warps, sm_count, sp, stream)
+             : launch_stream_t<__half, 128>(tmk, tmv, a, scratch, part, max_warps, sm_count, sp, stream);
+}
+
+cudaError_t launch_decode_stream_schedule(const DecodeArgs& a, int dtype, int head_dim, int max_warps, int sm_count,
+                                          const StreamSchedPtrs& sp, bool wait_at_end, cudaStream_t stream) {
+  int ctas = 0;
+  cudaError_t e;
+  if (dtype == MVB_DTYPE_BF16)
+    e = head_dim == 64 ? stream_ctas_t<__nv_bfloat16, 64>(a.num_seqs, max_warps, sm_count, &ctas)
+                       : stream_ctas_t<__nv_bfloat16, 128>(a.num_seqs, max_warps, sm_count, &ctas);
+  else
+    e = head_dim == 64 ? stream_ctas_t<__half, 64>(a.num_seqs, max_warps, sm_count, &ctas)
+                       : stream_ctas_t<__half, 128>(a.num_seqs, max_warps, sm_count, &ctas);
+  if (e != cudaSuccess) return e;
+  const int num_warps = ctas * stream_warps_per_cta(head_dim);
+  auto kern = decode_stream_schedule_kernel;
+  const int smem = (a.num_seqs + 1) * 4;
+  e = ensure_kernel_attrs(kern, smem);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(kern, dim3(sm_count), dim3(kStreamSchedThreads), smem, stream, a.kv_len, a.bt, a.bt_s0,
+                    a.num_seqs, a.num_kv_heads, a.head_groups, a.block_size, a.max_blocks, a.num_blocks, num_warps,
+                    static_cast<StreamSchedHeader*>(sp.hdr), const_cast<int*>(sp.pre), const_cast<int*>(sp.ctx),
+                    const_cast<int*>(sp.rows), static_cast<StreamRec*>(const_cast<void*>(sp.rec)), a.err,
+                    wait_at_end ? 1 : 0);
 }
 
 }  // namespace mvb

@@ -85,6 +85,17 @@ struct PrefillArgs {
   int* err;
 };
 
+// The stream kernel's per-step schedule inside its workspace (pointers; the
+// layout is the plan's): header, tile prefix, servable kv_len, pool rows in
+// stream order, one record per stream warp.
+struct StreamSchedPtrs {
+  void* hdr;
+  const int* pre;
+  const int* ctx;
+  const int* rows;
+  const void* rec;
+};
+
 // Workspace layout of the scheduled decode (MVB_DECODE_SCHED): a 256-byte
 // header, one 256-byte record per CTA, the piece descriptors, the pool rows of
 // every tile, the list of sequences left out, the arrival counters of cut units

@@ -102,7 +102,8 @@ def test_schedule_matches_the_cpu_restatement(num_seqs, heads):
         ctx[:] = [1, 20000, 33]
     spec = W.build_spec("s", ctx, h, kh, d, 16, seed=1)
     t = W.torch_tensors(spec, torch.bfloat16, DEV)
-    sched = M.build_decode_schedule(t["kv_len"], t["block_tables"], h, kh, d, 16, spec.num_blocks, torch.bfloat16)
+    sched = M.build_decode_schedule(t["kv_len"], t["block_tables"], h, kh, d, 16, spec.num_blocks, torch.bfloat16,
+                                    variant="sched")
     torch.cuda.synchronize()
     check_schedule(read_schedule(sched, spec, h, kh, d), spec, h, kh, d)
 
@@ -110,7 +111,8 @@ def test_schedule_matches_the_cpu_restatement(num_seqs, heads):
 def test_one_schedule_serves_every_layer():
     spec = W.make_spec(2, seed=40)
     t = W.torch_tensors(spec, torch.bfloat16, DEV, num_layers=3)
-    sched = M.build_decode_schedule(t["kv_len"], t["block_tables"], 14, 2, 64, 16, spec.num_blocks, torch.bfloat16)
+    sched = M.build_decode_schedule(t["kv_len"], t["block_tables"], 14, 2, 64, 16, spec.num_blocks, torch.bfloat16,
+                                    variant="sched")
     for layer in range(3):
         out = M.paged_decode_attention(t["query"], t["key_caches"][layer], t["value_caches"][layer],
                                        t["block_tables"], t["kv_len"], 16, schedule=sched)
@@ -146,7 +148,7 @@ def test_long_units_many_ctas(head_dim, heads, kv_heads):
     spec = W.build_spec("long", ctx, heads, kv_heads, head_dim, 16, seed=41)
     t = W.torch_tensors(spec, torch.bfloat16, DEV)
     sched = M.build_decode_schedule(t["kv_len"], t["block_tables"], heads, kv_heads, head_dim, 16, spec.num_blocks,
-                                    torch.bfloat16)
+                                    torch.bfloat16, variant="sched")
     dev = read_schedule(sched, spec, heads, kv_heads, head_dim)
     want = check_schedule(dev, spec, heads, kv_heads, head_dim)
     assert max(d1[3] >> 1 for _, d1 in want["pieces"]) > 4
@@ -178,7 +180,8 @@ def test_write_then_decode_with_a_schedule(num_seqs):
     The new tokens dominate attention (K = 4, V = 3), so a decode that read
     the cache before the write landed would be far off."""
     spec, t, ref = _write_then_decode_case(33, num_seqs)
-    sched = M.build_decode_schedule(t["kv_len"], t["block_tables"], 14, 2, 64, 16, spec.num_blocks, torch.bfloat16)
+    sched = M.build_decode_schedule(t["kv_len"], t["block_tables"], 14, 2, 64, 16, spec.num_blocks, torch.bfloat16,
+                                    variant="sched")
     outs = []
     for _ in range(3):
         kc, vc = t["key_caches"][0].clone(), t["value_caches"][0].clone()

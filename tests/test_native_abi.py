@@ -186,20 +186,37 @@ def test_schedule_host_checks_without_gpu():
     lib = _native.lib()
 
     def call(num_seqs, kv_len=None, bt=None, bt_stride=8, ws=None, wsb=0, flags=0, dtype=_native.DTYPE_BF16,
-             err=None):
-        return lib.mvb_paged_decode_schedule(kv_len, bt, bt_stride, num_seqs, 14, 2, 64, 16, 100, 8, dtype, flags,
-                                             ws, wsb, err, None)
+             err=None, variant=_native.DECODE_SCHED):
+        return lib.mvb_paged_decode_schedule(kv_len, bt, bt_stride, num_seqs, 14, 2, 64, 16, 100, 8, dtype,
+                                             variant, flags, ws, wsb, err, None)
 
-    assert call(0) == _native.OK  # empty batch: nothing launched
-    assert call(1) == _native.ERR_INVALID_ARG  # null kv_len
-    assert call(1, kv_len=16, err=16) == _native.ERR_INVALID_ARG  # null block table
-    assert call(1, kv_len=16, bt=16, bt_stride=4, err=16) == _native.ERR_INVALID_ARG  # rows shorter than 8 blocks
-    assert call(1, dtype=_native.DTYPE_F32) == _native.ERR_VARIANT  # the scheduled kernel is bf16 / f16 only
-    assert call(1, kv_len=16, bt=16, err=16, flags=0x400) == _native.ERR_INVALID_ARG  # unknown flag
-    assert call(1, kv_len=16, bt=16, err=16) == _native.ERR_WORKSPACE  # no workspace
-    assert call(1, kv_len=16, bt=16, err=16, ws=256 * 7 + 16, wsb=1 << 30) == _native.ERR_WORKSPACE  # misaligned
+    for v in (_native.DECODE_SCHED, _native.DECODE_STREAM):
+        assert call(0, variant=v) == _native.OK  # empty batch: nothing launched
+        assert call(1, variant=v) == _native.ERR_INVALID_ARG  # null kv_len
+        assert call(1, kv_len=16, err=16, variant=v) == _native.ERR_INVALID_ARG  # null block table
+        # rows shorter than 8 blocks
+        assert call(1, kv_len=16, bt=16, bt_stride=4, err=16, variant=v) == _native.ERR_INVALID_ARG
+        assert call(1, dtype=_native.DTYPE_F32, variant=v) == _native.ERR_VARIANT  # bf16 / f16 kernels only
+        assert call(1, kv_len=16, bt=16, err=16, flags=0x400, variant=v) == _native.ERR_INVALID_ARG  # unknown flag
+        assert call(1, kv_len=16, bt=16, err=16, variant=v) == _native.ERR_WORKSPACE  # no workspace
+        # misaligned
+        assert call(1, kv_len=16, bt=16, err=16, ws=256 * 7 + 16, wsb=1 << 30, variant=v) == _native.ERR_WORKSPACE
     # more sequences than the schedule kernel's prefix arrays hold: the plan refuses the variant
     assert call(16385, kv_len=16, bt=16, err=16) == _native.ERR_VARIANT
+    assert call(4097, kv_len=16, bt=16, err=16, variant=_native.DECODE_STREAM) == _native.ERR_VARIANT
+    # kernels without a per-step set-up: nothing to build, nothing launched
+    assert call(1, kv_len=16, bt=16, err=16, variant=_native.DECODE_MMA) == _native.OK
+    assert call(1, dtype=_native.DTYPE_F32, variant=_native.DECODE_AUTO) == _native.OK  # fp32 plans the FMA kernel
+
+
+def test_plan_stream_workspace_holds_the_schedule():
+    """The stream kernel's workspace: tile prefix and context lengths, the
+    per-warp partial slots, then the per-step schedule (header, per-warp
+    records of 144 bytes, the rows in stream order)."""
+    p = _plan(variant="stream", num_seqs=256, max_blocks_per_seq=128)
+    warps = 148 * 3 * 4  # 3 CTAs of 4 warps per SM at head_dim 64 (an upper bound: the plan sizes for it)
+    tiles = 256 * 2 * 128
+    assert p["workspace_bytes"] >= 256 + warps * 144 + tiles * 4 + (2 * 256 + 1) * 4
 
 
 def test_direct_binding_loads_and_routes_cpu_tensors_to_the_full_path():
