@@ -373,7 +373,7 @@ def ours(args, rank, world, local_rank):
 
     # launches per layer-step of this repository's kernels: write + decode
     # (+ the stream kernel's fixup / split-K reduction); the schedule once per model step
-    per_layer = 2 + (1 if plan["num_partitions"] > 1 or plan["variant"] == "stream" else 0)
+    per_layer = 1 + plan["launches"] - (1 if plan["variant"] == "sched" else 0)
 
     # correctness gate before timing: one strict step through the public API
     M.paged_cache_write(nk, nv, kcs[0], vcs[0], slots, spec.block_size)

@@ -294,18 +294,22 @@ int mvb_kv_cache_write(const void* key, int64_t key_stride_token, int64_t key_st
 /*
  * Plan a paged decode: picks the kernel variant and the split-K partition
  * length for the given shape and returns the workspace size in bytes (0 when
- * the decode needs none).  MVB_DECODE_STREAM reports partition_tokens = 0 and
- * num_partitions = 0; its workspace needs no initialisation.  `variant` /
- * `partition_tokens` are the caller's requests (MVB_DECODE_AUTO / 0 = let the library choose).
- * `cache_ptr` is only inspected for TMA alignment (it may be NULL, in which
- * case alignment is assumed).
+ * the decode needs none) and the number of kernels one mvb_paged_decode call
+ * launches without MVB_DECODE_SCHEDULE_READY (launches_out; NULL to skip).
+ * MVB_DECODE_STREAM reports partition_tokens = 0 and num_partitions = 0; its
+ * workspace needs no initialisation, and one workspace serves one stream at a
+ * time.  `variant` / `partition_tokens` are the caller's
+ * requests (MVB_DECODE_AUTO / 0 = let the library choose).  `cache_ptr` is
+ * only inspected for TMA alignment (it may be NULL, in which case alignment
+ * is assumed).
  */
 int mvb_paged_decode_plan(int32_t num_seqs, int32_t num_heads, int32_t num_kv_heads,
                           int32_t head_dim, int32_t block_size, int32_t num_blocks,
                           int32_t max_blocks_per_seq, int32_t dtype,
                           int32_t variant, int32_t partition_tokens, const void* cache_ptr,
                           int32_t* variant_out, int32_t* partition_tokens_out,
-                          int32_t* num_partitions_out, int64_t* workspace_bytes_out);
+                          int32_t* num_partitions_out, int64_t* workspace_bytes_out,
+                          int32_t* launches_out);
 
 /*
  * Paged decode attention, one query token per sequence:

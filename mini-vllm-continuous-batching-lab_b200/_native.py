@@ -51,7 +51,7 @@ DECODE_SCHED = 4
 DECODE_AFTER_WRITE = 0x100
 DECODE_SCHEDULE_READY = 0x200
 
-ABI_VERSION = 5
+ABI_VERSION = 6
 
 # Every symbol include/mini_vllm_b200.h declares, with (restype, argtypes).
 _i32, _i64, _u32, _f32, _vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_uint32, ctypes.c_float, ctypes.c_void_p
@@ -67,7 +67,7 @@ SIGNATURES = {
     "mvb_paged_decode_plan": (
         _i32,
         [_i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _vp,
-         _p_i32, _p_i32, _p_i32, _p_i64],
+         _p_i32, _p_i32, _p_i32, _p_i64, _p_i32],
     ),
     "mvb_paged_decode": (
         _i32,

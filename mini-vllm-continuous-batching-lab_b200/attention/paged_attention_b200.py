@@ -107,9 +107,9 @@ class _DeviceState:
     def workspace(self, nbytes: int, variant: str, stream: int = 0) -> torch.Tensor:
         """Decode workspace of one kernel variant (the stream, scheduled and
         split-K kernels each keep their own buffer), zero-filled when allocated.
-        The scheduled kernel's holds its schedule and hand-out counters, so each
-        stream gets its own."""
-        key = ("sched", stream) if variant == "sched" else variant if variant == "stream" else "split"
+        The stream and scheduled kernels' hold arrival counters (and the
+        scheduled kernel's its schedule), so each stream gets its own."""
+        key = (variant, stream) if variant in ("sched", "stream") else "split"
         buf = self._workspaces.get(key)
         if buf is None or buf.numel() < nbytes:
             buf = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
@@ -414,16 +414,16 @@ def decode_plan(
     """The library's launch plan for a decode of this shape (no GPU work)."""
     import ctypes
 
-    v, pt, np_ = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
+    v, pt, np_, nl = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
     ws = ctypes.c_int64()
     status = _native.lib().mvb_paged_decode_plan(
         num_seqs, num_heads, num_kv_heads, head_dim, block_size, num_blocks, max_blocks_per_seq,
         _DTYPE_CODES[dtype], _VARIANTS[variant], int(partition_tokens or 0), cache_ptr or None,
-        ctypes.byref(v), ctypes.byref(pt), ctypes.byref(np_), ctypes.byref(ws),
+        ctypes.byref(v), ctypes.byref(pt), ctypes.byref(np_), ctypes.byref(ws), ctypes.byref(nl),
     )
     _host_status(status, "paged decode plan")
     return {"variant": _VARIANT_NAMES[v.value], "partition_tokens": pt.value,
-            "num_partitions": np_.value, "workspace_bytes": ws.value}
+            "num_partitions": np_.value, "workspace_bytes": ws.value, "launches": nl.value}
 
 
 def _decode_fast(query, key_cache, value_cache, block_table, kv_len_after, block_size, scale, out, variant,

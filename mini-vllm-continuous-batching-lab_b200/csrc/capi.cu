@@ -55,7 +55,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 namespace {
 
-constexpr int kAbiVersion = 5;
+constexpr int kAbiVersion = 6;
 // Longest context the auto plan serves with one CTA per (sequence, KV head);
 // beyond it the flash-decoding split is used.
 constexpr int64_t kUnsplitMaxTokens = 8192;
@@ -214,7 +214,7 @@ int make_plan(int num_seqs, int num_heads, int num_kv_heads, int head_dim, int b
     pl->max_bids = 0;
     pl->max_warps = per_sm * sm_count_current() * nw;
     pl->off_m = pl->off_l = 0;
-    pl->off_part = round_up((int64_t)per_sm * sm_count_current() * nw * 32, 256);
+    pl->off_part = round_up((int64_t)pl->max_warps * 32, 256);
     // the per-step schedule (MVB_DECODE_SCHEDULE_READY): header, tile prefix,
     // servable kv_len, one row per tile, one 144-byte record per warp
     pl->off_shdr = round_up(pl->off_part + (int64_t)pl->max_warps * 2 * 16 * (head_dim + 2) * 4, 256);
@@ -386,7 +386,7 @@ int mvb_paged_decode_plan(int32_t num_seqs, int32_t num_heads, int32_t num_kv_he
                           int32_t max_blocks_per_seq, int32_t dtype, int32_t variant,
                           int32_t partition_tokens, const void* cache_ptr, int32_t* variant_out,
                           int32_t* partition_tokens_out, int32_t* num_partitions_out,
-                          int64_t* workspace_bytes_out) {
+                          int64_t* workspace_bytes_out, int32_t* launches_out) {
   Plan pl;
   variant &= ~(MVB_DECODE_AFTER_WRITE | MVB_DECODE_SCHEDULE_READY);  // launch-ordering hints: no effect on the plan
   const int st = make_plan(num_seqs, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
@@ -396,6 +396,15 @@ int mvb_paged_decode_plan(int32_t num_seqs, int32_t num_heads, int32_t num_kv_he
   if (partition_tokens_out) *partition_tokens_out = pl.part_tokens;
   if (num_partitions_out) *num_partitions_out = pl.num_parts;
   if (workspace_bytes_out) *workspace_bytes_out = pl.ws_bytes;
+  if (launches_out) {
+    // kernels one mvb_paged_decode call launches (without MVB_DECODE_SCHEDULE_READY)
+    if (pl.variant == MVB_DECODE_SCHED)
+      *launches_out = 2;  // schedule + decode
+    else if (pl.variant == MVB_DECODE_STREAM)
+      *launches_out = 2;  // + the fixup
+    else
+      *launches_out = pl.num_parts > 1 ? 2 : 1;  // + the split-K reduction
+  }
   return MVB_OK;
 }
 

@@ -64,11 +64,11 @@ extern "C" int mvb_paged_decode_noalloc(
   if (variant == MVB_DECODE_AUTO || variant == MVB_DECODE_MMA)
     st = mvb_paged_decode_plan(num_seqs, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
                                max_blocks_per_seq, dtype, MVB_DECODE_MMA, partition_tokens, key_cache,
-                               &v, &pt, &parts, &ws);
+                               &v, &pt, &parts, &ws, nullptr);
   if (st == MVB_ERR_VARIANT && variant != MVB_DECODE_MMA)
     st = mvb_paged_decode_plan(num_seqs, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
                                max_blocks_per_seq, dtype, MVB_DECODE_FMA, partition_tokens, key_cache,
-                               &v, &pt, &parts, &ws);
+                               &v, &pt, &parts, &ws, nullptr);
   if (st != MVB_OK) return st;
   if (ws > mvb::kNoAllocScratchBytes) return MVB_ERR_WORKSPACE;
   void* scratch = nullptr;

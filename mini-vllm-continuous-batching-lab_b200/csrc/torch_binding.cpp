@@ -45,10 +45,12 @@ int dtype_code(at::ScalarType t) {
 std::mutex g_ws_mu;
 std::vector<at::Tensor> g_ws[3];
 
-// The scheduled kernel's workspace holds its schedule and hand-out counters,
-// so calls on different streams, which may overlap, each get their own.
+// The stream and scheduled kernels' workspaces hold arrival counters (and the
+// scheduled kernel's its schedule), so calls on different streams, which may
+// overlap, each get their own.
 struct StreamWorkspace {
   int dev;
+  int kind;
   cudaStream_t stream;
   at::Tensor t;
 };
@@ -56,21 +58,20 @@ std::vector<StreamWorkspace> g_ws_stream;
 
 at::Tensor workspace(int dev, int kind, int64_t nbytes, cudaStream_t stream) {
   std::lock_guard<std::mutex> lock(g_ws_mu);
-  if (kind == 2) {
+  auto zeros = [&]() { return at::zeros({nbytes}, at::TensorOptions().dtype(at::kByte).device(at::kCUDA, dev)); };
+  if (kind == 0 || kind == 2) {
     for (StreamWorkspace& w : g_ws_stream) {
-      if (w.dev != dev || w.stream != stream) continue;
-      if (w.t.numel() < nbytes)
-        w.t = at::zeros({nbytes}, at::TensorOptions().dtype(at::kByte).device(at::kCUDA, dev));
+      if (w.dev != dev || w.kind != kind || w.stream != stream) continue;
+      if (w.t.numel() < nbytes) w.t = zeros();
       return w.t;
     }
-    g_ws_stream.push_back({dev, stream, at::zeros({nbytes}, at::TensorOptions().dtype(at::kByte).device(at::kCUDA, dev))});
+    g_ws_stream.push_back({dev, kind, stream, zeros()});
     return g_ws_stream.back().t;
   }
   std::vector<at::Tensor>& v = g_ws[kind];
   if ((int)v.size() <= dev) v.resize(dev + 1);
   at::Tensor& t = v[dev];
-  if (!t.defined() || t.numel() < nbytes)
-    t = at::zeros({nbytes}, at::TensorOptions().dtype(at::kByte).device(at::kCUDA, dev));
+  if (!t.defined() || t.numel() < nbytes) t = zeros();
   return t;
 }
 
@@ -174,7 +175,7 @@ std::tuple<int64_t, at::Tensor> decode(const at::Tensor& query, const at::Tensor
   int st = mvb_paged_decode_plan(
       (int32_t)nd, (int32_t)query.size(1), (int32_t)key_cache.size(1), (int32_t)query.size(2),
       (int32_t)block_size, (int32_t)key_cache.size(0), (int32_t)block_table.size(1), dt, (int32_t)variant,
-      (int32_t)partition_tokens, key_cache.data_ptr(), &v, &pt, &parts, &ws_bytes);
+      (int32_t)partition_tokens, key_cache.data_ptr(), &v, &pt, &parts, &ws_bytes, nullptr);
   if (st != MVB_OK) return {st, out};
   cudaStream_t stream = c10::cuda::getCurrentCUDAStream(dev).stream();
   void* ws = nullptr;

@@ -62,6 +62,22 @@ def test_wait_that_runs_out_is_reported_and_the_context_stays_usable(variant):
     assert (s2 == 0).all()
     g = res.float().cpu().numpy()
     assert (np.abs(g - ref) <= 2e-3 + 1e-2 * np.abs(ref)).all()
+    # the failed call's own workspace serves the next decode: the arrival
+    # counters of cut units ended at zero (the timed-out warp still counted its
+    # pieces in), so every cut unit is merged again
+    err.zero_()
+    out2 = torch.full_like(q, 9.0)
+    st = _native.lib().mvb_paged_decode(
+        q.data_ptr(), q.stride(0), q.stride(1), kc.data_ptr(), vc.data_ptr(), bt.data_ptr(), bt.stride(0),
+        bt.shape[1], kvl.data_ptr(), out2.data_ptr(), out2.stride(0), out2.stride(1), spec.num_seqs, 14, 2, 64, 16,
+        spec.num_blocks, 0.125, _native.DTYPE_BF16,
+        _native.DECODE_STREAM if variant == "stream" else _native.DECODE_SCHED, 0, ws.data_ptr(), ws.numel(),
+        err.data_ptr(), torch.cuda.current_stream(DEV).cuda_stream)
+    assert st == _native.OK, _native.status_string(st)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    g2 = out2.float().cpu().numpy()
+    assert (np.abs(g2 - ref) <= 2e-3 + 1e-2 * np.abs(ref)).all()
 
 
 def test_hook_rejects_bad_arguments():

@@ -101,6 +101,15 @@ def test_plan_scheduled_kernel_when_asked():
     assert lay["bytes"] >= 256 + 148 * 256 + 660 * 32 + 65536 * 4 + 256 * 4 + 148 * 4 + 296 * 7 * 68 * 4
 
 
+def test_plan_launches():
+    """Kernels one decode call launches: the stream kernel + its fixup;
+    split-K + its reduction; the scheduled kernel's schedule + decode."""
+    assert _plan(variant="stream")["launches"] == 2
+    assert _plan(variant="mma", partition_tokens=512)["launches"] == 2
+    assert _plan(variant="mma")["launches"] == 1
+    assert _plan(variant="sched")["launches"] == 2
+
+
 def test_plan_stream_kernel_when_asked():
     p = _plan(variant="stream")
     assert p["variant"] == "stream" and p["num_partitions"] == 0
@@ -110,7 +119,7 @@ def test_plan_stream_kernel_when_asked():
 
 def test_plan_one_cta_per_sequence_and_kv_head_when_asked():
     p = _plan(variant="mma")
-    assert p == {"variant": "mma", "partition_tokens": 2048, "num_partitions": 1, "workspace_bytes": 0}
+    assert p == {"variant": "mma", "partition_tokens": 2048, "num_partitions": 1, "workspace_bytes": 0, "launches": 1}
 
 
 def test_plan_stream_limits():
@@ -210,9 +219,9 @@ def test_schedule_host_checks_without_gpu():
 
 
 def test_plan_stream_workspace_holds_the_schedule():
-    """The stream kernel's workspace: tile prefix and context lengths, the
-    per-warp partial slots, then the per-step schedule (header, per-warp
-    records of 144 bytes, the rows in stream order)."""
+    """The stream kernel's workspace: the per-warp descriptors and partial
+    slots, then the per-step schedule (header, tile prefix and context
+    lengths, the rows in stream order, per-warp records of 144 bytes)."""
     p = _plan(variant="stream", num_seqs=256, max_blocks_per_seq=128)
     warps = 148 * 3 * 4  # 3 CTAs of 4 warps per SM at head_dim 64 (an upper bound: the plan sizes for it)
     tiles = 256 * 2 * 128
