@@ -114,7 +114,7 @@ struct Plan {
   int max_warps;         // stream variant: warps the partial-state slots cover
   int64_t off_part;      // stream variant: workspace offset of the partial slots
   // stream variant: its per-step schedule after the per-launch part
-  int64_t off_shdr, off_spre, off_sctx, off_srows, off_srec;
+  int64_t off_shdr, off_spre, off_sctx, off_srows, off_srec, off_sdesc;
   SchedLayout sched;     // sched variant: workspace layout
 };
 
@@ -125,6 +125,7 @@ StreamSchedPtrs stream_sched_ptrs(const Plan& pl, char* ws) {
   sp.ctx = reinterpret_cast<const int*>(ws + pl.off_sctx);
   sp.rows = reinterpret_cast<const int*>(ws + pl.off_srows);
   sp.rec = ws + pl.off_srec;
+  sp.desc = ws + pl.off_sdesc;
   return sp;
 }
 
@@ -216,13 +217,15 @@ int make_plan(int num_seqs, int num_heads, int num_kv_heads, int head_dim, int b
     pl->off_m = pl->off_l = 0;
     pl->off_part = round_up((int64_t)pl->max_warps * 32, 256);
     // the per-step schedule (MVB_DECODE_SCHEDULE_READY): header, tile prefix,
-    // servable kv_len, one row per tile, one 144-byte record per warp
+    // servable kv_len, one row per tile, one 144-byte record and one 32-byte
+    // fixup descriptor per warp
     pl->off_shdr = round_up(pl->off_part + (int64_t)pl->max_warps * 2 * 16 * (head_dim + 2) * 4, 256);
     pl->off_spre = pl->off_shdr + 256;
     pl->off_sctx = round_up(pl->off_spre + ((int64_t)num_seqs + 1) * 4, 256);
     pl->off_srows = round_up(pl->off_sctx + (int64_t)num_seqs * 4, 256);
     pl->off_srec = round_up(pl->off_srows + (int64_t)num_seqs * khg16 * max_ctx_tiles * 4, 256);
-    pl->ws_bytes = pl->off_srec + (int64_t)pl->max_warps * 144;
+    pl->off_sdesc = round_up(pl->off_srec + (int64_t)pl->max_warps * 144, 256);
+    pl->ws_bytes = pl->off_sdesc + (int64_t)pl->max_warps * 32;
     return MVB_OK;
   }
   pl->max_warps = 0;

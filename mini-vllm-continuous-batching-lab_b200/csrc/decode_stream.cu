@@ -30,6 +30,9 @@
 namespace mvb {
 
 constexpr int kStreamRowBatch = 128;  // tiles whose pool rows a warp resolves at once
+#ifndef MVB_STREAM_FIXUP_CB
+#define MVB_STREAM_FIXUP_CB 4
+#endif
 
 // Per-step schedule of the stream kernel (MVB_DECODE_SCHEDULE_READY): what
 // every layer of a model step would otherwise derive again from kv_len and the
@@ -59,6 +62,7 @@ struct StreamArgs {
   const int* sctx;        // [Nd] servable kv_len (0 = left out)
   const int* srows;       // [total_tiles] pool row of every tile, in stream order
   const StreamRec* srec;  // [num_warps]
+  const int4* sdesc;      // [num_warps][2] the schedule's copy of `desc` (the fixup reads it)
 };
 
 // Warp whose range [R(w), R(w+1)), R(w) = floor(w * T / Wtot), holds global
@@ -437,15 +441,20 @@ template <typename T, int D>
 __global__ void __launch_bounds__(128) decode_stream_fixup_kernel(const DecodeArgs a, const StreamArgs sa) {
   constexpr int ROW = D + 2, DPL = D / 32;
   constexpr int RP = D == 64 ? 8 : 4;  // head rows per pass
-  constexpr int CB = 4;                // contributors per batch of O loads (divides 32)
-  grid_dependency_wait();  // the streaming kernel's partials and descriptors are visible
+  constexpr int CB = MVB_STREAM_FIXUP_CB;  // contributors per batch of O loads (divides 32)
   const int lane = threadIdx.x & 31;
   const int w_first = blockIdx.x * 4 + (threadIdx.x >> 5);
   const int Wtot = sa.num_warps;
+  // The descriptor in one round trip: with a schedule its copy there, written
+  // before the stream kernel ran, so it is read while that kernel finishes and
+  // warps without a unit leave at once; else the stream kernel's, after it.
+  if (sa.sdesc == nullptr) grid_dependency_wait();
   if (w_first >= Wtot) return;
-  const int4 d0 = __ldcg(sa.desc + 2 * w_first);
+  const int4* dsrc = sa.sdesc != nullptr ? sa.sdesc : sa.desc;
+  const int4 d0 = __ldcg(dsrc + 2 * w_first);
+  const int4 d1 = __ldcg(dsrc + 2 * w_first + 1);
   if (d0.x < 0) return;
-  const int4 d1 = __ldcg(sa.desc + 2 * w_first + 1);
+  if (sa.sdesc != nullptr) grid_dependency_wait();  // the streaming kernel's partials are visible
   const int us = d0.x, ue = d0.y, seq = d0.z, T_all = d0.w, h0 = d1.x, nrows = d1.y;
   const bool dense = T_all >= Wtot;
   const int nct = dense ? stream_warp_of(ue - 1, T_all, Wtot) - w_first + 1 : ue - us;
@@ -583,7 +592,7 @@ __global__ void __launch_bounds__(kFixupWarps * 32) decode_stream_fixup_cta_kern
   const int Wtot = sa.num_warps;
   if (threadIdx.x < 2 * FW) {  // the FW descriptors of this CTA's stream warps, in one round trip
     const int w = blockIdx.x * FW + (threadIdx.x >> 1);
-    s_desc[threadIdx.x >> 1][threadIdx.x & 1] = w < Wtot ? __ldcg(sa.desc + 2 * w + (threadIdx.x & 1))
+    s_desc[threadIdx.x >> 1][threadIdx.x & 1] = w < Wtot ? __ldcg((sa.sdesc != nullptr ? sa.sdesc : sa.desc) + 2 * w + (threadIdx.x & 1))
                                                          : make_int4(-1, 0, 0, 0);
   }
   __syncthreads();
@@ -741,8 +750,8 @@ __device__ __forceinline__ int stream_sched_seq_error(int ctx, int block_size, i
 __global__ void __launch_bounds__(kStreamSchedThreads)
 decode_stream_schedule_kernel(const int* __restrict__ kv_len, const int64_t* __restrict__ bt, int64_t bt_s0,
                               int num_seqs, int num_kv_heads, int head_groups, int block_size, int max_blocks,
-                              int num_blocks, int num_warps, StreamSchedHeader* hdr, int* spre, int* sctx,
-                              int* srows, StreamRec* srec, int* err, int wait_at_end) {
+                              int num_blocks, int G, int num_warps, StreamSchedHeader* hdr, int* spre, int* sctx,
+                              int* srows, StreamRec* srec, int4* sdesc, int* err, int wait_at_end) {
   extern __shared__ int spre_s[];  // [num_seqs + 1]
   constexpr int NT = kStreamSchedThreads, NWP = NT / 32;
   __shared__ int s_red[2][NWP];
@@ -789,8 +798,8 @@ decode_stream_schedule_kernel(const int* __restrict__ kv_len, const int64_t* __r
   __syncthreads();
   if (blockIdx.x == 0)
     for (int i = tid; i <= num_seqs; i += NT) spre[i] = spre_s[i];
-  // pool row of stream tile g (-1 for a bad block id)
-  auto row_of = [&](int g, int& bad) -> int {
+  // the unit holding stream tile g: sequence s, unit k of it, its first tile us and its tiles ut
+  auto unit_of = [&](int g, int& s, int& k, int& us, int& ut) {
     int lo = 0, hi = num_seqs;  // spre_s[lo] <= g < spre_s[hi]: lo has tiles
     while (hi - lo > 1) {
       const int mid = (lo + hi) >> 1;
@@ -799,13 +808,19 @@ decode_stream_schedule_kernel(const int* __restrict__ kv_len, const int64_t* __r
       else
         hi = mid;
     }
-    const int ut = (spre_s[lo + 1] - spre_s[lo]) / ups;
-    const int off = g - spre_s[lo];
-    const int k = off / ut, t = off - k * ut;
+    s = lo;
+    ut = (spre_s[lo + 1] - spre_s[lo]) / ups;
+    k = (g - spre_s[lo]) / ut;
+    us = spre_s[lo] + k * ut;
+  };
+  // pool row of stream tile g (-1 for a bad block id)
+  auto row_of = [&](int g, int& bad) -> int {
+    int s, k, us, ut;
+    unit_of(g, s, k, us, ut);
     const int kvh = k / head_groups;
-    const int tok = t * kTile;
+    const int tok = (g - us) * kTile;
     const int bi = tok / block_size;
-    const int64_t b = __ldg(bt + (int64_t)lo * bt_s0 + bi);
+    const int64_t b = __ldg(bt + (int64_t)s * bt_s0 + bi);
     if (b >= 0 && b < num_blocks) return ((int)b * num_kv_heads + kvh) * block_size + (tok - bi * block_size);
     bad = MVB_DEV_BLOCK_ID;
     return -1;
@@ -818,7 +833,23 @@ decode_stream_schedule_kernel(const int* __restrict__ kv_len, const int64_t* __r
   for (int e = tid; e < (w1 - w0) * 32; e += NT) {
     const int W = w0 + e / 32, j = e % 32;
     const int r0 = (int)((int64_t)W * T / num_warps), r1 = (int)((int64_t)(W + 1) * T / num_warps);
-    if (j == 0) srec[W].h = make_int4(r0, r1 - r0, 0, 0);
+    if (j == 0) {
+      srec[W].h = make_int4(r0, r1 - r0, 0, 0);
+      // the fixup's descriptor of the unit this warp begins and its range
+      // cuts, as the decode kernel would write it
+      int4 d0 = make_int4(-1, 0, 0, 0), d1 = make_int4(0, 0, 0, 0);
+      if (r1 > r0) {
+        int s, k, us, ut;
+        unit_of(r1 - 1, s, k, us, ut);
+        if (us >= r0 && us + ut > r1) {
+          const int kvh = k / head_groups, hg = k - kvh * head_groups;
+          d0 = make_int4(us, us + ut, s, T);
+          d1 = make_int4(kvh * G + hg * 16, min(16, G - hg * 16), 0, 0);
+        }
+      }
+      sdesc[2 * W] = d0;
+      sdesc[2 * W + 1] = d1;
+    }
     srec[W].rows[j] = r0 + j < r1 ? row_of(r0 + j, my_bad) : -1;
   }
 #pragma unroll
@@ -932,6 +963,7 @@ cudaError_t launch_stream_t(const CUtensorMap& tmk, const CUtensorMap& tmv, cons
     sa.sctx = sp->ctx;
     sa.srows = sp->rows;
     sa.srec = static_cast<const StreamRec*>(sp->rec);
+    sa.sdesc = static_cast<const int4*>(sp->desc);
   }
   e = launch_pdl(kern, dim3(ctas), dim3(NW * 32), smem, stream, tmk, tmv, a, sa);
   if (e != cudaSuccess) return e;
@@ -975,9 +1007,11 @@ cudaError_t launch_decode_stream_schedule(const DecodeArgs& a, int dtype, int he
   e = ensure_kernel_attrs(kern, smem);
   if (e != cudaSuccess) return e;
   return launch_pdl(kern, dim3(sm_count), dim3(kStreamSchedThreads), smem, stream, a.kv_len, a.bt, a.bt_s0,
-                    a.num_seqs, a.num_kv_heads, a.head_groups, a.block_size, a.max_blocks, a.num_blocks, num_warps,
+                    a.num_seqs, a.num_kv_heads, a.head_groups, a.block_size, a.max_blocks, a.num_blocks, a.G,
+                    num_warps,
                     static_cast<StreamSchedHeader*>(sp.hdr), const_cast<int*>(sp.pre), const_cast<int*>(sp.ctx),
-                    const_cast<int*>(sp.rows), static_cast<StreamRec*>(const_cast<void*>(sp.rec)), a.err,
+                    const_cast<int*>(sp.rows), static_cast<StreamRec*>(const_cast<void*>(sp.rec)),
+                    static_cast<int4*>(const_cast<void*>(sp.desc)), a.err,
                     wait_at_end ? 1 : 0);
 }
 

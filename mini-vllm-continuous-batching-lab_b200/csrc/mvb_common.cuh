@@ -87,13 +87,14 @@ struct PrefillArgs {
 
 // The stream kernel's per-step schedule inside its workspace (pointers; the
 // layout is the plan's): header, tile prefix, servable kv_len, pool rows in
-// stream order, one record per stream warp.
+// stream order, one record and one fixup descriptor per stream warp.
 struct StreamSchedPtrs {
   void* hdr;
   const int* pre;
   const int* ctx;
   const int* rows;
   const void* rec;
+  const void* desc;
 };
 
 // Workspace layout of the scheduled decode (MVB_DECODE_SCHED): a 256-byte
