@@ -33,6 +33,15 @@ constexpr int kStreamRowBatch = 128;  // tiles whose pool rows a warp resolves a
 #ifndef MVB_STREAM_FIXUP_CB
 #define MVB_STREAM_FIXUP_CB 4
 #endif
+#ifndef MVB_STREAM_FIXUP_SPLIT
+#define MVB_STREAM_FIXUP_SPLIT 2
+#endif
+// The warp fixup's warps per cut unit, each merging its share of the unit's
+// head rows: half the rows per warp halve the merge's serial work and its
+// registers per contributor (config-2 decode with a schedule 34.1 -> 32.9 us,
+// without one 35.6 -> 34.6 us; four warps per unit, or 8 contributors per
+// batch, were slower).
+constexpr int kFixupWarpsPerUnit = MVB_STREAM_FIXUP_SPLIT;
 
 // Per-step schedule of the stream kernel (MVB_DECODE_SCHEDULE_READY): what
 // every layer of a model step would otherwise derive again from kv_len and the
@@ -440,10 +449,12 @@ decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
 template <typename T, int D>
 __global__ void __launch_bounds__(128) decode_stream_fixup_kernel(const DecodeArgs a, const StreamArgs sa) {
   constexpr int ROW = D + 2, DPL = D / 32;
-  constexpr int RP = D == 64 ? 8 : 4;  // head rows per pass
-  constexpr int CB = MVB_STREAM_FIXUP_CB;  // contributors per batch of O loads (divides 32)
+  constexpr int RP = D == 64 ? 4 : 2;          // head rows per pass
+  constexpr int CB = MVB_STREAM_FIXUP_CB;      // contributors per batch of O loads (divides 32)
+  constexpr int SPLIT = kFixupWarpsPerUnit;    // warps per cut unit, each on its share of the head rows
   const int lane = threadIdx.x & 31;
-  const int w_first = blockIdx.x * 4 + (threadIdx.x >> 5);
+  const int gw = blockIdx.x * 4 + (threadIdx.x >> 5);
+  const int w_first = gw / SPLIT, part_of = gw - w_first * SPLIT;
   const int Wtot = sa.num_warps;
   // The descriptor in one round trip: with a schedule its copy there, written
   // before the stream kernel ran, so it is read while that kernel finishes and
@@ -464,8 +475,11 @@ __global__ void __launch_bounds__(128) decode_stream_fixup_kernel(const DecodeAr
     return sa.part + ((int64_t)w * 2 + (w == w_first ? 1 : 0)) * 16 * ROW + r * ROW;
   };
   T* out = static_cast<T*>(a.out) + (int64_t)seq * a.o_s0;
+  // this warp's head rows [r_lo, r_hi) of the unit
+  const int rows_per = (nrows + SPLIT - 1) / SPLIT;
+  const int r_lo = min(nrows, part_of * rows_per), r_hi = min(nrows, r_lo + rows_per);
 
-  for (int rb = 0; rb < nrows; rb += RP) {
+  for (int rb = r_lo; rb < r_hi; rb += RP) {
     float x[CB][RP][DPL];  // O columns of contributors c0 .. c0 + CB - 1 (0 past the last)
     auto load_batch = [&](int c0) {
 #pragma unroll
@@ -475,7 +489,7 @@ __global__ void __launch_bounds__(128) decode_stream_fixup_kernel(const DecodeAr
         for (int r = 0; r < RP; ++r)
 #pragma unroll
           for (int i = 0; i < DPL; ++i)
-            x[c][r][i] = w >= 0 && rb + r < nrows ? __ldcg(row_ptr(w, rb + r) + 2 + lane + 32 * i) : 0.f;
+            x[c][r][i] = w >= 0 && rb + r < r_hi ? __ldcg(row_ptr(w, rb + r) + 2 + lane + 32 * i) : 0.f;
       }
     };
     float2 ml[RP];  // (m, l) of contributor c32 + lane
@@ -485,7 +499,7 @@ __global__ void __launch_bounds__(128) decode_stream_fixup_kernel(const DecodeAr
       ok = w >= 0;
 #pragma unroll
       for (int r = 0; r < RP; ++r)
-        ml[r] = ok && rb + r < nrows ? __ldcg(reinterpret_cast<const float2*>(row_ptr(w, rb + r)))
+        ml[r] = ok && rb + r < r_hi ? __ldcg(reinterpret_cast<const float2*>(row_ptr(w, rb + r)))
                                      : make_float2(-INFINITY, 0.f);
     };
     load_batch(0);  // in flight during the (m, l) pass
@@ -545,7 +559,7 @@ __global__ void __launch_bounds__(128) decode_stream_fixup_kernel(const DecodeAr
     }
 #pragma unroll
     for (int r = 0; r < RP; ++r)
-      if (rb + r < nrows) {
+      if (rb + r < r_hi) {
         T* po = out + (int64_t)(h0 + rb + r) * a.o_s1;
 #pragma unroll
         for (int i = 0; i < DPL; ++i) po[lane + 32 * i] = from_f32<T>(acc[r][i]);
@@ -981,7 +995,8 @@ cudaError_t launch_stream_t(const CUtensorMap& tmk, const CUtensorMap& tmv, cons
   if ((int64_t)sa.num_warps > kFixupCtaPiecesPerUnit * units)
     return launch_pdl(decode_stream_fixup_cta_kernel<T, D>, dim3(fixup_ctas), dim3(kFixupWarps * 32), 0, stream, a,
                       sa);
-  return launch_pdl(decode_stream_fixup_kernel<T, D>, dim3(fixup_ctas), dim3(128), 0, stream, a, sa);
+  return launch_pdl(decode_stream_fixup_kernel<T, D>, dim3((sa.num_warps * kFixupWarpsPerUnit + 3) / 4), dim3(128), 0,
+                    stream, a, sa);
 }
 
 cudaError_t launch_decode_stream(const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a,
