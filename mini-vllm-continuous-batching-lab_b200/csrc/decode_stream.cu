@@ -61,7 +61,7 @@ static_assert(sizeof(StreamRec) == 144, "record is 144 bytes");
 
 struct StreamArgs {
   int4* desc;     // [num_warps][2] the cut unit each warp begins, for the fixup:
-                  // {first tile, end tile, sequence, T_all}, {first head, heads, 0, 0};
+                  // {first tile, end tile, sequence, T_all}, {first head, heads, contributors, 0};
                   // first tile = -1 when the warp begins no cut unit
   float* part;    // [num_warps][2][16][D + 2] partial states (m, l, O[D] per row)
   int num_warps;  // gridDim.x * NW
@@ -81,6 +81,71 @@ __device__ __forceinline__ int stream_warp_of(int g, int T, int Wtot) {
 }
 __device__ __forceinline__ int stream_range_start(int w, int T, int Wtot) {
   return (int)((int64_t)w * T / Wtot);
+}
+
+// Cost-aware split.  A warp that enters a unit pays its flush, the lookup of
+// the next unit and that unit's partial last tile besides the tiles (about one
+// tile's time each: warps whose equal range touched two units ended 1.4 us
+// later, three units 3.1 us later).  With F(g) = g + kStreamUnitCost * u(g),
+// u(g) the index of the unit holding tile g (KHG units per sequence, counted
+// over every sequence), warp w takes [b(w), b(w + 1)) with
+//   b(w) = min{ g : F(g) * Wtot >= w * F(T) },   F(T) = T + kStreamUnitCost * KHG * Nd,
+// and tile g belongs to warp floor(F(g) * Wtot / F(T)).  The schedule kernel
+// cuts it when no sequence is left out (a left-out sequence would add cost
+// without tiles) and F(T) >= 3 * Wtot (then every range holds a tile, so the
+// contributors of a cut unit are consecutive warps); else, and without a
+// schedule, the equal split R(w).
+constexpr int kStreamUnitCost = 1;
+// floor(a * b / c) for 0 <= a * b < 2^53 and c > 0: a double quotient
+// corrected in integers (a 64-bit integer division is a long software routine)
+__device__ __forceinline__ int64_t mul_div_floor(int64_t a, int64_t b, int64_t c) {
+  const int64_t p = a * b;
+  int64_t q = (int64_t)((double)p / (double)c);
+  while (q * c > p) --q;
+  while ((q + 1) * c <= p) ++q;
+  return q;
+}
+struct StreamSplit {
+  int T, KHG, Wtot;
+  int64_t FT;  // F(T); 0: the equal split
+};
+__device__ __forceinline__ StreamSplit stream_split(int T, int KHG, int Nd, int Wtot, bool any_left_out) {
+  StreamSplit sp;
+  sp.T = T;
+  sp.KHG = KHG;
+  sp.Wtot = Wtot;
+  const int64_t FT = (int64_t)T + (int64_t)kStreamUnitCost * KHG * Nd;
+  sp.FT = !any_left_out && FT >= 3 * (int64_t)Wtot ? FT : 0;
+  return sp;
+}
+// First tile of warp w's range; pre: the tile prefix per sequence (Nd + 1).
+__device__ __forceinline__ int stream_split_start(const int* pre, int Nd, const StreamSplit& sp, int w) {
+  if (sp.FT == 0) return stream_range_start(w, sp.T, sp.Wtot);
+  const int64_t q = mul_div_floor(w, sp.FT, sp.Wtot);
+  const int64_t target = q * sp.Wtot == (int64_t)w * sp.FT ? q : q + 1;  // ceil(w * F(T) / Wtot)
+  const int64_t cu = (int64_t)kStreamUnitCost * sp.KHG;  // G(s) = pre[s] + cu * s: F at sequence s's first tile
+  if (pre[Nd] + cu * Nd <= target) return pre[Nd];
+  int lo = 0, hi = Nd;  // the last sequence s with G(s) <= target
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (pre[mid] + cu * mid <= target)
+      lo = mid;
+    else
+      hi = mid;
+  }
+  const int64_t off = target - (pre[lo] + cu * lo);
+  const int ut = (pre[lo + 1] - pre[lo]) / sp.KHG;
+  if (ut == 0) return pre[lo + 1];
+  // within the sequence: F(pre[s] + x) = G(s) + x + cost * floor(x / ut)
+  const int64_t k = off / (ut + kStreamUnitCost), t = off - k * (ut + kStreamUnitCost);
+  const int64_t x = t >= ut ? (k + 1) * ut : k * ut + t;
+  return (int)min((int64_t)pre[lo + 1], pre[lo] + x);
+}
+// Warp holding tile g, which is tile t of unit k of sequence s.
+__device__ __forceinline__ int stream_split_warp_of(const int* pre, const StreamSplit& sp, int g, int s, int k) {
+  if (sp.FT == 0) return stream_warp_of(g, sp.T, sp.Wtot);
+  const int64_t F = (int64_t)g + (int64_t)kStreamUnitCost * ((int64_t)sp.KHG * s + k);
+  return (int)min((int64_t)sp.Wtot - 1, mul_div_floor(F, sp.Wtot, sp.FT));
 }
 
 template <typename T, int D, int NW, int STAGES>
@@ -114,7 +179,9 @@ decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
 
   const bool from_schedule = sa.srec != nullptr;
   int rec_row = -1;
+  int4 rec_h = make_int4(0, 0, 0, 0);
   if (from_schedule) {
+    rec_h = __ldcg(&(sa.srec + blockIdx.x * NW + warp)->h);
     // The step's schedule: the pool rows of this warp's first 32 tiles in one
     // read, the tile prefix and servable kv_len for locating units
     // (L2-resident: every layer of the step reads them).
@@ -186,8 +253,12 @@ decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
   const int T_all = pre[Nd];
   const int Wtot = sa.num_warps;
   const int W = blockIdx.x * NW + warp;
-  auto range_start = [&](int w) { return stream_range_start(w, T_all, Wtot); };
-  const int r0 = range_start(W), r1 = range_start(W + 1);
+  // This warp's range: the record's with a schedule (the schedule kernel cut
+  // the cost-aware split), else the equal split (the cost-aware split's
+  // boundaries computed here made the launch 1.6 us slower at config 2).
+  const StreamSplit split = stream_split(T_all, KHG, Nd, Wtot, /*any_left_out=*/true);
+  const int r0 = from_schedule ? rec_h.x : stream_split_start(pre, Nd, split, W);
+  const int r1 = from_schedule ? rec_h.x + rec_h.y : stream_split_start(pre, Nd, split, W + 1);
   const int n = r1 - r0;
   if (n <= 0) {  // no CTA-wide barrier follows
     if (lane == 0) sa.desc[2 * W] = make_int4(-1, 0, 0, 0);
@@ -423,10 +494,16 @@ decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
   flush();
   // A unit that starts in this range and ends past it was begun here: this
   // warp is its first contributor, and the fixup finds the unit through it.
-  if (lane == 0) {
+  if (lane == 0 && !from_schedule) {  // (a schedule holds its own copy of the descriptors)
     const bool begins_cut = u_start >= r0 && u_end > r1;
     sa.desc[2 * W] = begins_cut ? make_int4(u_start, u_end, u_seq, T_all) : make_int4(-1, 0, 0, 0);
-    if (begins_cut) sa.desc[2 * W + 1] = make_int4(h0, nh, 0, 0);
+    if (begins_cut) {
+      // contributors: warps W .. the warp of the unit's last tile (every warp has
+      // tiles), else one warp per tile
+      const int nct = T_all >= Wtot ? stream_split_warp_of(pre, split, u_end - 1, u_seq, u_k) - W + 1
+                                    : u_end - u_start;
+      sa.desc[2 * W + 1] = make_int4(h0, nh, nct, 0);
+    }
   }
 }
 
@@ -466,9 +543,8 @@ __global__ void __launch_bounds__(128) decode_stream_fixup_kernel(const DecodeAr
   const int4 d1 = __ldcg(dsrc + 2 * w_first + 1);
   if (d0.x < 0) return;
   if (sa.sdesc != nullptr) grid_dependency_wait();  // the streaming kernel's partials are visible
-  const int us = d0.x, ue = d0.y, seq = d0.z, T_all = d0.w, h0 = d1.x, nrows = d1.y;
+  const int us = d0.x, ue = d0.y, seq = d0.z, T_all = d0.w, h0 = d1.x, nrows = d1.y, nct = d1.z;
   const bool dense = T_all >= Wtot;
-  const int nct = dense ? stream_warp_of(ue - 1, T_all, Wtot) - w_first + 1 : ue - us;
   auto contributor = [&](int c) { return dense ? w_first + c : stream_warp_of(us + c, T_all, Wtot); };
   // w_first keeps the unit in its "last" slot (1), later contributors in slot 0
   auto row_ptr = [&](int w, int r) -> const float* {
@@ -615,9 +691,8 @@ __global__ void __launch_bounds__(kFixupWarps * 32) decode_stream_fixup_cta_kern
     if (d0.x < 0) continue;  // CTA-uniform
     const int4 d1 = s_desc[q][1];
     const int w_first = blockIdx.x * FW + q;
-    const int us = d0.x, ue = d0.y, seq = d0.z, T_all = d0.w, h0 = d1.x, nrows = d1.y;
+    const int us = d0.x, ue = d0.y, seq = d0.z, T_all = d0.w, h0 = d1.x, nrows = d1.y, nct = d1.z;
     const bool dense = T_all >= Wtot;
-    const int nct = dense ? stream_warp_of(ue - 1, T_all, Wtot) - w_first + 1 : ue - us;
     auto contributor = [&](int c) { return dense ? w_first + c : stream_warp_of(us + c, T_all, Wtot); };
     // w_first keeps the unit in its "last" slot (1), later contributors in slot 0
     auto row_ptr = [&](int w, int r) -> const float* {
@@ -844,9 +919,11 @@ decode_stream_schedule_kernel(const int* __restrict__ kv_len, const int64_t* __r
   const int g0 = (int)((int64_t)blockIdx.x * T / C), g1 = (int)((int64_t)(blockIdx.x + 1) * T / C);
   for (int g = g0 + tid; g < g1; g += NT) srows[g] = row_of(g, my_bad);
   const int w0 = (int)((int64_t)blockIdx.x * num_warps / C), w1 = (int)((int64_t)(blockIdx.x + 1) * num_warps / C);
+  const StreamSplit split = stream_split(T, ups, num_seqs, num_warps, bits != 0);
   for (int e = tid; e < (w1 - w0) * 32; e += NT) {
     const int W = w0 + e / 32, j = e % 32;
-    const int r0 = (int)((int64_t)W * T / num_warps), r1 = (int)((int64_t)(W + 1) * T / num_warps);
+    const int r0 = stream_split_start(spre_s, num_seqs, split, W);
+    const int r1 = stream_split_start(spre_s, num_seqs, split, W + 1);
     if (j == 0) {
       srec[W].h = make_int4(r0, r1 - r0, 0, 0);
       // the fixup's descriptor of the unit this warp begins and its range
@@ -857,8 +934,9 @@ decode_stream_schedule_kernel(const int* __restrict__ kv_len, const int64_t* __r
         unit_of(r1 - 1, s, k, us, ut);
         if (us >= r0 && us + ut > r1) {
           const int kvh = k / head_groups, hg = k - kvh * head_groups;
+          const int nct = T >= num_warps ? stream_split_warp_of(spre_s, split, us + ut - 1, s, k) - W + 1 : ut;
           d0 = make_int4(us, us + ut, s, T);
-          d1 = make_int4(kvh * G + hg * 16, min(16, G - hg * 16), 0, 0);
+          d1 = make_int4(kvh * G + hg * 16, min(16, G - hg * 16), nct, 0);
         }
       }
       sdesc[2 * W] = d0;
