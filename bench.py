@@ -693,7 +693,9 @@ def config4_strong(args, rank, world, dev, peak):
     shard against its own pools, and the outputs are all-gathered in global
     order (NCCL all_gather_into_tensor + index_copy_).  Timed per rank as CUDA
     graphs of L back-to-back launches (decode alone, gather alone, decode then
-    gather), median of repeats, max over ranks."""
+    gather), median of repeats, max over ranks.  The decodes read the per-step
+    schedule of their kernel, built once (as once per model step) and timed on
+    its own (schedule_us)."""
     import torch
     import torch.distributed as dist
 
@@ -715,10 +717,17 @@ def config4_strong(args, rank, world, dev, peak):
     gather = sharding.OutputGather(owned_all, spec.num_heads, spec.head_dim, torch.bfloat16, dev) if world > 1 else None
     plan = M.decode_plan(spec.num_seqs, spec.num_heads, spec.num_kv_heads, spec.head_dim, 16, spec.num_blocks,
                          spec.max_blocks, torch.bfloat16, "auto")
+    sched = M.build_decode_schedule(kvl, bt, spec.num_heads, spec.num_kv_heads, spec.head_dim, 16, spec.num_blocks,
+                                    torch.bfloat16, strict=False)
 
     def decodes():
         for layer in range(L):
-            M.paged_decode_attention(q, kcs[layer], vcs[layer], bt, kvl, 16, out=out, strict=False)
+            M.paged_decode_attention(q, kcs[layer], vcs[layer], bt, kvl, 16, out=out, strict=False, schedule=sched)
+
+    def schedules():
+        for _ in range(L):
+            M.build_decode_schedule(kvl, bt, spec.num_heads, spec.num_kv_heads, spec.head_dim, 16, spec.num_blocks,
+                                    torch.bfloat16, schedule=sched, strict=False)
 
     def gathers():
         for _ in range(L):
@@ -727,7 +736,7 @@ def config4_strong(args, rank, world, dev, peak):
 
     def both():
         for layer in range(L):
-            M.paged_decode_attention(q, kcs[layer], vcs[layer], bt, kvl, 16, out=out, strict=False)
+            M.paged_decode_attention(q, kcs[layer], vcs[layer], bt, kvl, 16, out=out, strict=False, schedule=sched)
             if gather is not None:
                 gather(out)
 
@@ -769,6 +778,10 @@ def config4_strong(args, rank, world, dev, peak):
 
     dec_s = time_graph(decodes)
     own_dec_s = dec_s
+    do_sched = torch.tensor([1 if sched.variant is not None else 0], device=dev)
+    if world > 1:  # every rank takes the same collective steps
+        dist.all_reduce(do_sched, op=dist.ReduceOp.MIN)
+    sched_s = time_graph(schedules) if int(do_sched.item()) else 0.0
     gat_s = time_graph(gathers) if world > 1 else 0.0
     both_s = time_graph(both) if world > 1 else dec_s
     # per-rank figures
@@ -783,6 +796,7 @@ def config4_strong(args, rank, world, dev, peak):
                     "snake-sharded by sequence",
         "scaling": "strong", "global_batch": int(ctx_all.size), "kernel": plan["variant"],
         "decode_us_max_rank": round(dec_s * 1e6, 2), "gather_us": round(gat_s * 1e6, 2),
+        "schedule_us": round(sched_s * 1e6, 2),
         "decode_then_gather_us": round(both_s * 1e6, 2),
         "decode_tok_s_no_gather": round(ctx_all.size / dec_s, 1),
         "decode_tok_s_with_gather": round(ctx_all.size / both_s, 1),
@@ -793,7 +807,7 @@ def config4_strong(args, rank, world, dev, peak):
         "seqs_per_rank": [int(v[1]) for v in allv],
         "timing": f"CUDA graphs of {L} launches, events, median of 20 replays, max over ranks",
     }
-    del t, q, bt, kvl, kcs, vcs, out
+    del t, q, bt, kvl, kcs, vcs, out, sched
     torch.cuda.empty_cache()
     return res
 
