@@ -419,6 +419,12 @@ def ours(args, rank, world, local_rank):
     # repeats: >= 20, and enough for ~1.5 s of load so the clock sampler sees it
     est = K * step_bytes_rank / 5e12
     R = int(min(5000, max(20, math.ceil(1.5 / max(est, 1e-6)))))
+    if world > 1:
+        # the same number of replays on every rank: each replay runs the graph's
+        # NCCL all-gathers, so a rank that replays more waits for a peer forever
+        rt = torch.tensor([R], device=dev, dtype=torch.int64)
+        dist.all_reduce(rt, op=dist.ReduceOp.MAX)
+        R = int(rt.item())
     timed_region()
     torch.cuda.synchronize()
     if world > 1:
