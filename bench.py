@@ -547,10 +547,19 @@ def ours(args, rank, world, local_rank):
     layer_host, layer_bytes, layer_slots = staged([("q", q), ("nk", nk), ("nv", nv)])
     meta_host, meta_bytes, meta_slots = staged([("slots", slots), ("bt", bt), ("kvl", kvl32)])
     outs_host = [torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(2)]
+    outs_dev = [torch.empty_like(q) for _ in range(2)]  # the decode writes its output here (out=)
     out_copied = [torch.cuda.Event(), torch.cuda.Event()]
     d2h = outs_host[0].numel() * outs_host[0].element_size()
     compute = torch.cuda.current_stream(dev)
-    side = torch.cuda.Stream(dev)
+    side = torch.cuda.Stream(dev)      # host -> device copies
+    side_d2h = torch.cuda.Stream(dev)  # device -> host copies (the link is full duplex)
+    # the loop's copies use fixed buffers: each is checked once (staging.CopyPlan)
+    layer_plans = [M.staging.CopyPlan(ls["buf"], layer_host, side, wait=ls["done"], record=ls["ready"])
+                   for ls in layer_slots]
+    meta_plans = [M.staging.CopyPlan(ms["buf"], meta_host, side, wait=ms["done"], record=ms["ready"])
+                  for ms in meta_slots]
+    out_plans = [M.staging.CopyPlan(outs_host[p], outs_dev[p], side_d2h, wait=layer_slots[p]["done"],
+                                    record=out_copied[p]) for p in range(2)]
     pending = []    # (step index, output) whose D2H is not issued yet
     releasing = []  # (event, output) freed once compute waited for the D2H
     meta_obj = [None]
@@ -560,7 +569,7 @@ def ours(args, rank, world, local_rank):
         ls, ms = layer_slots[i & 1], meta_slots[m & 1]
         waits = []
         if layer == 0:  # this model step's metadata, once
-            M.staging.stream_copy(ms["buf"], meta_host, side, wait=ms["done"], record=ms["ready"])
+            meta_plans[m & 1].run()
             v = ms["views"]
             group = M.AttentionGroup(seq_indices=list(range(spec.num_seqs)), attention_type="decode_gpu",
                                      cached_len_before=None, query_len=None, kv_len_after=v["kvl"])
@@ -568,12 +577,11 @@ def ours(args, rank, world, local_rank):
                                               block_size=spec.block_size, num_kv_heads=spec.num_kv_heads,
                                               head_dim=spec.head_dim)
             waits.append(ms["ready"])
-        M.staging.stream_copy(ls["buf"], layer_host, side, wait=ls["done"], record=ls["ready"])
+        layer_plans[i & 1].run()
         waits.append(ls["ready"])
         if pending:  # D2H of the previous step's output
             pi, po = pending.pop()
-            M.staging.stream_copy(outs_host[pi & 1], po, side, wait=layer_slots[pi & 1]["done"],
-                                  record=out_copied[pi & 1])
+            out_plans[pi & 1].run()
             releasing.append((out_copied[pi & 1], po))
         if len(releasing) > 1:
             # an output is freed only after the compute stream has waited for its
@@ -584,7 +592,7 @@ def ours(args, rank, world, local_rank):
         M.staging.wait_events(compute, *waits)
         v = ls["views"]
         backend.write_kv_cache(layer, v["nk"], v["nv"], ms["views"]["slots"])
-        o = backend.decode_attention(layer, v["q"], meta_obj[0], pool)
+        o = backend.decode_attention(layer, v["q"], meta_obj[0], pool, out=outs_dev[i & 1])
         M.staging.record(ls["done"], compute)
         if layer == L - 1:
             M.staging.record(ms["done"], compute)
@@ -593,10 +601,10 @@ def ours(args, rank, world, local_rank):
     def e2e_flush():
         while pending:
             pi, po = pending.pop()
-            M.staging.stream_copy(outs_host[pi & 1], po, side, wait=layer_slots[pi & 1]["done"],
-                                  record=out_copied[pi & 1])
+            out_plans[pi & 1].run()
             releasing.append((out_copied[pi & 1], po))
         compute.wait_stream(side)
+        compute.wait_stream(side_d2h)
         releasing.clear()
 
     e2e_n = max(L, (args.e2e_steps // L) * L)
@@ -609,6 +617,7 @@ def ours(args, rank, world, local_rank):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(compute)
     side.wait_stream(compute)
+    side_d2h.wait_stream(compute)
     h0 = time.perf_counter()
     for i in range(e2e_n):
         e2e_step(i)
@@ -679,8 +688,10 @@ def ours(args, rank, world, local_rank):
                     "h2d_detail": f"{layer_bytes} B of query / new K / new V per layer-step + {meta_bytes} B of "
                                   f"metadata per model step of {L} layer-steps",
                     "ms_per_step": round(e2e_sec * 1e3, 4),
-                    "copies": "H2D and D2H on a side stream, double-buffered, overlapping compute; "
-                              "staged with mini_vllm_b200.staging (one CUDA call per copy / wait / record)",
+                    "copies": "H2D and D2H on two side streams, double-buffered, overlapping compute and each other; "
+                              "staged with mini_vllm_b200.staging (fixed buffers as staging.CopyPlan, one "
+                              "binding call per copy / wait / record); the decode writes into one of two "
+                              "output buffers (out=)",
                     "host_us_per_step": round(e2e_host_us, 1),
                     "decode_tok_s": round(seqs_all / e2e_sec, 1)},
             "gpu_launches": K * per_layer + (-(-K // L) if scheduled else 0),

@@ -1054,6 +1054,7 @@ class AttentionBackendB200(AttentionBackend):
         # tensors or the shapes change; every other layer reuses it.
         self._schedule: Optional[DecodeSchedule] = None
         self._schedule_key: Optional[tuple] = None
+        self._schedule_src: tuple = (None, None, None, None, None, None)
 
     def begin_step(self) -> None:
         """Forget the current step's decode schedule, so the next decode builds
@@ -1118,6 +1119,14 @@ class AttentionBackendB200(AttentionBackend):
         kernel, built when needed (None when the decode runs another
         kernel)."""
         self._schedule_built_now = False
+        if (layer_idx != 0 and self._schedule_key is not None and attn_metadata is self._schedule_src[0]
+                and bt is self._schedule_src[1] and kvl is self._schedule_src[2]):
+            # the same metadata object and tensors as the layer that built it
+            # (the full key below also covers shapes and pools; a caller that
+            # rewrites these tensors in place calls begin_step)
+            if kc.shape == self._schedule_src[3] and query.shape == self._schedule_src[4] and \
+                    query.dtype == self._schedule_src[5]:
+                return self._schedule
         if self.decode_variant not in ("auto", "sched", "stream") or not (query.is_cuda and kvl.is_cuda and bt.is_cuda):
             return None
         if query.dtype not in (torch.bfloat16, torch.float16) or block_size % 16 or kc.dtype != query.dtype:
@@ -1136,6 +1145,7 @@ class AttentionBackendB200(AttentionBackend):
                                                kc.shape[0], query.dtype, schedule=self._schedule,
                                                after_write=after, strict=False, variant=plan["variant"])
         self._schedule_key = key
+        self._schedule_src = (attn_metadata, bt, kvl, kc.shape, query.shape, query.dtype)
         self._schedule_built_now = True
         return self._schedule
 

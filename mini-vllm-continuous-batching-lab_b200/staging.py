@@ -82,3 +82,44 @@ def record(event: torch.cuda.Event, stream: torch.cuda.Stream) -> None:
     st = _binding().event_record(handle, stream.cuda_stream)
     if st != 0:
         raise RuntimeError(f"record failed: CUDA error {st}")
+
+
+class CopyPlan:
+    """A fixed ``stream_copy`` — the same tensors, stream and events every
+    step, as a serving loop's preallocated staging buffers are — checked once;
+    ``run()`` then issues it (wait, copy, record on the stream) in one binding
+    call with the handles resolved, skipping the per-call checks.  The plan
+    keeps its tensors and events alive."""
+
+    __slots__ = ("_dst", "_src", "_stream", "_wait", "_record", "_args", "_wait_h", "_rec_h")
+
+    def __init__(self, dst: torch.Tensor, src: torch.Tensor, stream: torch.cuda.Stream, *,
+                 wait: Optional[torch.cuda.Event] = None, record: Optional[torch.cuda.Event] = None) -> None:
+        if dst.is_cuda == src.is_cuda:
+            raise ValueError("CopyPlan copies between host and device memory: exactly one tensor must be on the GPU")
+        if not (dst.is_contiguous() and src.is_contiguous()):
+            raise ValueError("CopyPlan needs contiguous tensors")
+        dev = dst.device if dst.is_cuda else src.device
+        if stream.device != dev:
+            raise ValueError(f"CopyPlan: the device tensor is on {dev} but the stream belongs to {stream.device}")
+        nbytes = dst.numel() * dst.element_size()
+        if nbytes != src.numel() * src.element_size():
+            raise ValueError(f"CopyPlan size mismatch: {nbytes} vs {src.numel() * src.element_size()} bytes")
+        _binding()
+        self._dst, self._src, self._stream, self._wait, self._record = dst, src, stream, wait, record
+        self._args = (dst.data_ptr(), src.data_ptr(), nbytes, 0 if dst.is_cuda else 1, stream.cuda_stream)
+        self._wait_h = 0
+        self._rec_h = 0
+
+    def run(self) -> None:
+        """Wait for ``wait`` (once it has been recorded), copy, record ``record``."""
+        if self._wait_h == 0 and self._wait is not None:
+            self._wait_h = _event_handle(self._wait)  # 0 until torch creates it on a first record
+        if self._rec_h == 0 and self._record is not None:
+            self._rec_h = _event_handle(self._record)
+            if self._rec_h == 0:  # torch creates an event on its first record
+                self._record.record(self._stream)
+                self._rec_h = int(self._record.cuda_event)
+        st = _native.fast().stream_copy(*self._args, self._wait_h, self._rec_h)
+        if st != 0:
+            raise RuntimeError(f"CopyPlan.run failed: CUDA error {st}")

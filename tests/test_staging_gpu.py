@@ -65,3 +65,29 @@ def test_staging_rejects_a_stream_of_another_device():
     other = types.SimpleNamespace(device=torch.device("cuda", DEV.index + 1), cuda_stream=0)
     with pytest.raises(ValueError, match="stream belongs to"):
         M.staging.stream_copy(torch.zeros(4, device=DEV), torch.zeros(4).pin_memory(), other)
+
+
+def test_copy_plan_repeats_the_checked_copy():
+    """A CopyPlan, checked once, copies its fixed tensors on every run: host
+    to device, a kernel in between, device to host, ordered by its events."""
+    dev = torch.device("cuda", 0)
+    side = torch.cuda.Stream(dev)
+    host_in = torch.empty(1 << 16, dtype=torch.float32).pin_memory()
+    host_out = torch.empty(1 << 16, dtype=torch.float32).pin_memory()
+    dbuf = torch.empty(1 << 16, dtype=torch.float32, device=dev)
+    dout = torch.empty_like(dbuf)
+    ready, done, copied = torch.cuda.Event(), torch.cuda.Event(), torch.cuda.Event()
+    h2d = M.staging.CopyPlan(dbuf, host_in, side, wait=done, record=ready)
+    d2h = M.staging.CopyPlan(host_out, dout, side, wait=done, record=copied)
+    compute = torch.cuda.current_stream(dev)
+    for step in range(5):
+        host_in.fill_(float(step))
+        h2d.run()
+        M.staging.wait_events(compute, ready)
+        torch.mul(dbuf, 2.0, out=dout)
+        M.staging.record(done, compute)
+        d2h.run()
+        copied.synchronize()
+        assert (host_out == 2.0 * step).all()
+    with pytest.raises(ValueError, match="exactly one"):
+        M.staging.CopyPlan(dbuf, dout, side)
