@@ -78,8 +78,12 @@ def parse_args():
     p.add_argument("--no-config4", action="store_true", help="skip the config-4 strong-scaling sub-object")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--requests", type=int, default=256, help="--op engine: requests per replica")
+    p.add_argument("--shard-of", type=int, default=1,
+                   help="--op profile / trace: run rank 0's shard of an N-GPU run of --config (config 4: "
+                        "its snake-assigned quarter at 4, a capture-sized case)")
+    p.add_argument("--trace-out", default="", help="--op trace: also save the raw stamps (.npz) here")
     p.add_argument("--op", choices=["step", "gather", "rope_write", "metadata", "sweep", "engine", "profile",
-                                    "variants"],
+                                    "variants", "trace"],
                    default="step",
                    help="step: the decode step (the headline); sweep: decode time per launch of every "
                         "kernel over batch x context (the plan's crossover table); variants: decode time per "
@@ -87,6 +91,8 @@ def parse_args():
                         "serving in the reference's own engine (config 5, bounded: --requests per replica; "
                         "--impl reference runs the reference's GPU backend); profile: a few KV writes and "
                         "decodes of --variant on --config over --layers pools, untimed (the case ncu captures); "
+                        "trace: the per-warp timeline of the stream decode (the trace build of the library, "
+                        "min(--layers, 8) KV writes + scheduled decodes in one CUDA graph); "
                         "gather: the prefill prefix gather "
                         "(mvb_paged_gather) of every config-2 context; rope_write: the fused RoPE + "
                         "KV write (mvb_rope_kv_cache_write) of an 8192-token prefill chunk; metadata: "
@@ -1228,7 +1234,7 @@ def profile_op(args):
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    spec, _ = rank_spec(args.config, 0, 1, args.seed)
+    spec, _ = rank_spec(args.config, 0, args.shard_of, args.seed)
     L = args.layers
     t = W.torch_tensors(spec, torch.bfloat16, dev, num_layers=L)
     q, nk, nv = t["query"], t["new_key"], t["new_value"]
@@ -1250,8 +1256,143 @@ def profile_op(args):
                                      schedule=sched)
     torch.cuda.synchronize()
     M.check_device_errors(dev)
-    print(json.dumps({"op": "profile", "config": args.config, "plan": plan, "layers": L,
+    print(json.dumps({"op": "profile", "config": args.config, "shard_of": args.shard_of, "num_seqs": spec.num_seqs,
+                      "plan": plan, "layers": L,
                       "decode_bytes": spec.decode_bytes(2), "write_bytes": spec.write_bytes(2)}), flush=True)
+
+
+def trace_op(args):
+    """The stream decode's per-warp timeline.  Loads the trace build of the
+    library (``lib/libmvb200_trace.so``: the stream and warp-fixup kernels with
+    %globaltimer stamps, built by ``build.build_trace()`` when absent) and runs
+    the headline step's layer-steps (KV write, then the decode with the step's
+    schedule and the set-up overlapped with the write) for min(--layers, 8)
+    pools in one CUDA graph.  After warm-up replays it times one replay with
+    CUDA events (the trace build's own time per layer-step), clears the stamps,
+    replays once more and prints, per launch, the times in microseconds from
+    the launch's first stream warp entry: warps entering, first loads issued,
+    first tile landed, loop end, stream end, the median time between a warp's
+    consecutive tiles (and the rate all warps' tiles make at it), and the
+    fixup warps' wait and end.  Launch-level figures only: the stamps cost a
+    few instructions per tile."""
+    import ctypes
+
+    import torch
+
+    from mini_vllm_b200 import _native
+    from mini_vllm_b200 import build as B
+
+    path = B.TRACE_LIB_PATH if os.path.exists(B.TRACE_LIB_PATH) else B.build_trace()
+    _native.LIB_PATH = path  # before the first call loads the library
+    import mini_vllm_b200 as M
+    from mini_vllm_b200 import workloads as W
+
+    lib = _native.lib()
+    lib.mvb_trace_clear.restype = ctypes.c_int
+    lib.mvb_trace_read.restype = ctypes.c_int
+    lib.mvb_trace_read.argtypes = [ctypes.c_void_p] * 3
+    NL, NW, NF, NT = 8, 4096, 16384, 32  # the trace arrays' shapes (csrc/decode_stream.cu)
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    spec, _ = rank_spec(args.config, 0, args.shard_of, args.seed)
+    L = max(1, min(args.layers, NL))
+    t = W.torch_tensors(spec, torch.bfloat16, dev, num_layers=L)
+    q, nk, nv = t["query"], t["new_key"], t["new_value"]
+    bt, kvl, slots = t["block_tables"], t["kv_len"], t["slot_mapping"]
+    out = torch.empty_like(q)
+    variant = "stream"
+    plan = M.decode_plan(spec.num_seqs, spec.num_heads, spec.num_kv_heads, spec.head_dim, spec.block_size,
+                         spec.num_blocks, spec.max_blocks, torch.bfloat16, variant)
+    sched = M.build_decode_schedule(kvl, bt, spec.num_heads, spec.num_kv_heads, spec.head_dim, spec.block_size,
+                                    spec.num_blocks, torch.bfloat16, variant=variant)
+
+    def layer_steps():
+        for layer in range(L):
+            M.paged_cache_write(nk, nv, t["key_caches"][layer], t["value_caches"][layer], slots, spec.block_size,
+                                strict=False, check_duplicates=False)
+            M.paged_decode_attention(q, t["key_caches"][layer], t["value_caches"][layer], bt, kvl,
+                                     spec.block_size, out=out, variant=variant, strict=False, after_write=True,
+                                     schedule=sched)
+
+    layer_steps()
+    torch.cuda.synchronize()
+    M.check_device_errors(dev)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        layer_steps()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        layer_steps()
+    for _ in range(3):
+        graph.replay()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    graph_us = e0.elapsed_time(e1) * 1e3 / L
+    if lib.mvb_trace_clear() != 0:
+        raise RuntimeError("mvb_trace_clear failed")
+    torch.cuda.synchronize()
+    graph.replay()
+    torch.cuda.synchronize()
+    M.check_device_errors(dev)
+    ws = np.zeros((NL, NW, 5), np.uint64)
+    tt = np.zeros((NL, NW, NT), np.uint64)
+    fx = np.zeros((NL, NF, 3), np.uint64)
+    if lib.mvb_trace_read(ws.ctypes.data, tt.ctypes.data, fx.ctypes.data) != 0:
+        raise RuntimeError("mvb_trace_read failed")
+    del graph
+    if args.trace_out:
+        np.savez_compressed(args.trace_out, warps=ws, tiles=tt, fixups=fx)
+
+    tile_bytes = 2 * 16 * spec.head_dim * 2  # K and V of one 16-token tile of one KV head, bf16
+    print(json.dumps({"op": "trace", "config": args.config, "shard_of": args.shard_of, "num_seqs": spec.num_seqs,
+                      "layers": L, "plan": plan,
+                      "trace_build_us_per_layer_step": round(graph_us, 2),
+                      "decode_bytes": spec.decode_bytes(2), "tile_bytes": tile_bytes}), flush=True)
+
+    def pct(x, p):
+        return round(float(np.percentile(x, p)) / 1e3, 2) if len(x) else None
+
+    prev_end = None
+    for i in range(L):
+        w = ws[i].astype(np.int64)
+        entered = w[:, 0] > 0
+        if not entered.any():
+            continue
+        t0 = int(w[entered, 0].min())
+        worked = entered & (w[:, 4] > 0) & (w[:, 2] > 0)
+        rel = w[worked] - t0
+        ti = tt[i][worked].astype(np.int64)
+        both = (ti[:, 1:] > 0) & (ti[:, :-1] > 0)
+        gaps = (ti[:, 1:] - ti[:, :-1])[both]
+        f = fx[i].astype(np.int64)
+        fw = f[(f[:, 0] > 0) & (f[:, 2] > 0)] - t0
+        stream_end = int(rel[:, 4].max()) if len(rel) else 0
+        fix_end = int(fw[:, 2].max()) if len(fw) else stream_end
+        med_gap = float(np.median(gaps)) if len(gaps) else 0.0
+        row = {
+            "launch": i, "stream_warps": int(entered.sum()), "warps_with_tiles": int(worked.sum()),
+            "entry_p50_us": pct(w[entered, 0] - t0, 50), "entry_max_us": pct(w[entered, 0] - t0, 100),
+            "first_issue_p50_us": pct(rel[:, 1], 50),
+            "first_tile_us": [pct(rel[:, 2], 10), pct(rel[:, 2], 50), pct(rel[:, 2], 90)],
+            "loop_end_us": [pct(rel[:, 3], 10), pct(rel[:, 3], 50), pct(rel[:, 3], 90)],
+            "stream_end_max_us": round(stream_end / 1e3, 2),
+            "tile_interval_p50_us": round(med_gap / 1e3, 3),
+            "steady_GBps": round(int(worked.sum()) * tile_bytes / med_gap, 1) if med_gap > 0 else None,
+            "fixup_warps": int(len(fw)),
+            "fixup_wait_us": [pct(fw[:, 1], 0), pct(fw[:, 1], 50)] if len(fw) else None,
+            "fixup_end_max_us": round(fix_end / 1e3, 2),
+            "fixup_after_stream_us": round((fix_end - stream_end) / 1e3, 2),
+            "start_after_previous_us": round((t0 - prev_end) / 1e3, 2) if prev_end is not None else None,
+        }
+        prev_end = t0 + max(fix_end, stream_end)
+        print(json.dumps(row), flush=True)
 
 
 def engine_op(args):
@@ -1445,6 +1586,9 @@ def main():
         return
     if args.op == "engine":
         engine_op(args)
+        return
+    if args.op == "trace":
+        trace_op(args)
         return
     if args.op == "profile":
         profile_op(args)

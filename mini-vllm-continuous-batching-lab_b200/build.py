@@ -86,6 +86,33 @@ def build_native(force: bool = False, verbose: bool = False) -> str:
     return LIB_PATH
 
 
+TRACE_LIB_PATH = os.path.join(LIB_DIR, "libmvb200_trace.so")
+
+
+def build_trace(force: bool = False) -> str:
+    """Link ``lib/libmvb200_trace.so``: the library with the stream decode
+    compiled with ``-DMVB_STREAM_TRACE`` (per-warp %globaltimer stamps and the
+    ``mvb_trace_clear`` / ``mvb_trace_read`` calls; ``bench.py --op trace``
+    loads it).  The other objects are the product's."""
+    build_native(force=force)
+    src = os.path.join(CSRC, "decode_stream.cu")
+    obj = os.path.join(OBJ_DIR, "decode_stream_trace.o")
+    if force or not os.path.exists(obj) or os.path.getmtime(obj) < max(os.path.getmtime(src), _deps_mtime()):
+        cmd = [nvcc_path(), *ARCH_FLAGS, *NVCC_FLAGS, "-DMVB_STREAM_TRACE", "-I", INCLUDE, "-c", src, "-o", obj]
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if res.returncode != 0:
+            raise RuntimeError(f"nvcc failed for the trace build of decode_stream.cu:\n{res.stdout}\n{res.stderr}")
+    objs = [obj if s_ == "decode_stream.cu" else os.path.join(OBJ_DIR, os.path.splitext(s_)[0] + ".o")
+            for s_ in SOURCES]
+    if force or not os.path.exists(TRACE_LIB_PATH) or os.path.getmtime(TRACE_LIB_PATH) < max(
+            os.path.getmtime(o) for o in objs):
+        cmd = [nvcc_path(), *ARCH_FLAGS, "-shared", "-Xlinker", "-soname=libmvb200_trace.so", "-o", TRACE_LIB_PATH,
+               *objs, "-lrt", "-ldl", "-lpthread"]
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if res.returncode != 0:
+            raise RuntimeError(f"link of libmvb200_trace.so failed:\n{res.stdout}\n{res.stderr}")
+    return TRACE_LIB_PATH
+
 TORCH_BINDING_SRC = os.path.join(CSRC, "torch_binding.cpp")
 TORCH_BINDING_PATH = os.path.join(LIB_DIR, "_mvb_torch.so")
 

@@ -32,18 +32,51 @@
 
 namespace mvb {
 
+// Per-warp timeline, compiled in only with -DMVB_STREAM_TRACE: the trace build
+// (lib/libmvb200_trace.so, made by build.build_trace(); bench.py --op trace
+// loads it).  The product library holds none of it.  Each launch takes the
+// next of kTraceLaunches slots (a per-warp arrival counter, so up to
+// kTraceLaunches back-to-back launches after mvb_trace_clear() keep their own
+// stamps), and lane 0 of a warp records %globaltimer (ns) at:
+//   stream warp W: entry, first loads issued, first tile landed, loop end,
+//                  end, and the landing of each of its first kTraceTiles tiles;
+//   fixup warp gw (one with a cut unit): entry, wait returned, end.
+#ifdef MVB_STREAM_TRACE
+constexpr int kTraceLaunches = 8, kTraceWarps = 4096, kTraceFixWarps = 16384, kTraceTiles = 32;
+__device__ int g_trace_wcnt[kTraceWarps];
+__device__ int g_trace_fcnt[kTraceFixWarps];
+__device__ unsigned long long g_trace_w[kTraceLaunches][kTraceWarps][5];
+__device__ unsigned long long g_trace_t[kTraceLaunches][kTraceWarps][kTraceTiles];
+__device__ unsigned long long g_trace_f[kTraceLaunches][kTraceFixWarps][3];
+__device__ __forceinline__ unsigned long long trace_now() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+#define MVB_TRACE(...) __VA_ARGS__
+#else
+#define MVB_TRACE(...)
+#endif
+
 constexpr int kStreamRowBatch = 128;  // tiles whose pool rows a warp resolves at once
 #ifndef MVB_STREAM_FIXUP_CB
 #define MVB_STREAM_FIXUP_CB 4
 #endif
 #ifndef MVB_STREAM_FIXUP_SPLIT
-#define MVB_STREAM_FIXUP_SPLIT 2
+#define MVB_STREAM_FIXUP_SPLIT 4
+#endif
+#ifndef MVB_STREAM_FIXUP_RP64
+#define MVB_STREAM_FIXUP_RP64 2   // the warp fixup's head rows per pass, head_dim 64
+#endif
+#ifndef MVB_STREAM_FIXUP_RP128
+#define MVB_STREAM_FIXUP_RP128 2  // ... head_dim 128
 #endif
 // The warp fixup's warps per cut unit, each merging its share of the unit's
-// head rows: half the rows per warp halve the merge's serial work and its
-// registers per contributor (config-2 decode with a schedule 34.1 -> 32.9 us,
-// without one 35.6 -> 34.6 us; four warps per unit, or 8 contributors per
-// batch, were slower).
+// head rows: fewer rows per warp shorten the merge's serial work and cut its
+// registers per contributor.  Config-2 decode with a schedule: 1 -> 2 warps
+// per unit 34.1 -> 32.9 us, later 2 -> 4 warps (two head rows each) 31.5 ->
+// 31.1 us; 8 warps, 8 contributors per batch, or two batches in flight
+// (the next batch loaded before the current one is summed) were slower.
 constexpr int kFixupWarpsPerUnit = MVB_STREAM_FIXUP_SPLIT;
 
 // Per-step schedule of the stream kernel (MVB_DECODE_SCHEDULE_READY): what
@@ -177,6 +210,7 @@ decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
   // stream: wait for it first.  With it (the previous kernel is the KV write,
   // which writes only the cache) the set-up below reads query, block table and
   // kv_len at once, and only the first cache load waits.
+  MVB_TRACE(const unsigned long long tr_entry = trace_now();)
   if (!a.early_inputs) grid_dependency_wait();
   grid_launch_dependents();    // the fixup kernel may be scheduled as CTAs retire
 
@@ -263,6 +297,11 @@ decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
   const int r0 = from_schedule ? rec_h.x : stream_split_start(pre, Nd, split, W);
   const int r1 = from_schedule ? rec_h.x + rec_h.y : stream_split_start(pre, Nd, split, W + 1);
   const int n = r1 - r0;
+  MVB_TRACE(int tr_slot = 0; const bool tr_on = lane == 0 && W < kTraceWarps;
+            if (tr_on) {
+              tr_slot = atomicAdd(&g_trace_wcnt[W], 1) % kTraceLaunches;
+              g_trace_w[tr_slot][W][0] = tr_entry;
+            })
   if (n <= 0) {  // no CTA-wide barrier follows
     if (lane == 0) sa.desc[2 * W] = make_int4(-1, 0, 0, 0);
     return;
@@ -438,6 +477,7 @@ decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
   // the warp reaches its loop, so each warp's first tile is queued behind
   // fewer loads (config 2: -0.3 us).
   if (lane == 0 && n > 0) issue(0);
+  MVB_TRACE(if (tr_on) g_trace_w[tr_slot][W][1] = trace_now();)
   fill_rows(0, 32);  // the rest of the first batch, while the first loads are in flight
   bool failed = false;
   int j = 0;
@@ -470,6 +510,11 @@ decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
       for (int jj = 1; jj < (n < STAGES ? n : STAGES); ++jj) issue(jj);
     const int st = j % STAGES;
     const bool got = mbar_wait_bounded(smem_u32(mybars + st), (uint32_t)((j / STAGES) & 1), a.wait_limit);
+    MVB_TRACE(if (tr_on) {
+      const unsigned long long t = trace_now();
+      if (j == 0) g_trace_w[tr_slot][W][2] = t;
+      if (j < kTraceTiles) g_trace_t[tr_slot][W][j] = t;
+    })
     if (__any_sync(0xffffffffu, !got)) {
       failed = true;
       break;
@@ -496,6 +541,7 @@ decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
     if (lane == 0) sa.desc[2 * W] = make_int4(-1, 0, 0, 0);
     return;  // the unit's output stays unwritten; the error flag reports it
   }
+  MVB_TRACE(if (tr_on) g_trace_w[tr_slot][W][3] = trace_now();)
   flush();
   // A unit that starts in this range and ends past it was begun here: this
   // warp is its first contributor, and the fixup finds the unit through it.
@@ -510,15 +556,16 @@ decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
       sa.desc[2 * W + 1] = make_int4(h0, nh, nct, 0);
     }
   }
+  MVB_TRACE(if (tr_on) g_trace_w[tr_slot][W][4] = trace_now();)
 }
 
 // ---------------------------------------------------------------------------
-// fixup, one warp per unit: merge the partial states of every unit cut by a
-// warp-range boundary (units cut into few pieces)
+// fixup, a few warps per unit: merge the partial states of every unit cut by
+// a warp-range boundary (units cut into few pieces)
 // ---------------------------------------------------------------------------
-// One warp per warp w of the stream grid: when w begins a cut unit (its
-// descriptor says which), the warp merges every head row of that unit, RP rows
-// per pass.  Lane c holds contributor c's (m, l) of each row; M and L come
+// kFixupWarpsPerUnit warps per warp w of the stream grid: when w begins a cut
+// unit (its descriptor says which), each of them merges its share of the
+// unit's head rows, RP rows per pass.  Lane c holds contributor c's (m, l) of each row; M and L come
 // from warp reductions, and each lane accumulates its D/32 columns over the
 // contributors with coefficients broadcast from the owning lane:
 //   out[r][d] = sum_c O_c[r][d] 2^(m_c - M_r) / L_r.
@@ -531,9 +578,10 @@ decode_stream_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
 template <typename T, int D>
 __global__ void __launch_bounds__(128) decode_stream_fixup_kernel(const DecodeArgs a, const StreamArgs sa) {
   constexpr int ROW = D + 2, DPL = D / 32;
-  constexpr int RP = D == 64 ? 4 : 2;          // head rows per pass
+  constexpr int RP = D == 64 ? MVB_STREAM_FIXUP_RP64 : MVB_STREAM_FIXUP_RP128;  // head rows per pass
   constexpr int CB = MVB_STREAM_FIXUP_CB;      // contributors per batch of O loads (divides 32)
   constexpr int SPLIT = kFixupWarpsPerUnit;    // warps per cut unit, each on its share of the head rows
+  MVB_TRACE(const unsigned long long tr_entry = trace_now();)
   const int lane = threadIdx.x & 31;
   const int gw = blockIdx.x * 4 + (threadIdx.x >> 5);
   const int w_first = gw / SPLIT, part_of = gw - w_first * SPLIT;
@@ -548,6 +596,12 @@ __global__ void __launch_bounds__(128) decode_stream_fixup_kernel(const DecodeAr
   const int4 d1 = __ldcg(dsrc + 2 * w_first + 1);
   if (d0.x < 0) return;
   if (sa.sdesc != nullptr) grid_dependency_wait();  // the streaming kernel's partials are visible
+  MVB_TRACE(int tr_slot = 0; const bool tr_on = lane == 0 && gw < kTraceFixWarps;
+            if (tr_on) {
+              tr_slot = atomicAdd(&g_trace_fcnt[gw], 1) % kTraceLaunches;
+              g_trace_f[tr_slot][gw][0] = tr_entry;
+              g_trace_f[tr_slot][gw][1] = trace_now();
+            })
   const int us = d0.x, ue = d0.y, seq = d0.z, T_all = d0.w, h0 = d1.x, nrows = d1.y, nct = d1.z;
   const bool dense = T_all >= Wtot;
   auto contributor = [&](int c) { return dense ? w_first + c : stream_warp_of(us + c, T_all, Wtot); };
@@ -646,6 +700,7 @@ __global__ void __launch_bounds__(128) decode_stream_fixup_kernel(const DecodeAr
         for (int i = 0; i < DPL; ++i) po[lane + 32 * i] = from_f32<T>(acc[r][i]);
       }
   }
+  MVB_TRACE(if (tr_on) g_trace_f[tr_slot][gw][2] = trace_now();)
 }
 
 // ---------------------------------------------------------------------------
@@ -1120,3 +1175,28 @@ cudaError_t launch_decode_stream_schedule(const DecodeArgs& a, int dtype, int he
 }
 
 }  // namespace mvb
+
+#ifdef MVB_STREAM_TRACE
+// Trace build only (not part of the product ABI): zero the arrival counters
+// and stamps, and copy the stamps out (host buffers of the arrays' sizes:
+// [8][4096][5], [8][4096][32] and [8][16384][3] unsigned 64-bit).
+extern "C" int mvb_trace_clear() {
+  cudaError_t e = cudaSuccess;
+  const void* syms[] = {&mvb::g_trace_wcnt, &mvb::g_trace_fcnt, &mvb::g_trace_w, &mvb::g_trace_t, &mvb::g_trace_f};
+  const size_t sizes[] = {sizeof(mvb::g_trace_wcnt), sizeof(mvb::g_trace_fcnt), sizeof(mvb::g_trace_w),
+                          sizeof(mvb::g_trace_t), sizeof(mvb::g_trace_f)};
+  for (int i = 0; i < 5 && e == cudaSuccess; ++i) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, syms[i]);
+    if (e == cudaSuccess) e = cudaMemset(p, 0, sizes[i]);
+  }
+  return (int)e;
+}
+
+extern "C" int mvb_trace_read(void* warps, void* tiles, void* fixups) {
+  cudaError_t e = cudaMemcpyFromSymbol(warps, mvb::g_trace_w, sizeof(mvb::g_trace_w));
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(tiles, mvb::g_trace_t, sizeof(mvb::g_trace_t));
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(fixups, mvb::g_trace_f, sizeof(mvb::g_trace_f));
+  return (int)e;
+}
+#endif

@@ -241,3 +241,20 @@ def test_direct_binding_loads_and_routes_cpu_tensors_to_the_full_path():
     st, out = fast.decode(q, kc, kc, torch.zeros(2, 1, dtype=torch.int64), torch.ones(2, dtype=torch.int32), 16,
                           -1.0, None, _native.DECODE_AUTO, 0, 0, None)
     assert st == fast.SLOW_PATH and out is None
+
+
+def test_trace_build_is_separate_from_the_product_library():
+    """The per-warp timeline stamps live only in the trace build
+    (lib/libmvb200_trace.so, -DMVB_STREAM_TRACE); the product library the
+    backend loads exports none of the trace calls."""
+    from mini_vllm_b200 import build as B
+
+    raw = ctypes.CDLL(_native.LIB_PATH)
+    assert not hasattr(raw, "mvb_trace_clear") and not hasattr(raw, "mvb_trace_read")
+    if not os.path.exists(B.TRACE_LIB_PATH):
+        pytest.skip("trace build not made (build.build_trace())")
+    trace = ctypes.CDLL(B.TRACE_LIB_PATH)
+    assert hasattr(trace, "mvb_trace_clear") and hasattr(trace, "mvb_trace_read")
+    assert trace.mvb_abi_version() == _native.ABI_VERSION
+    for name in declared_symbols():
+        assert hasattr(trace, name), name
