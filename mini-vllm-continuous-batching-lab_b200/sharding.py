@@ -36,9 +36,12 @@ def snake_assignment(context_lens: np.ndarray, world_size: int) -> List[np.ndarr
 class OutputGather:
     """Reusable all-gather of per-rank ``[n_rank, H, D]`` outputs into global order.
 
-    The receive buffer and the per-rank index tensors are built once on the
-    device, so one call is a single ``all_gather_into_tensor`` plus one
-    ``index_copy_`` — no host work, no allocation, capturable in a CUDA graph.
+    The buffers and the permutation are built once on the device, so one call
+    is a single ``all_gather_into_tensor`` plus one ``index_select`` into the
+    output (global row g <- received row ``perm[g]``) — no host work, no
+    allocation, capturable in a CUDA graph.  A decode that writes its output
+    into ``send_view(n)`` (``decode_attention(out=...)``) saves the copy into
+    the send buffer.
     """
 
     def __init__(self, owned: List[np.ndarray], heads: int, head_dim: int, dtype, device, group=None):
@@ -52,19 +55,26 @@ class OutputGather:
         self.send = torch.zeros((self.cap, heads, head_dim), dtype=dtype, device=device)
         self.recv = torch.empty((self.world * self.cap, heads, head_dim), dtype=dtype, device=device)
         self.out = torch.empty((self.total, heads, head_dim), dtype=dtype, device=device)
-        # rows of `recv` that hold real sequences, and their global indices
-        src = np.concatenate([r * self.cap + np.arange(c) for r, c in enumerate(self.counts)])
-        dst = np.concatenate(owned) if owned else np.zeros(0, np.int64)
-        self.src = torch.from_numpy(src.astype(np.int64)).to(device)
-        self.dst = torch.from_numpy(dst.astype(np.int64)).to(device)
+        # received row of every global sequence (rank r's i-th owned sequence
+        # arrives at row r * cap + i)
+        perm = np.zeros(self.total, np.int64)
+        for r, o in enumerate(owned):
+            perm[np.asarray(o, dtype=np.int64)] = r * self.cap + np.arange(o.size)
+        self.perm = torch.from_numpy(perm).to(device)
+
+    def send_view(self, n: int):
+        """The first ``n`` rows of the send buffer: a decode's ``out=`` target."""
+        return self.send[:n]
 
     def __call__(self, local_out):
+        import torch
         import torch.distributed as dist
 
         n = local_out.shape[0]
-        self.send[:n].copy_(local_out)
+        if local_out.data_ptr() != self.send.data_ptr():
+            self.send[:n].copy_(local_out)
         dist.all_gather_into_tensor(self.recv, self.send, group=self.group)
-        self.out.index_copy_(0, self.dst, self.recv.index_select(0, self.src))
+        torch.index_select(self.recv, 0, self.perm, out=self.out)
         return self.out
 
 
