@@ -105,7 +105,7 @@ def _unsharded_reference():
     return out
 
 
-@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("world", [2, 3, 5])  # 5: uneven shares (5, 5, 5, 5, 4), padded in the gather
 def test_sharded_decode_with_gloo_gather_matches_unsharded(tmp_path, world):
     result = str(tmp_path / "gathered.npy")
     ctx = mp.get_context("spawn")
